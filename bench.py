@@ -1,0 +1,361 @@
+#!/usr/bin/env python
+"""Benchmark: Qwen3-4B BF16 greedy decode tok/s on B200.
+
+Workload: random-init Qwen3-4B (36 layers, 2560 hidden, tied 151936 vocab,
+seeded synthetic weights), batch 1, 512 uniform-random prompt ids (seed 1),
+static KV cache of 4096 positions.  One step = one greedy decode token: the
+whole 36-layer stack + final norm + lm_head + argmax, replayed as one CUDA
+graph.  Each step streams 8.05 GB of weights (> 126 MB L2), so no L2 flush is
+needed between steps.
+
+Arms:
+* default: the native path (libleanb200.so).  ``value`` = tokens / device time
+  (CUDA events, max over ranks); ``e2e`` = the same through the public engine
+  API with the step's input token copied from pinned host memory and the
+  result read back every step; ``roofline`` = the dominant kernel (fused
+  post-norm + gate_up + SiLU*up) timed with CUDA events; ``cpu_baseline`` = the
+  CPU oracle (the reference's eager torch path restated) on this host's cores.
+* ``--impl reference``: the reference's CPU implementation of the path (the
+  oracle port; the reference cannot travel to the GPU box) timed alone.
+
+Multi-GPU (torchrun, N > 1): every rank runs an independent bs1 replica
+(``scaling: weak``); tensor parallelism is not in this build yet.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+from leanstack_b200 import synth  # noqa: E402
+from leanstack_b200.config import QWEN3_4B  # noqa: E402
+
+METRIC = "Qwen3-4B BF16 greedy decode tok/s (bs1, 512-token prompt, static KV 4096)"
+WORKLOAD = "cfg2: Qwen3-4B random-init, batch 1, 512 uniform prompt ids, greedy decode"
+SEED = 1
+PROMPT = 512
+MAX_SEQ = 4096
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
+    ap.add_argument("--e2e-steps", type=int, default=64)
+    return ap.parse_args()
+
+
+def measured_peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        if args.impl == "ours":
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        else:
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle (reference path restated) — the timed CPU baseline
+# ---------------------------------------------------------------------------
+
+def cpu_decode_rate(tensors_cpu: dict, budget_s: float, max_steps: int | None = None):
+    """Time full-model bs1 decode steps of the CPU oracle (bf16, all host cores).
+
+    The KV cache holds 512 seeded positions (a prefill on the CPU would take
+    minutes and is not part of the timed metric).  Returns (tok/s, steps, threads).
+    """
+    from oracle import qwen_oracle as qo
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = QWEN3_4B
+    m = qo.OracleModel.from_checkpoint(g, tensors_cpu, precision="bf16")
+    kv = m.new_kv(1, MAX_SEQ)
+    kv.key_cache[:, :, :, :PROMPT] = synth.normal((g.num_hidden_layers, 1, g.num_key_value_heads, PROMPT, g.head_dim),
+                                                  1.0, SEED, "bench/cpu_k")
+    kv.value_cache[:, :, :, :PROMPT] = synth.normal((g.num_hidden_layers, 1, g.num_key_value_heads, PROMPT,
+                                                     g.head_dim), 1.0, SEED, "bench/cpu_v")
+    kv.set_all(PROMPT)
+    pc = m.rope(MAX_SEQ)
+    tok = torch.tensor([[1]])
+    with torch.inference_mode():
+        hidden = qo.stack_forward(m, qo.embed(m, tok), kv, pc)  # warm-up step
+        tok = qo.greedy_token(m, hidden).view(1, 1)
+        steps = 0
+        t0 = time.perf_counter()
+        while True:
+            hidden = qo.stack_forward(m, qo.embed(m, tok), kv, pc)
+            tok = qo.greedy_token(m, hidden).view(1, 1)
+            steps += 1
+            el = time.perf_counter() - t0
+            if (max_steps is not None and steps >= max_steps) or (max_steps is None and el >= budget_s):
+                break
+    return steps / el, steps, torch.get_num_threads(), el
+
+
+def cpu_checkpoint():
+    """Synthesize the 4B checkpoint (on the GPU when present: same values) and bring it to the host."""
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    t = synth.synth_checkpoint(QWEN3_4B, SEED, device=dev)
+    return {k: v.to("cpu") for k, v in t.items()}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        barrier(world)
+        return 0
+    tensors = cpu_checkpoint()
+    torch.cuda.empty_cache() if torch.cuda.is_available() else None
+    # warm-up steps, then exactly `steps` timed steps (each a full decode token)
+    if args.warmup:
+        cpu_decode_rate(tensors, 0, max_steps=min(args.warmup, 3))
+    rate, steps, threads, el = cpu_decode_rate(tensors, 0, max_steps=args.steps)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": rate, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": 1000.0 * el / steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights)",
+        "config": {"workload": WORKLOAD, "model": "Qwen3-4B (random init)", "global_batch": 1, "seq_len": PROMPT,
+                   "parallelism": "single process (CPU)", "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"{steps} full-model bs1 decode steps over a 512-position KV cache, torch CPU bf16"},
+        "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    barrier(world)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# native arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, world, rank, local):
+    from leanstack_b200 import kernels as K
+    from leanstack_b200.engine import DecodeEngine
+    from leanstack_b200.leanserve import materialize_from_tensors
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    g = QWEN3_4B
+    peaks = measured_peaks()
+    tensors = synth.synth_checkpoint(g, SEED, device=dev)
+    rt = materialize_from_tensors(g, tensors, device=dev, free_source=True)
+    del tensors
+    torch.cuda.empty_cache()
+    prompt = synth.token_ids((1, PROMPT), g.vocab_size, SEED, "cfg2/prompt")
+    eng = DecodeEngine(rt, batch_size=1, max_seq_len=MAX_SEQ)
+    eng.prefill(prompt)
+    eng.capture()
+    total_steps = args.warmup + args.steps + args.e2e_steps + 2
+    if PROMPT + total_steps > eng.S:
+        raise SystemExit(f"--warmup + --steps + --e2e-steps exceed the {MAX_SEQ}-position cache")
+
+    for _ in range(args.warmup):
+        eng.decode_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = ClockSampler(local)
+    clocks.start()
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        eng.decode_step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    elapsed_ms = ev0.elapsed_time(ev1)
+    barrier(world)
+    elapsed_ms = max_over_ranks(elapsed_ms, world)
+    ms_per_step = elapsed_ms / args.steps
+    value = world * args.steps * eng.B / (elapsed_ms / 1000.0)
+
+    # --- e2e through the public API: host ids in, host ids out, every step ---
+    pin_in = torch.empty((1,), dtype=torch.int64, pin_memory=True)
+    pin_out = torch.empty((1,), dtype=torch.int64, pin_memory=True)
+    pin_out.copy_(eng.current_ids.cpu())
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        pin_in.copy_(pin_out)
+        eng.current_ids.copy_(pin_in, non_blocking=True)
+        eng.decode_step()
+        pin_out.copy_(eng.current_ids, non_blocking=True)
+        stream.synchronize()
+    e2e_s = time.perf_counter() - t0
+    e2e_s = max_over_ranks(e2e_s, world)
+    e2e = {"value": world * args.e2e_steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 8,
+           "d2h_bytes_per_step": 8, "steps": args.e2e_steps}
+
+    # --- roofline of the dominant kernel: fused post-norm + gate_up + SiLU*up ---
+    a = eng.arenas
+    reps = 4
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev2.record(stream)
+    for _ in range(reps):
+        for layer in rt.layers:
+            K.gateup_silu(a.h[:1], layer.post_attention_layernorm_weight, layer.mlp.gate_up_proj_weight,
+                          g.rms_norm_eps, out=a.act[:1])
+    ev3.record(stream)
+    torch.cuda.synchronize()
+    per_launch_s = ev2.elapsed_time(ev3) / 1000.0 / (reps * len(rt.layers))
+    gu_bytes = 2 * g.intermediate_size * g.hidden_size * 2 + g.hidden_size * 2 * 2 + g.intermediate_size * 2
+    achieved = gu_bytes / per_launch_s / 1e9
+    traffic = None
+    tp = REPO / "profiles" / "traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get("gateup_silu_per_launch_bytes")
+    step_bytes = g.num_hidden_layers * g.layer_weight_bytes() + g.lm_head_bytes() + \
+        (PROMPT + args.warmup + args.steps // 2) * g.kv_bytes_per_token()
+    roofline = {"kernel": "linear_small_m<1,SILU_MUL,norm> (post-norm + gate_up + SiLU*up, M=1)", "bound": "hbm",
+                "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                "traffic": traffic, "algorithmic_bytes_per_launch": gu_bytes,
+                "avg_launch_us": per_launch_s * 1e6, "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json copy)",
+                "step_achieved_gbs": step_bytes / (ms_per_step / 1000.0) / 1e9,
+                "step_frac": step_bytes / (ms_per_step / 1000.0) / 1e9 / peaks["hbm_gbs"],
+                "step_bytes": step_bytes}
+
+    # --- CPU baseline (rank 0, N == 1 only) ---
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tensors_cpu = cpu_checkpoint()
+        rate, steps, threads, el = cpu_decode_rate(tensors_cpu, args.cpu_sample_seconds)
+        del tensors_cpu
+        cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"{steps} full-model bs1 decode steps ({el:.1f} s) over a 512-position KV cache, "
+                         f"CPU oracle (reference eager torch path restated), bf16"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights, uniform ids)",
+            "config": {"workload": WORKLOAD, "model": "Qwen3-4B (random init)", "global_batch": world,
+                       "seq_len": PROMPT, "max_seq": MAX_SEQ, "parallelism": f"replicas x{world}" if world > 1
+                       else "single GPU", "l2": "not flushed: each step streams 8.05 GB of weights (> 126 MB L2)"},
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
+            "gpu_launches": args.steps * eng.kernel_launches_per_step(),
+        }
+        print(json.dumps(line), flush=True)
+    barrier(world)
+    return 0
+
+
+def main() -> int:
+    args = parse_args()
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            return run_reference(args, world, rank)
+        return run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,166 @@
+/*
+ * leanb200.h — C ABI of libleanb200.so, the B200 (sm_100a) kernels behind the
+ * leanstack decode hot path.
+ *
+ * Every entry point takes raw device pointers, int64 sizes and a CUDA stream
+ * (passed as void*), enqueues its work on that stream, and returns an
+ * ls_status code.  Nothing here allocates device memory: outputs and
+ * workspaces are caller-provided (the resident arenas of the buffer planner).
+ * Errors are returned as codes, never by aborting; ls_last_error() describes
+ * the most recent failure of the calling thread.  Every call is valid inside
+ * CUDA stream capture.
+ *
+ * Tensor layouts (bf16 unless stated, row-major, innermost dimension last):
+ *   hidden / residual     [m, hidden]                 m = batch * q_len tokens
+ *   weights               [out_features, in_features] (torch nn.Linear layout)
+ *   fused qkv weight      [(Hq + 2*Hkv) * D, hidden]  rows: q heads, k heads, v heads
+ *   fused gate_up weight  [2 * I, hidden]             rows: gate, then up
+ *   q (rotated)           [m, Hq, D]
+ *   attention output      [m, Hq * D]
+ *   K / V cache (1 layer) [batch, Hkv, max_seq, D]
+ *   rope cos / sin        [rope_len, D / 2]           the reference's bf16 position cache
+ *   cache_pos             int32 [batch] on device:    cached positions of each sequence
+ *                         before this call; token i of sequence b sits at
+ *                         position cache_pos[b] + i and attends keys 0..cache_pos[b]+i.
+ *                         Where an entry point also takes uniform_past, cache_pos may be
+ *                         NULL and every sequence then uses cache_pos[b] = uniform_past
+ *                         (the reference's per-layer host cursor, kv_cache.py:219).
+ */
+#ifndef LEANB200_H
+#define LEANB200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LS_ABI_VERSION 1
+
+typedef enum ls_status {
+  LS_OK = 0,
+  LS_ERR_INVALID_ARGUMENT = 1,  /* null pointer, non-positive size */
+  LS_ERR_UNSUPPORTED_SHAPE = 2, /* shape outside what the kernels implement */
+  LS_ERR_MISALIGNED = 3,        /* pointer not 16-byte aligned / size not a multiple of 8 */
+  LS_ERR_WORKSPACE = 4,         /* workspace null or too small */
+  LS_ERR_CUDA = 5,              /* a CUDA runtime call failed */
+  LS_ERR_KV_OVERFLOW = 6,       /* a KV position beyond max_seq (device-detected) */
+  LS_ERR_TIMEOUT = 7,           /* a bounded device-side wait ran out */
+  LS_ERR_NOT_SUPPORTED = 8      /* feature not available on this device */
+} ls_status;
+
+/* Epilogues of ls_linear_bf16. */
+typedef enum ls_epilogue {
+  LS_EPI_STORE = 0,     /* out = bf16(W x) */
+  LS_EPI_RESIDUAL = 1,  /* out = bf16(residual + bf16(W x)) */
+  LS_EPI_SILU_MUL = 2   /* W = [gate; up] (2I rows): out[I] = bf16(bf16(silu(bf16 g)) * bf16 u) */
+} ls_epilogue;
+
+typedef void* ls_stream_t; /* a cudaStream_t */
+
+/* Library version (LS_ABI_VERSION) and the last error message of this thread. */
+int ls_version(void);
+const char* ls_last_error(void);
+
+/* Read (and optionally clear) the device-side error flag that kernels set when
+ * they skip an out-of-range access.  Synchronizes the current device. */
+int ls_get_device_error(int* code, int clear);
+
+/* Number of SMs of the current device (grid sizing is a multiple of it). */
+int ls_sm_count(int* out);
+
+/*
+ * x[m] = embed[ids[m]] — the embedding lookup of run_semantic_stack_decode
+ * (reference: src/leanstack/runtime/qwen_explicit.py:1623, F.embedding).
+ * ids: int64 [m] on device.
+ */
+int ls_embed_gather(const int64_t* ids, int64_t m, const void* embed, int64_t vocab, int64_t hidden,
+                    void* out, ls_stream_t stream);
+
+/*
+ * Skinny linear on the CUDA cores for m <= 8 activation rows, with an optional
+ * RMSNorm prologue over x (norm_w == NULL: none) and one of ls_epilogue.
+ * For LS_EPI_SILU_MUL, n is the number of weight rows (2I) and out has n/2
+ * columns.  Replaces the torch.mv / F.linear calls of the reference's
+ * dispatch helpers (src/leanstack/runtime/qwen_explicit.py:787, :913, :942-948).
+ */
+int ls_linear_bf16(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w, int64_t n,
+                   int epilogue, const void* residual, void* out, ls_stream_t stream);
+
+/*
+ * Input RMSNorm + fused QKV projection + per-head q/k RMSNorm + NeoX RoPE +
+ * KV append, for m = batch * q_len tokens.
+ * Replaces _semantic_attention_qkv_vector / _semantic_attention_qkv
+ * (src/leanstack/runtime/qwen_explicit.py:733-806) followed by
+ * StaticKVBlockManager.append (src/leanstack/runtime/kv_cache.py:222-243).
+ *   input_norm_w  NULL if x is already normed (the reference helper's input)
+ *   k_cache/v_cache  layer slice [batch, Hkv, max_seq, D], or NULL to skip the append
+ *   k_out/v_out   optional [m, Hkv, D] copies of the rotated k and raw v (NULL: skip)
+ *   qkv_scratch   [m, (Hq + 2 Hkv) D] raw projection (caller workspace)
+ *   q_out         [m, Hq, D] normed + rotated q
+ */
+int ls_rmsnorm_qkv_rope_kvappend(const void* x, int64_t batch, int64_t q_len, int64_t hidden,
+                                 const void* input_norm_w, float eps, const void* qkv_w, int64_t num_heads,
+                                 int64_t num_kv_heads, int64_t head_dim, const void* q_norm_w,
+                                 const void* k_norm_w, const void* rope_cos, const void* rope_sin,
+                                 int64_t rope_len, const int32_t* cache_pos, int64_t uniform_past, void* k_cache,
+                                 void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* qkv_scratch,
+                                 void* q_out, ls_stream_t stream);
+
+/*
+ * GQA attention of q [m, Hq, D] over the cache (keys 0..cache_pos[b]+i for
+ * token i of sequence b), split over the sequence and combined in-kernel.
+ * Covers decode (q_len 1, unmasked) and verify (q_len k+1 with the decode
+ * mask of src/leanstack/runtime/qwen_explicit.py:551-563).  Replaces the
+ * SDPA calls at src/leanstack/runtime/qwen_explicit.py:886-903 and :1000-1039.
+ * workspace: ls_decode_attention_workspace_bytes() bytes, zero-filled once
+ * before first use (the kernel leaves its counters at zero).
+ */
+int ls_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
+                        int64_t uniform_past, int64_t batch, int64_t q_len, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                        int64_t max_seq, float scale, void* out, void* workspace, int64_t workspace_bytes,
+                        ls_stream_t stream);
+int ls_decode_attention_workspace_bytes(int64_t batch, int64_t q_len, int64_t num_heads, int64_t num_kv_heads,
+                                        int64_t head_dim, int64_t max_seq, int64_t* bytes);
+
+/* h = residual + bf16(o_w attn): o_proj with the residual epilogue
+ * (src/leanstack/runtime/qwen_explicit.py:913 and :1262, :819-820). */
+int ls_oproj_residual(const void* attn, int64_t m, int64_t k, const void* o_w, int64_t n, const void* residual,
+                      void* out, ls_stream_t stream);
+
+/* act = silu(gate) * up of the post-attention-normed h
+ * (src/leanstack/runtime/qwen_explicit.py:932-947, :821-828). */
+int ls_rmsnorm_gateup_silu(const void* h, int64_t m, int64_t hidden, const void* post_norm_w, float eps,
+                           const void* gate_up_w, int64_t intermediate, void* out, ls_stream_t stream);
+
+/* out = residual + bf16(down_w act) (src/leanstack/runtime/qwen_explicit.py:947-949, :829). */
+int ls_down_residual(const void* act, int64_t m, int64_t intermediate, const void* down_w, int64_t hidden,
+                     const void* residual, void* out, ls_stream_t stream);
+
+/*
+ * Greedy head: final RMSNorm + lm_head + argmax over the bf16-rounded logits,
+ * lowest index on ties, for each of m rows.  out_ids: int64 [m] on device.
+ * Replaces select_semantic_greedy_token's torch head
+ * (src/leanstack/runtime/qwen_explicit.py:952-960, :1814-1832) and the cuTile
+ * cutile_logits_argmax (src/leanstack/runtime/cutile_logits.py:37-69).
+ * workspace: ls_lmhead_workspace_bytes() bytes, zero-filled once before first use.
+ */
+int ls_lmhead_argmax(const void* h, int64_t m, int64_t hidden, const void* final_norm_w, float eps,
+                     const void* lm_head_w, int64_t vocab, int64_t* out_ids, void* workspace,
+                     int64_t workspace_bytes, ls_stream_t stream);
+int ls_lmhead_workspace_bytes(int64_t m, int64_t vocab, int64_t* bytes);
+
+/* Standalone RMSNorm over the last dim, bf16((x * rsqrt(mean(x^2) + eps)) * w),
+ * for m rows of length n (src/leanstack/runtime/qwen_explicit.py:621-637). */
+int ls_rmsnorm(const void* x, int64_t m, int64_t n, const void* w, float eps, void* out, ls_stream_t stream);
+
+/* cache_pos[b] += delta[b] (delta NULL: += q_len): moves the device cursors
+ * after a step, the device-side counterpart of the reference's host cursor
+ * bookkeeping (src/leanstack/runtime/kv_cache.py:239-245, :298-318). */
+int ls_advance_cursors(int32_t* cache_pos, const int32_t* delta, int64_t batch, int64_t q_len, ls_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LEANB200_H */

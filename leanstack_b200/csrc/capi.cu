@@ -1,0 +1,312 @@
+// C ABI of libleanb200.so: argument checking, error reporting and the small
+// glue kernels (embedding gather, cursor advance).  The heavy kernels live in
+// linear_small_m.cu and attention.cu.
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace lsb {
+__device__ int g_device_error = 0;
+
+__global__ void embed_gather_kernel(const int64_t* ids, const __nv_bfloat16* embed, int64_t vocab, int hidden,
+                                    __nv_bfloat16* out, int* err) {
+  grid_dep_wait();
+  const int m = blockIdx.y;
+  const int64_t id = ids[m];
+  const int vec = hidden >> 3;
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) raise_device_error(err, LS_ERR_INVALID_ARGUMENT);
+    return;
+  }
+  for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < vec; v += gridDim.x * blockDim.x)
+    reinterpret_cast<uint4*>(out + (size_t)m * hidden)[v] =
+        reinterpret_cast<const uint4*>(embed + (size_t)id * hidden)[v];
+}
+
+// One CTA per row: y = bf16((x * rsqrt(mean(x^2) + eps)) * w).
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, int n, const __nv_bfloat16* w,
+                                                      float eps, __nv_bfloat16* out) {
+  grid_dep_wait();
+  __shared__ float red[8];
+  const __nv_bfloat16* xr = x + (size_t)blockIdx.x * n;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = bf16_to_f(xr[i]);
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+  const float r = rsqrtf(tot / (float)n + eps);
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    out[(size_t)blockIdx.x * n + i] = f_to_bf16((bf16_to_f(xr[i]) * r) * bf16_to_f(w[i]));
+}
+
+__global__ void advance_cursors_kernel(int* cache_pos, const int* delta, int batch, int q_len) {
+  grid_dep_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < batch) cache_pos[b] += delta ? delta[b] : q_len;
+}
+}  // namespace lsb
+
+namespace lsb_host {
+
+static thread_local char g_last_error[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int* device_error_ptr() {
+  static int* cached[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cached[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, lsb::g_device_error) == cudaSuccess) cached[dev] = static_cast<int*>(ptr);
+  }
+  return cached[dev];
+}
+
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("LEANB200_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// Defined in the kernel translation units.
+int launch_linear(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w, int64_t n,
+                  int epi, const void* residual, void* out, cudaStream_t stream, float* part_val, int* part_idx,
+                  unsigned int* counter, int64_t* out_ids, int grid_override);
+int lmhead_grid(int64_t vocab, int64_t m);
+int launch_qk_norm_rope(const void* qkv, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, const void* qn,
+                        const void* kn, const void* cos, const void* sin, int64_t rope_len, const int32_t* cache_pos,
+                        int64_t uniform_past, void* k_cache, void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* q_out,
+                        float eps, cudaStream_t stream);
+int attention_workspace_bytes(int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int64_t max_seq,
+                              int64_t* bytes);
+int launch_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
+                            int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int64_t max_seq, float scale,
+                            void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream);
+
+}  // namespace lsb_host
+
+using namespace lsb_host;
+
+#define LS_REQUIRE(cond, code, ...) \
+  do {                              \
+    if (!(cond)) return set_error(code, __VA_ARGS__); \
+  } while (0)
+
+extern "C" {
+
+int ls_version(void) { return LS_ABI_VERSION; }
+
+const char* ls_last_error(void) { return g_last_error; }
+
+int ls_sm_count(int* out) {
+  LS_REQUIRE(out, LS_ERR_INVALID_ARGUMENT, "ls_sm_count: out is null");
+  *out = sm_count();
+  return LS_OK;
+}
+
+int ls_get_device_error(int* code, int clear) {
+  LS_REQUIRE(code, LS_ERR_INVALID_ARGUMENT, "ls_get_device_error: code is null");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "device synchronize: %s", cudaGetErrorString(e));
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, lsb::g_device_error, sizeof(int));
+  if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "read device error: %s", cudaGetErrorString(e));
+  *code = v;
+  if (clear && v) {
+    int zero = 0;
+    e = cudaMemcpyToSymbol(lsb::g_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "clear device error: %s", cudaGetErrorString(e));
+  }
+  return LS_OK;
+}
+
+int ls_embed_gather(const int64_t* ids, int64_t m, const void* embed, int64_t vocab, int64_t hidden, void* out,
+                    ls_stream_t stream) {
+  LS_REQUIRE(ids && embed && out, LS_ERR_INVALID_ARGUMENT, "ls_embed_gather: null pointer");
+  LS_REQUIRE(m > 0 && m <= 65535 && vocab > 0 && hidden > 0, LS_ERR_INVALID_ARGUMENT, "ls_embed_gather: bad sizes");
+  LS_REQUIRE(hidden % 8 == 0 && aligned16(embed) && aligned16(out), LS_ERR_MISALIGNED,
+             "ls_embed_gather: hidden must be a multiple of 8 and pointers 16-byte aligned");
+  const int vec = (int)(hidden / 8);
+  const int threads = 128;
+  const int blocks = (vec + threads - 1) / threads;
+  lsb::embed_gather_kernel<<<dim3(blocks, (unsigned)m), threads, 0, (cudaStream_t)stream>>>(
+      ids, static_cast<const __nv_bfloat16*>(embed), vocab, (int)hidden, static_cast<__nv_bfloat16*>(out),
+      device_error_ptr());
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "embed_gather launch: %s", cudaGetErrorString(e));
+}
+
+int ls_linear_bf16(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w, int64_t n,
+                   int epilogue, const void* residual, void* out, ls_stream_t stream) {
+  LS_REQUIRE(epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL, LS_ERR_INVALID_ARGUMENT,
+             "ls_linear_bf16: unknown epilogue %d", epilogue);
+  return launch_linear(x, m, k, norm_w, eps, w, n, epilogue, residual, out, (cudaStream_t)stream, nullptr, nullptr,
+                       nullptr, nullptr, 0);
+}
+
+int ls_rmsnorm_qkv_rope_kvappend(const void* x, int64_t batch, int64_t q_len, int64_t hidden,
+                                 const void* input_norm_w, float eps, const void* qkv_w, int64_t num_heads,
+                                 int64_t num_kv_heads, int64_t head_dim, const void* q_norm_w,
+                                 const void* k_norm_w, const void* rope_cos, const void* rope_sin,
+                                 int64_t rope_len, const int32_t* cache_pos, int64_t uniform_past, void* k_cache,
+                                 void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* qkv_scratch,
+                                 void* q_out, ls_stream_t stream) {
+  LS_REQUIRE(x && qkv_w && q_norm_w && k_norm_w && rope_cos && rope_sin && qkv_scratch && q_out,
+             LS_ERR_INVALID_ARGUMENT, "ls_rmsnorm_qkv_rope_kvappend: null pointer");
+  LS_REQUIRE(head_dim == 128, LS_ERR_UNSUPPORTED_SHAPE, "head_dim=%lld (only 128 is implemented)",
+             (long long)head_dim);
+  LS_REQUIRE(batch > 0 && q_len > 0 && num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
+             LS_ERR_INVALID_ARGUMENT, "ls_rmsnorm_qkv_rope_kvappend: bad head counts / sizes");
+  LS_REQUIRE(rope_len > 0, LS_ERR_INVALID_ARGUMENT, "rope_len must be positive");
+  LS_REQUIRE(cache_pos || (uniform_past >= 0 && uniform_past + q_len <= rope_len), LS_ERR_KV_OVERFLOW,
+             "uniform_past=%lld + q_len=%lld beyond rope_len=%lld", (long long)uniform_past, (long long)q_len,
+             (long long)rope_len);
+  LS_REQUIRE(cache_pos || !k_cache || uniform_past + q_len <= max_seq, LS_ERR_KV_OVERFLOW,
+             "cache overflow: %lld tokens with max_seq=%lld", (long long)(uniform_past + q_len), (long long)max_seq);
+  LS_REQUIRE((k_cache == nullptr) == (v_cache == nullptr) && (k_out == nullptr) == (v_out == nullptr),
+             LS_ERR_INVALID_ARGUMENT, "k/v cache and k/v out come in pairs");
+  LS_REQUIRE(!k_cache || max_seq > 0, LS_ERR_INVALID_ARGUMENT, "max_seq must be positive");
+  const int64_t m = batch * q_len;
+  LS_REQUIRE(m <= 65535, LS_ERR_UNSUPPORTED_SHAPE, "too many tokens for the small-m path: %lld", (long long)m);
+  const int64_t qkv_dim = (num_heads + 2 * num_kv_heads) * head_dim;
+  int rc = launch_linear(x, m, hidden, input_norm_w, eps, qkv_w, qkv_dim, 0, nullptr, qkv_scratch,
+                         (cudaStream_t)stream, nullptr, nullptr, nullptr, nullptr, 0);
+  if (rc) return rc;
+  return launch_qk_norm_rope(qkv_scratch, batch, q_len, num_heads, num_kv_heads, q_norm_w, k_norm_w, rope_cos,
+                             rope_sin, rope_len, cache_pos, uniform_past, k_cache, v_cache, max_seq, k_out, v_out, q_out, eps,
+                             (cudaStream_t)stream);
+}
+
+int ls_decode_attention_workspace_bytes(int64_t batch, int64_t q_len, int64_t num_heads, int64_t num_kv_heads,
+                                        int64_t head_dim, int64_t max_seq, int64_t* bytes) {
+  LS_REQUIRE(bytes, LS_ERR_INVALID_ARGUMENT, "bytes is null");
+  LS_REQUIRE(head_dim == 128, LS_ERR_UNSUPPORTED_SHAPE, "head_dim=%lld (only 128 is implemented)",
+             (long long)head_dim);
+  LS_REQUIRE(batch > 0 && q_len > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0 && max_seq > 0,
+             LS_ERR_INVALID_ARGUMENT, "bad attention sizes");
+  return attention_workspace_bytes(batch, q_len, num_heads, num_kv_heads, max_seq, bytes);
+}
+
+int ls_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
+                        int64_t uniform_past, int64_t batch, int64_t q_len, int64_t num_heads, int64_t num_kv_heads,
+                        int64_t head_dim, int64_t max_seq, float scale, void* out, void* workspace,
+                        int64_t workspace_bytes, ls_stream_t stream) {
+  LS_REQUIRE(q && k_cache && v_cache && out, LS_ERR_INVALID_ARGUMENT, "ls_decode_attention: null pointer");
+  LS_REQUIRE(cache_pos || (uniform_past >= 0 && uniform_past + q_len <= max_seq), LS_ERR_KV_OVERFLOW,
+             "uniform_past=%lld + q_len=%lld beyond max_seq=%lld", (long long)uniform_past, (long long)q_len,
+             (long long)max_seq);
+  LS_REQUIRE(head_dim == 128, LS_ERR_UNSUPPORTED_SHAPE, "head_dim=%lld (only 128 is implemented)",
+             (long long)head_dim);
+  LS_REQUIRE(batch > 0 && batch <= 65535 && q_len > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0 &&
+                 max_seq > 0,
+             LS_ERR_INVALID_ARGUMENT, "ls_decode_attention: bad sizes");
+  LS_REQUIRE(aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out), LS_ERR_MISALIGNED,
+             "ls_decode_attention: pointers must be 16-byte aligned");
+  return launch_decode_attention(q, k_cache, v_cache, cache_pos, uniform_past, batch, q_len, num_heads, num_kv_heads, max_seq,
+                                 scale, out, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int ls_oproj_residual(const void* attn, int64_t m, int64_t k, const void* o_w, int64_t n, const void* residual,
+                      void* out, ls_stream_t stream) {
+  LS_REQUIRE(residual, LS_ERR_INVALID_ARGUMENT, "ls_oproj_residual: residual is null");
+  return launch_linear(attn, m, k, nullptr, 0.f, o_w, n, LS_EPI_RESIDUAL, residual, out, (cudaStream_t)stream,
+                       nullptr, nullptr, nullptr, nullptr, 0);
+}
+
+int ls_rmsnorm_gateup_silu(const void* h, int64_t m, int64_t hidden, const void* post_norm_w, float eps,
+                           const void* gate_up_w, int64_t intermediate, void* out, ls_stream_t stream) {
+  return launch_linear(h, m, hidden, post_norm_w, eps, gate_up_w, 2 * intermediate, LS_EPI_SILU_MUL, nullptr, out,
+                       (cudaStream_t)stream, nullptr, nullptr, nullptr, nullptr, 0);
+}
+
+int ls_down_residual(const void* act, int64_t m, int64_t intermediate, const void* down_w, int64_t hidden,
+                     const void* residual, void* out, ls_stream_t stream) {
+  LS_REQUIRE(residual, LS_ERR_INVALID_ARGUMENT, "ls_down_residual: residual is null");
+  return launch_linear(act, m, intermediate, nullptr, 0.f, down_w, hidden, LS_EPI_RESIDUAL, residual, out,
+                       (cudaStream_t)stream, nullptr, nullptr, nullptr, nullptr, 0);
+}
+
+int ls_lmhead_workspace_bytes(int64_t m, int64_t vocab, int64_t* bytes) {
+  LS_REQUIRE(bytes && m > 0 && vocab > 0, LS_ERR_INVALID_ARGUMENT, "ls_lmhead_workspace_bytes: bad arguments");
+  const int64_t g = lmhead_grid(vocab, m);
+  *bytes = 256 + 2 * ((m * g * 4 + 255) / 256) * 256;
+  return LS_OK;
+}
+
+int ls_lmhead_argmax(const void* h, int64_t m, int64_t hidden, const void* final_norm_w, float eps,
+                     const void* lm_head_w, int64_t vocab, int64_t* out_ids, void* workspace,
+                     int64_t workspace_bytes, ls_stream_t stream) {
+  LS_REQUIRE(out_ids && workspace, LS_ERR_INVALID_ARGUMENT, "ls_lmhead_argmax: null pointer");
+  LS_REQUIRE(m >= 1 && m <= 8, LS_ERR_UNSUPPORTED_SHAPE, "ls_lmhead_argmax: m=%lld outside 1..8", (long long)m);
+  int64_t need = 0;
+  int rc = ls_lmhead_workspace_bytes(m, vocab, &need);
+  if (rc) return rc;
+  LS_REQUIRE(workspace_bytes >= need, LS_ERR_WORKSPACE, "ls_lmhead_argmax: workspace needs %lld bytes",
+             (long long)need);
+  const int g = lmhead_grid(vocab, m);
+  char* ws = static_cast<char*>(workspace);
+  unsigned int* counter = reinterpret_cast<unsigned int*>(ws);
+  const int64_t region = ((m * g * 4 + 255) / 256) * 256;
+  float* part_val = reinterpret_cast<float*>(ws + 256);
+  int* part_idx = reinterpret_cast<int*>(ws + 256 + region);
+  return launch_linear(h, m, hidden, final_norm_w, eps, lm_head_w, vocab, 3, nullptr, nullptr,
+                       (cudaStream_t)stream, part_val, part_idx, counter, out_ids, g);
+}
+
+int ls_rmsnorm(const void* x, int64_t m, int64_t n, const void* w, float eps, void* out, ls_stream_t stream) {
+  LS_REQUIRE(x && w && out, LS_ERR_INVALID_ARGUMENT, "ls_rmsnorm: null pointer");
+  LS_REQUIRE(m > 0 && m < (1ll << 31) && n > 0 && n <= (1 << 20), LS_ERR_INVALID_ARGUMENT, "ls_rmsnorm: bad sizes");
+  lsb::rmsnorm_kernel<<<(unsigned)m, 256, 0, (cudaStream_t)stream>>>(static_cast<const __nv_bfloat16*>(x), (int)n,
+                                                                     static_cast<const __nv_bfloat16*>(w), eps,
+                                                                     static_cast<__nv_bfloat16*>(out));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "rmsnorm launch: %s", cudaGetErrorString(e));
+}
+
+int ls_advance_cursors(int32_t* cache_pos, const int32_t* delta, int64_t batch, int64_t q_len, ls_stream_t stream) {
+  LS_REQUIRE(cache_pos && batch > 0, LS_ERR_INVALID_ARGUMENT, "ls_advance_cursors: bad arguments");
+  const int threads = 128;
+  lsb::advance_cursors_kernel<<<(unsigned)((batch + threads - 1) / threads), threads, 0, (cudaStream_t)stream>>>(
+      cache_pos, delta, (int)batch, (int)q_len);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "advance_cursors launch: %s", cudaGetErrorString(e));
+}
+
+}  // extern "C"

@@ -1,0 +1,97 @@
+// Shared device helpers for the leanstack_b200 kernels (sm_100a only).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/leanb200.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "leanstack_b200 kernels are written for sm_100a (B200) only"
+#endif
+
+namespace lsb {
+
+// ---------------------------------------------------------------------------
+// bf16 <-> fp32.  A bf16 is the top half of an fp32, so widening is a shift.
+// Narrowing uses the CUDA intrinsic (round to nearest even), the same rounding
+// torch applies when an fp32 intermediate is stored as bf16.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_lo(uint32_t packed) { return __uint_as_float(packed << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t packed) { return __uint_as_float(packed & 0xFFFF0000u); }
+__device__ __forceinline__ float bf16_to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ __nv_bfloat16 f_to_bf16(float v) { return __float2bfloat16_rn(v); }
+// Round an fp32 to the nearest bf16 and return it widened again: models one
+// bf16 store of a torch intermediate.
+__device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ void unpack8(const uint4& u, float f[8]) {
+  f[0] = bf16_lo(u.x); f[1] = bf16_hi(u.x);
+  f[2] = bf16_lo(u.y); f[3] = bf16_hi(u.y);
+  f[4] = bf16_lo(u.z); f[5] = bf16_hi(u.z);
+  f[6] = bf16_lo(u.w); f[7] = bf16_hi(u.w);
+}
+
+__device__ __forceinline__ float dot8(const uint4& w, const uint4& x, float acc) {
+  acc = fmaf(bf16_lo(w.x), bf16_lo(x.x), acc);
+  acc = fmaf(bf16_hi(w.x), bf16_hi(x.x), acc);
+  acc = fmaf(bf16_lo(w.y), bf16_lo(x.y), acc);
+  acc = fmaf(bf16_hi(w.y), bf16_hi(x.y), acc);
+  acc = fmaf(bf16_lo(w.z), bf16_lo(x.z), acc);
+  acc = fmaf(bf16_hi(w.z), bf16_hi(x.z), acc);
+  acc = fmaf(bf16_lo(w.w), bf16_lo(x.w), acc);
+  acc = fmaf(bf16_hi(w.w), bf16_hi(x.w), acc);
+  return acc;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Streaming 16-byte load that does not allocate in L1 (weights are read once).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint4 ldg16(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with the PDL attribute may
+// start before its predecessor finishes; it must call grid_dep_wait() before
+// reading anything the predecessor wrote.  grid_dep_launch() lets the next
+// kernel in the stream begin its own prologue.  Both are no-ops when the
+// launch had no PDL attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// Device-side error flag: kernels record the first failure code there (for
+// example a KV position beyond the arena) and skip the offending access.  The
+// flag is one int per device owned by capi.cu; kernels receive its address.
+__device__ __forceinline__ void raise_device_error(int* flag, int code) {
+  if (flag) atomicCAS(flag, 0, code);
+}
+
+}  // namespace lsb
+
+// Host-side helpers shared by the C-ABI translation units.
+namespace lsb_host {
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+int sm_count();
+bool aligned16(const void* p);
+bool pdl_enabled();
+int* device_error_ptr();
+}  // namespace lsb_host

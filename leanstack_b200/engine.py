@@ -1,0 +1,160 @@
+"""Resident decode engine: arenas from the buffer planner + a CUDA-graph step.
+
+This is the serving fast path behind the reference-shaped API.  One engine
+owns, for a fixed (batch, max_seq): the KV arenas, the activation arenas, the
+position cache, the kernel workspaces and one captured CUDA graph of a whole
+decode step (embedding gather, 36 x 5 layer kernels, greedy head, cursor
+advance).  Every kernel reads the per-sequence cursors from the device
+(``cache_pos``), so the captured graph stays valid as the sequences grow and
+the host only replays it.
+
+Token flow: the step's input ids live in ``arenas.ids[:B]``; the greedy head
+writes the next ids back into the same slots, so consecutive replays decode
+autoregressively with no host round trip.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import kernels as K
+from .leanserve import allocate_arenas, build_resident_buffer_plan, runtime_weight_bytes
+from .qwen_explicit import QwenSemanticStackRuntime, build_qwen_position_cache
+
+SMALL_M = 8
+
+
+class DecodeEngine:
+    def __init__(self, runtime: QwenSemanticStackRuntime, batch_size: int, max_seq_len: int,
+                 max_tokens_per_step: int = SMALL_M, use_graph: bool = True):
+        if runtime.final_norm_weight is None or runtime.lm_head_weight is None:
+            raise ValueError("the engine needs the output head (include_output_head=True)")
+        if batch_size < 1 or batch_size > SMALL_M:
+            raise ValueError(f"batch_size {batch_size}: the CUDA-core step handles 1..{SMALL_M} sequences")
+        self.rt = runtime
+        self.g = g = runtime.config
+        self.B = batch_size
+        self.max_seq = max_seq_len
+        self.T = max(max_tokens_per_step, batch_size)
+        self.plan = build_resident_buffer_plan(g, weights_bytes=runtime_weight_bytes(runtime), batch_size=batch_size,
+                                               max_seq_len=max_seq_len, max_tokens_per_step=self.T)
+        self.arenas = allocate_arenas(self.plan, g, runtime.device, runtime.dtype)
+        self.kv = self.arenas.kv
+        self.S = self.kv.layout.max_seq_len
+        self.cos, self.sin = build_qwen_position_cache(runtime.rope_inv_freq, runtime.attention_scaling, self.S,
+                                                       runtime.dtype)
+        dev = runtime.device
+        ws = max(K.attention_workspace_bytes(batch_size, q, g.num_attention_heads, g.num_key_value_heads, g.head_dim,
+                                             self.S) for q in range(1, self.T // batch_size + 1))
+        self.attn_ws = torch.zeros(max(ws, 256), device=dev, dtype=torch.uint8)
+        self.lm_ws = torch.zeros(K.lmhead_workspace_bytes(batch_size, g.vocab_size), device=dev, dtype=torch.uint8)
+        self.use_graph = use_graph
+        self.graph: torch.cuda.CUDAGraph | None = None
+
+    # ------------------------------------------------------------------
+    def _forward(self, q_len: int, head: bool) -> None:
+        """Enqueue one step of ``q_len`` tokens per sequence on the current stream."""
+        B, g, a, rt = self.B, self.g, self.arenas, self.rt
+        m = B * q_len
+        eps = g.rms_norm_eps
+        kv = self.kv
+        K.embed_gather(a.ids[:m], rt.embed_tokens_weight, out=a.x[:m])
+        for li, layer in enumerate(rt.layers):
+            att, mlp = layer.attention, layer.mlp
+            K.qkv_rope_append(a.x[:m], B, q_len, att.qkv_proj_weight, g.num_attention_heads, g.num_key_value_heads,
+                              g.head_dim, att.q_norm_weight, att.k_norm_weight, self.cos, self.sin,
+                              input_norm_w=layer.input_layernorm_weight, eps=eps, cache_pos=kv.cache_pos,
+                              k_cache=kv.key_cache[li], v_cache=kv.value_cache[li], max_seq=self.S,
+                              qkv_scratch=a.qkv[:m], q_out=a.q[:m])
+            K.decode_attention(a.q[:m], kv.key_cache[li], kv.value_cache[li], B, q_len, g.num_attention_heads,
+                               g.num_key_value_heads, g.head_dim, self.S, att.attention_scale,
+                               cache_pos=kv.cache_pos, out=a.attn[:m], workspace=self.attn_ws)
+            K.oproj_residual(a.attn[:m], att.o_proj_weight, a.x[:m], out=a.h[:m])
+            K.gateup_silu(a.h[:m], layer.post_attention_layernorm_weight, mlp.gate_up_proj_weight, eps,
+                          out=a.act[:m])
+            K.down_residual(a.act[:m], mlp.down_proj_weight, a.h[:m], out=a.x[:m])
+        if head:
+            if q_len == 1:
+                rows = a.x[:B]
+            else:
+                a.head_rows.copy_(a.x[:m].view(B, q_len, -1)[:, -1])
+                rows = a.head_rows
+            K.lmhead_argmax(rows, rt.final_norm_weight, rt.lm_head_weight, eps, out_ids=a.ids[:B],
+                            workspace=self.lm_ws)
+        K.advance_cursors(kv.cache_pos, q_len)
+
+    # ------------------------------------------------------------------
+    def reset(self) -> None:
+        self.kv.reset()
+
+    def prefill(self, prompt_ids: torch.Tensor) -> torch.Tensor:
+        """Run ``prompt_ids [B, P]`` through the stack; returns the first greedy token per sequence ``[B]``.
+
+        The prompt runs in chunks of ``T // B`` tokens per sequence; the head
+        runs once, on the last position.
+        """
+        if prompt_ids.dim() != 2 or prompt_ids.shape[0] != self.B:
+            raise ValueError(f"prompt_ids must be [{self.B}, P]")
+        ids = prompt_ids.to(self.rt.device, torch.int64)
+        P = ids.shape[1]
+        start = self.kv.sequence_lens[0]
+        if start + P > self.S:
+            raise ValueError(f"prompt of {P} tokens does not fit: cursor {start}, max_seq {self.S}")
+        chunk = max(1, self.T // self.B)
+        for c0 in range(0, P, chunk):
+            c1 = min(P, c0 + chunk)
+            q = c1 - c0
+            self.arenas.ids[:self.B * q].copy_(ids[:, c0:c1].reshape(-1))
+            self._forward(q, head=(c1 == P))
+            self.kv.note_advanced(q)
+        return self.arenas.ids[:self.B].clone()
+
+    def set_next_ids(self, ids: torch.Tensor) -> None:
+        self.arenas.ids[:self.B].copy_(ids.reshape(-1).to(self.arenas.ids.device))
+
+    def capture(self) -> None:
+        """Capture one decode step (q_len 1 + head + cursor advance) as a CUDA graph."""
+        a = self.arenas
+        saved_pos = self.kv.cache_pos.clone()
+        saved_ids = a.ids[:self.B].clone()
+        self._forward(1, head=True)  # eager warm-up: sets kernel attributes, resolves symbols
+        torch.cuda.synchronize()
+        self.kv.cache_pos.copy_(saved_pos)
+        a.ids[:self.B].copy_(saved_ids)
+        graph = torch.cuda.CUDAGraph()
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.graph(graph, stream=stream):
+            self._forward(1, head=True)
+        torch.cuda.current_stream().wait_stream(stream)
+        torch.cuda.synchronize()
+        self.graph = graph
+
+    def decode_step(self) -> None:
+        """Enqueue one decode step (graph replay when captured)."""
+        if self.kv.sequence_lens[0] + 1 > self.S:
+            raise ValueError("KV cache is full")
+        if self.use_graph and self.graph is None:
+            self.capture()
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._forward(1, head=True)
+        self.kv.note_advanced(1)
+
+    @property
+    def current_ids(self) -> torch.Tensor:
+        return self.arenas.ids[:self.B]
+
+    def generate(self, prompt_ids: torch.Tensor, new_tokens: int) -> torch.Tensor:
+        """Prefill then greedy-decode; returns ``[B, new_tokens]`` (first token from the prefill)."""
+        first = self.prefill(prompt_ids)
+        out = [first]
+        for _ in range(new_tokens - 1):
+            self.decode_step()
+            out.append(self.current_ids.clone())
+        return torch.stack(out, dim=1)
+
+    def kernel_launches_per_step(self) -> int:
+        """Kernels one decode step launches: embed + per layer (2 QKV + attention + 3 linears) + head + cursor."""
+        return 1 + 6 * len(self.rt.layers) + 1 + 1

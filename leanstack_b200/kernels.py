@@ -1,0 +1,227 @@
+"""Torch-tensor front end of the C ABI.
+
+Each function takes CUDA tensors, checks dtype / device / layout, and enqueues
+the kernel on torch's current stream.  Outputs are written into caller tensors
+when given (the engine passes its resident arenas) and allocated otherwise (the
+reference-style dispatch helpers return fresh tensors, as the reference does).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native as nat
+from ._native import EPI_RESIDUAL, EPI_SILU_MUL, EPI_STORE  # noqa: F401
+
+BF16 = torch.bfloat16
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _check(t: torch.Tensor, name: str, dtype=BF16, contiguous: bool = True) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (got {t.device}); there is no CPU path")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if contiguous and not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def sm_count() -> int:
+    v = ctypes.c_int(0)
+    nat.call("ls_sm_count", ctypes.byref(v))
+    return v.value
+
+
+def device_error(clear: bool = True) -> int:
+    v = ctypes.c_int(0)
+    nat.call("ls_get_device_error", ctypes.byref(v), int(clear))
+    return v.value
+
+
+def embed_gather(ids: torch.Tensor, embed: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(ids, "ids", torch.int64)
+    _check(embed, "embed")
+    m = ids.numel()
+    if out is None:
+        out = torch.empty((m, embed.shape[1]), device=embed.device, dtype=BF16)
+    nat.call("ls_embed_gather", ids.data_ptr(), m, embed.data_ptr(), embed.shape[0], embed.shape[1],
+             out.data_ptr(), _stream())
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(x, "x")
+    _check(w, "w")
+    n = x.shape[-1]
+    m = x.numel() // n
+    if out is None:
+        out = torch.empty_like(x)
+    nat.call("ls_rmsnorm", x.data_ptr(), m, n, w.data_ptr(), float(eps), out.data_ptr(), _stream())
+    return out
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, *, norm_w: torch.Tensor | None = None, eps: float = 1e-6,
+           epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """``out = epilogue(w @ rmsnorm?(x))`` for x ``[m, k]`` with m <= 8."""
+    _check(x, "x")
+    _check(w, "w")
+    k = x.shape[-1]
+    m = x.numel() // k
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"weight in-features {w.shape[1]} != activation width {k}")
+    if norm_w is not None:
+        _check(norm_w, "norm_w")
+    if residual is not None:
+        _check(residual, "residual")
+    cols = n // 2 if epilogue == EPI_SILU_MUL else n
+    if out is None:
+        out = torch.empty((*x.shape[:-1], cols), device=x.device, dtype=BF16)
+    nat.call("ls_linear_bf16", x.data_ptr(), m, k, _ptr(norm_w), float(eps), w.data_ptr(), n, int(epilogue),
+             _ptr(residual), out.data_ptr(), _stream())
+    return out
+
+
+def qkv_rope_append(x: torch.Tensor, batch: int, q_len: int, qkv_w: torch.Tensor, num_heads: int,
+                    num_kv_heads: int, head_dim: int, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor,
+                    cos: torch.Tensor, sin: torch.Tensor, *, input_norm_w: torch.Tensor | None = None,
+                    eps: float = 1e-6, cache_pos: torch.Tensor | None = None, uniform_past: int = 0,
+                    k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None, max_seq: int = 0,
+                    k_out: torch.Tensor | None = None, v_out: torch.Tensor | None = None,
+                    qkv_scratch: torch.Tensor | None = None, q_out: torch.Tensor | None = None):
+    """Input RMSNorm + QKV projection + q/k norm + RoPE + KV append (one C call)."""
+    _check(x, "x")
+    _check(qkv_w, "qkv_w")
+    _check(cos, "cos")
+    _check(sin, "sin")
+    m = batch * q_len
+    hidden = x.shape[-1]
+    if cache_pos is not None:
+        _check(cache_pos, "cache_pos", torch.int32)
+    dev = x.device
+    if qkv_scratch is None:
+        qkv_scratch = torch.empty((m, qkv_w.shape[0]), device=dev, dtype=BF16)
+    if q_out is None:
+        q_out = torch.empty((m, num_heads, head_dim), device=dev, dtype=BF16)
+    nat.call("ls_rmsnorm_qkv_rope_kvappend", x.data_ptr(), batch, q_len, hidden, _ptr(input_norm_w), float(eps),
+             qkv_w.data_ptr(), num_heads, num_kv_heads, head_dim, q_norm_w.data_ptr(), k_norm_w.data_ptr(),
+             cos.data_ptr(), sin.data_ptr(), cos.shape[0], _ptr(cache_pos), int(uniform_past), _ptr(k_cache),
+             _ptr(v_cache), int(max_seq), _ptr(k_out), _ptr(v_out), qkv_scratch.data_ptr(), q_out.data_ptr(),
+             _stream())
+    return q_out
+
+
+def attention_workspace_bytes(batch: int, q_len: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                              max_seq: int) -> int:
+    v = ctypes.c_int64(0)
+    nat.call("ls_decode_attention_workspace_bytes", batch, q_len, num_heads, num_kv_heads, head_dim, max_seq,
+             ctypes.byref(v))
+    return v.value
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, batch: int, q_len: int,
+                     num_heads: int, num_kv_heads: int, head_dim: int, max_seq: int, scale: float, *,
+                     cache_pos: torch.Tensor | None = None, uniform_past: int = 0,
+                     out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """GQA attention over a ``[batch, Hkv, max_seq, D]`` cache slice.
+
+    ``k_cache`` may be a strided view whose base pointer starts the slice; its
+    sequence stride must equal ``head_dim`` and the (b, h) stride
+    ``max_seq * head_dim``.
+    """
+    _check(q, "q")
+    for name, t in (("k_cache", k_cache), ("v_cache", v_cache)):
+        if t.dtype != BF16 or t.device.type != "cuda":
+            raise TypeError(f"{name} must be a bf16 CUDA tensor")
+    m = batch * q_len
+    if out is None:
+        out = torch.empty((m, num_heads * head_dim), device=q.device, dtype=BF16)
+    need = attention_workspace_bytes(batch, q_len, num_heads, num_kv_heads, head_dim, max_seq)
+    if workspace is None:
+        workspace = torch.zeros(max(need, 256), device=q.device, dtype=torch.uint8)
+    nat.call("ls_decode_attention", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _ptr(cache_pos),
+             int(uniform_past), batch, q_len, num_heads, num_kv_heads, head_dim, max_seq, float(scale),
+             out.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
+    return out
+
+
+def oproj_residual(attn: torch.Tensor, o_w: torch.Tensor, residual: torch.Tensor,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(attn, "attn")
+    _check(o_w, "o_w")
+    _check(residual, "residual")
+    k = attn.shape[-1]
+    m = attn.numel() // k
+    if out is None:
+        out = torch.empty_like(residual)
+    nat.call("ls_oproj_residual", attn.data_ptr(), m, k, o_w.data_ptr(), o_w.shape[0], residual.data_ptr(),
+             out.data_ptr(), _stream())
+    return out
+
+
+def gateup_silu(h: torch.Tensor, post_norm_w: torch.Tensor | None, gate_up_w: torch.Tensor, eps: float,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(h, "h")
+    _check(gate_up_w, "gate_up_w")
+    hidden = h.shape[-1]
+    m = h.numel() // hidden
+    inter = gate_up_w.shape[0] // 2
+    if out is None:
+        out = torch.empty((*h.shape[:-1], inter), device=h.device, dtype=BF16)
+    nat.call("ls_rmsnorm_gateup_silu", h.data_ptr(), m, hidden, _ptr(post_norm_w), float(eps),
+             gate_up_w.data_ptr(), inter, out.data_ptr(), _stream())
+    return out
+
+
+def down_residual(act: torch.Tensor, down_w: torch.Tensor, residual: torch.Tensor,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(act, "act")
+    _check(down_w, "down_w")
+    _check(residual, "residual")
+    inter = act.shape[-1]
+    m = act.numel() // inter
+    if out is None:
+        out = torch.empty_like(residual)
+    nat.call("ls_down_residual", act.data_ptr(), m, inter, down_w.data_ptr(), down_w.shape[0],
+             residual.data_ptr(), out.data_ptr(), _stream())
+    return out
+
+
+def lmhead_workspace_bytes(m: int, vocab: int) -> int:
+    v = ctypes.c_int64(0)
+    nat.call("ls_lmhead_workspace_bytes", m, vocab, ctypes.byref(v))
+    return v.value
+
+
+def lmhead_argmax(h: torch.Tensor, final_norm_w: torch.Tensor | None, lm_head_w: torch.Tensor, eps: float, *,
+                  out_ids: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    _check(h, "h")
+    _check(lm_head_w, "lm_head_w")
+    hidden = h.shape[-1]
+    m = h.numel() // hidden
+    vocab = lm_head_w.shape[0]
+    if out_ids is None:
+        out_ids = torch.empty((m,), device=h.device, dtype=torch.int64)
+    need = lmhead_workspace_bytes(m, vocab)
+    if workspace is None:
+        workspace = torch.zeros(need, device=h.device, dtype=torch.uint8)
+    nat.call("ls_lmhead_argmax", h.data_ptr(), m, hidden, _ptr(final_norm_w), float(eps), lm_head_w.data_ptr(),
+             vocab, out_ids.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
+    return out_ids
+
+
+def advance_cursors(cache_pos: torch.Tensor, q_len: int, delta: torch.Tensor | None = None) -> None:
+    _check(cache_pos, "cache_pos", torch.int32)
+    nat.call("ls_advance_cursors", cache_pos.data_ptr(), _ptr(delta), cache_pos.numel(), int(q_len), _stream())

@@ -1,0 +1,209 @@
+"""Kernel-level parity of libleanb200.so against fp32 references (B200 only).
+
+Each kernel is checked against the same op computed in fp32 by torch with the
+reference's bf16 rounding points, within the north star's bound
+(max-abs error <= 2e-2 * max(1, max|ref|)); elementwise kernels must also be
+bit-exact on nearly every element.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import tol
+from leanstack_b200 import kernels as K
+from leanstack_b200 import synth
+from oracle import qwen_oracle as qo
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _rms_ref(x, w, eps):
+    xf = x.float()
+    r = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return ((xf * r) * w.float()).bfloat16()
+
+
+def _rand(shape, std, name, seed=11):
+    return synth.normal(shape, std, seed, name, device=DEV)
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("k,n", [(2560, 6144), (4096, 2560), (9728, 2560), (264, 136)])
+def test_linear_store_and_norm(m, k, n):
+    x = _rand((m, k), 1.0, f"x{m}{k}")
+    w = _rand((n, k), 0.02, f"w{k}{n}")
+    nw = synth.norm_weight((k,), 11, f"nw{k}", device=DEV)
+    y = K.linear(x, w)
+    ref = (x.float() @ w.float().t())
+    assert (y.float() - ref).abs().max().item() <= tol(ref)
+    assert (y == ref.bfloat16()).float().mean().item() > 0.99
+    yn = K.linear(x, w, norm_w=nw, eps=1e-6)
+    xn = _rms_ref(x, nw, 1e-6)
+    refn = xn.float() @ w.float().t()
+    assert (yn.float() - refn).abs().max().item() <= tol(refn)
+    assert (yn == refn.bfloat16()).float().mean().item() > 0.99
+
+
+@pytest.mark.parametrize("m", [1, 4, 8])
+def test_linear_residual_and_silu(m):
+    k, n = 2560, 2560
+    x = _rand((m, 4096), 1.0, "xo")
+    w = _rand((n, 4096), 0.02, "wo")
+    res = _rand((m, n), 1.0, "res")
+    y = K.oproj_residual(x, w, res)
+    ref = res.float() + (x.float() @ w.float().t()).bfloat16().float()
+    assert (y.float() - ref).abs().max().item() <= tol(ref)
+    assert (y == ref.bfloat16()).float().mean().item() > 0.99
+    inter = 1536
+    gu = _rand((2 * inter, k), 0.02, "gu")
+    nw = synth.norm_weight((k,), 11, "post", device=DEV)
+    h = _rand((m, k), 1.0, "h")
+    act = K.gateup_silu(h, nw, gu, 1e-6)
+    hn = _rms_ref(h, nw, 1e-6)
+    g_u = (hn.float() @ gu.float().t()).bfloat16()
+    g, u = g_u[:, :inter], g_u[:, inter:]
+    ref = (F.silu(g.float()).bfloat16().float() * u.float())
+    assert act.shape == (m, inter)
+    assert (act.float() - ref).abs().max().item() <= tol(ref)
+    assert (act == ref.bfloat16()).float().mean().item() > 0.99
+    d = _rand((k, inter), 0.02, "down")
+    out = K.down_residual(act, d, h)
+    ref = h.float() + (act.float() @ d.float().t()).bfloat16().float()
+    assert (out.float() - ref).abs().max().item() <= tol(ref)
+
+
+def test_linear_is_deterministic():
+    x = _rand((1, 9728), 1.0, "xd")
+    w = _rand((2560, 9728), 0.02, "wd")
+    a = K.linear(x, w)
+    for _ in range(3):
+        assert torch.equal(K.linear(x, w), a)
+
+
+def test_rmsnorm_and_embed():
+    x = _rand((3, 2560), 1.0, "xr")
+    w = synth.norm_weight((2560,), 1, "nr", device=DEV)
+    y = K.rmsnorm(x, w, 1e-6)
+    ref = qo.rmsnorm(x.cpu(), w.cpu(), 1e-6)
+    assert (y.cpu() == ref).float().mean().item() > 0.999
+    assert (y.float().cpu() - ref.float()).abs().max().item() <= 2 ** -6
+    emb = _rand((1000, 256), 0.02, "emb")
+    ids = torch.tensor([5, 999, 0, 5], device=DEV)
+    assert torch.equal(K.embed_gather(ids, emb), emb[ids])
+
+
+@pytest.mark.parametrize("q_len", [1, 2, 5])
+def test_qkv_rope_append_matches_oracle(q_len):
+    hq, hkv, d, hidden, batch, past = 32, 8, 128, 2560, 2, 37
+    x = _rand((batch * q_len, hidden), 1.0, "qx")
+    qkv_w = _rand(((hq + 2 * hkv) * d, hidden), 0.02, "qkvw")
+    qn = synth.norm_weight((d,), 2, "qn", device=DEV)
+    kn = synth.norm_weight((d,), 2, "kn", device=DEV)
+    ln = synth.norm_weight((hidden,), 2, "ln", device=DEV)
+    cos, sin = qo.rope_cache(qo.rope_inv_freq(d, 1e6), 128, torch.bfloat16)
+    kc = torch.zeros(batch, hkv, 128, d, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    cache_pos = torch.tensor([past, past + 3], device=DEV, dtype=torch.int32)
+    q = K.qkv_rope_append(x, batch, q_len, qkv_w, hq, hkv, d, qn, kn, cos.to(DEV), sin.to(DEV), input_norm_w=ln,
+                          cache_pos=cache_pos, k_cache=kc, v_cache=vc, max_seq=128)
+    # oracle on the CPU with the same inputs, per sequence (positions differ)
+    for b in range(batch):
+        p0 = past + 3 * b
+        xb = x[b * q_len:(b + 1) * q_len].cpu().view(1, q_len, hidden)
+        w = qo.LayerWeights(input_layernorm=ln.cpu(), qkv_proj=qkv_w.cpu(), o_proj=None, q_norm=qn.cpu(),
+                            k_norm=kn.cpu(), post_attention_layernorm=None, gate_up_proj=None, down_proj=None)
+        xn = qo.rmsnorm(xb, w.input_layernorm, 1e-6)
+        rq, rk, rv = qo.qkv_project(xn, w, hq, hkv, d, cos[p0:p0 + q_len][None], sin[p0:p0 + q_len][None], 1e-6)
+        got_q = q[b * q_len:(b + 1) * q_len].cpu().view(q_len, hq, d).transpose(0, 1)[None]
+        for got, want in ((got_q, rq), (kc[b, :, p0:p0 + q_len].cpu()[None], rk),
+                          (vc[b, :, p0:p0 + q_len].cpu()[None], rv)):
+            assert got.shape == want.shape
+            assert (got == want).float().mean().item() > 0.99
+            assert (got.float() - want.float()).abs().max().item() <= tol(want.float())
+
+
+def _attn_ref(q, kc, vc, cache_pos, q_len, hq, hkv, scale):
+    """fp32 GQA attention with the causal-suffix visibility rule."""
+    batch = kc.shape[0]
+    out = []
+    for b in range(batch):
+        past = int(cache_pos[b])
+        L = past + q_len
+        qb = q[b * q_len:(b + 1) * q_len].float().transpose(0, 1)  # [Hq, Q, D]
+        kb = kc[b, :, :L].float().repeat_interleave(hq // hkv, 0)
+        vb = vc[b, :, :L].float().repeat_interleave(hq // hkv, 0)
+        s = (qb @ kb.transpose(1, 2)) * scale
+        mask = torch.arange(L, device=q.device)[None, :] > (past + torch.arange(q_len, device=q.device))[:, None]
+        s = s.masked_fill(mask[None], float("-inf"))
+        o = torch.softmax(s, -1) @ vb  # [Hq, Q, D]
+        out.append(o.transpose(0, 1).reshape(q_len, -1))
+    return torch.cat(out, 0)
+
+
+@pytest.mark.parametrize("batch,q_len,lens", [(1, 1, [513]), (1, 1, [4000]), (3, 1, [5, 700, 2049]),
+                                              (2, 5, [64, 1024]), (1, 8, [504]), (4, 2, [1, 2, 3, 17])])
+def test_decode_attention(batch, q_len, lens):
+    hq, hkv, d, S = 32, 8, 128, 4096
+    kc = _rand((batch, hkv, S, d), 1.0, "kc")
+    vc = _rand((batch, hkv, S, d), 1.0, "vc")
+    q = _rand((batch * q_len, hq, d), 1.0, "q")
+    cache_pos = torch.tensor(lens, device=DEV, dtype=torch.int32)
+    scale = d ** -0.5
+    out = K.decode_attention(q, kc, vc, batch, q_len, hq, hkv, d, S, scale, cache_pos=cache_pos)
+    ref = _attn_ref(q, kc, vc, lens, q_len, hq, hkv, scale)
+    assert (out.float() - ref).abs().max().item() <= tol(ref)
+    assert (out.float() - ref).abs().max().item() <= 2 ** -7
+    if len(set(lens)) == 1:  # uniform cursor via the host argument
+        out2 = K.decode_attention(q, kc, vc, batch, q_len, hq, hkv, d, S, scale, uniform_past=lens[0])
+        assert torch.equal(out, out2)
+
+
+def test_lmhead_argmax_matches_bf16_logits_and_ties():
+    vocab, hidden = 151936, 2560
+    w = _rand((vocab, hidden), 0.02, "lm")
+    h = _rand((2, hidden), 1.0, "hh")
+    nw = synth.norm_weight((hidden,), 3, "fn", device=DEV)
+    ids = K.lmhead_argmax(h, nw, w, 1e-6)
+    hn = _rms_ref(h, nw, 1e-6)
+    logits = (hn.float() @ w.float().t()).bfloat16()
+    for r in range(2):
+        row = logits[r].float()
+        top2 = row.topk(2).values
+        best = row.max()
+        first_max = int(torch.nonzero(row == best)[0])
+        if (top2[0] - top2[1]).item() > 2 ** -5:  # no near-tie: must be the reference's argmax
+            assert int(ids[r]) == first_max
+        else:  # near-tie: a different fp32 summation order may pick the neighbour
+            assert row[ids[r]].item() >= best.item() - 2 ** -5
+    # exact ties with exactly representable logits: lowest index must win
+    w2 = torch.zeros(vocab, 256, device=DEV, dtype=torch.bfloat16)
+    w2[:, 0] = 0.25
+    w2[100000, 1] = 1.0
+    w2[7, 1] = 1.0
+    w2[150000, 1] = 1.0
+    h2 = torch.zeros(1, 256, device=DEV, dtype=torch.bfloat16)
+    h2[0, :2] = 1.0
+    assert int(K.lmhead_argmax(h2, None, w2, 1e-6)[0]) == 7
+    w2[3, 1] = 1.0
+    assert int(K.lmhead_argmax(h2, None, w2, 1e-6)[0]) == 3
+
+
+def test_kv_overflow_sets_device_flag_without_fault():
+    hq, hkv, d, hidden = 4, 2, 128, 512
+    x = _rand((1, hidden), 1.0, "ox")
+    w = _rand(((hq + 2 * hkv) * d, hidden), 0.02, "ow")
+    qn = synth.norm_weight((d,), 2, "oqn", device=DEV)
+    cos, sin = qo.rope_cache(qo.rope_inv_freq(d, 1e6), 64, torch.bfloat16)
+    kc = torch.zeros(1, hkv, 16, d, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    K.device_error(clear=True)
+    cache_pos = torch.tensor([16], device=DEV, dtype=torch.int32)  # one past the arena
+    K.qkv_rope_append(x, 1, 1, w, hq, hkv, d, qn, qn, cos.to(DEV), sin.to(DEV), cache_pos=cache_pos, k_cache=kc,
+                      v_cache=vc, max_seq=16)
+    assert K.device_error(clear=True) == 6  # LS_ERR_KV_OVERFLOW
+    assert kc.abs().sum().item() == 0
+    assert K.device_error(clear=True) == 0

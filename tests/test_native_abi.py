@@ -1,0 +1,73 @@
+"""The C-ABI library loads on a machine without a GPU and exports every
+symbol that include/leanb200.h declares.  No kernel is launched here."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from leanstack_b200 import _native as nat
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "leanb200.h"
+
+
+def declared_symbols() -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(ls_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not nat.LIB_PATH.exists():
+        from leanstack_b200 import build
+
+        build.build()
+    return nat.load()
+
+
+def test_header_declares_the_hot_path_entry_points():
+    syms = declared_symbols()
+    for name in ("ls_rmsnorm_qkv_rope_kvappend", "ls_decode_attention", "ls_oproj_residual",
+                 "ls_rmsnorm_gateup_silu", "ls_down_residual", "ls_lmhead_argmax", "ls_version", "ls_last_error"):
+        assert name in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_symbols():
+        assert hasattr(lib, name), f"{name} declared in leanb200.h but not exported"
+    assert set(declared_symbols()) <= set(nat.exported_symbols()), "ctypes signature table is incomplete"
+
+
+def test_version_and_argument_errors_without_gpu(lib):
+    assert lib.ls_version() == 1
+    # argument validation happens before any CUDA call and returns a code
+    rc = lib.ls_linear_bf16(None, 1, 2560, None, ctypes.c_float(1e-6), None, 4096, 0, None, None, None)
+    assert rc == 1  # LS_ERR_INVALID_ARGUMENT
+    assert "null" in nat.last_error()
+    rc = lib.ls_rmsnorm_qkv_rope_kvappend(*([None] + [1, 1, 2560, None, ctypes.c_float(1e-6), None, 32, 8, 64]
+                                            + [None] * 4 + [16, None, 0, None, None, 16, None, None, None, None,
+                                                            None]))
+    assert rc != 0
+    with pytest.raises(nat.LeanB200Error):
+        nat.call("ls_embed_gather", None, 1, None, 10, 8, None, None)
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(nat, "LIB_PATH", tmp_path / "nope.so")
+    monkeypatch.setattr(nat, "_LIB", None)
+    with pytest.raises(nat.NativeLibraryMissing):
+        nat.load()
+
+
+def test_kernel_wrappers_refuse_cpu_tensors():
+    import torch
+
+    from leanstack_b200 import kernels as K
+
+    x = torch.zeros(1, 256, dtype=torch.bfloat16)
+    w = torch.zeros(256, 256, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="no CPU path"):
+        K.linear(x, w)
