@@ -18,7 +18,8 @@
  *   q (rotated)           [m, Hq, D]
  *   attention output      [m, Hq * D]
  *   K / V cache (1 layer) [batch, Hkv, max_seq, D]
- *   rope cos / sin        [rope_len, D / 2]           the reference's bf16 position cache
+ *   rope cos / sin        [rope_len, D / 2]           the reference's bf16 position cache; row r
+ *                         holds position rope_offset + r
  *   cache_pos             int32 [batch] on device:    cached positions of each sequence
  *                         before this call; token i of sequence b sits at
  *                         position cache_pos[b] + i and attends keys 0..cache_pos[b]+i.
@@ -103,9 +104,33 @@ int ls_rmsnorm_qkv_rope_kvappend(const void* x, int64_t batch, int64_t q_len, in
                                  const void* input_norm_w, float eps, const void* qkv_w, int64_t num_heads,
                                  int64_t num_kv_heads, int64_t head_dim, const void* q_norm_w,
                                  const void* k_norm_w, const void* rope_cos, const void* rope_sin,
-                                 int64_t rope_len, const int32_t* cache_pos, int64_t uniform_past, void* k_cache,
+                                 int64_t rope_len, int64_t rope_offset, const int32_t* cache_pos,
+                                 int64_t uniform_past, void* k_cache,
                                  void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* qkv_scratch,
                                  void* q_out, ls_stream_t stream);
+
+/*
+ * The second half of ls_rmsnorm_qkv_rope_kvappend on a precomputed fused
+ * projection qkv [m, (Hq + 2 Hkv) D]: per-head q/k RMSNorm, NeoX RoPE and the
+ * K/V append (src/leanstack/runtime/qwen_explicit.py:793-806, :690-716;
+ * src/leanstack/runtime/kv_cache.py:222-243).  Used after
+ * ls_gemm_bf16_tcgen05 computes the projection for larger batches.
+ */
+int ls_qk_norm_rope_kvappend(const void* qkv, int64_t batch, int64_t q_len, int64_t num_heads, int64_t num_kv_heads,
+                             int64_t head_dim, const void* q_norm_w, const void* k_norm_w, float eps,
+                             const void* rope_cos, const void* rope_sin, int64_t rope_len, int64_t rope_offset,
+                             const int32_t* cache_pos, int64_t uniform_past, void* k_cache, void* v_cache,
+                             int64_t max_seq, void* k_out, void* v_out, void* q_out, ls_stream_t stream);
+
+/*
+ * Row-wise argmax of bf16 logits [m, n] (lowest index on ties): the
+ * reference's `logits.argmax(dim=-1)` (src/leanstack/runtime/qwen_explicit.py:960)
+ * for logits produced by ls_gemm_bf16_tcgen05.  out_ids: int64 [m].
+ * workspace: ls_argmax_rows_workspace_bytes() bytes, zero-filled once.
+ */
+int ls_argmax_rows(const void* logits, int64_t m, int64_t n, int64_t* out_ids, void* workspace,
+                   int64_t workspace_bytes, ls_stream_t stream);
+int ls_argmax_rows_workspace_bytes(int64_t m, int64_t n, int64_t* bytes);
 
 /*
  * GQA attention of q [m, Hq, D] over the cache (keys 0..cache_pos[b]+i for
@@ -149,6 +174,22 @@ int ls_lmhead_argmax(const void* h, int64_t m, int64_t hidden, const void* final
                      const void* lm_head_w, int64_t vocab, int64_t* out_ids, void* workspace,
                      int64_t workspace_bytes, ls_stream_t stream);
 int ls_lmhead_workspace_bytes(int64_t m, int64_t vocab, int64_t* bytes);
+
+/*
+ * Weight-streaming GEMM on the tcgen05 tensor cores for 1 <= m <= 128
+ * activation rows (larger batches run as several launches): out[m, n] = epilogue(x[m, k] . w[n, k]^T) with epilogue one
+ * of ls_epilogue.  For LS_EPI_SILU_MUL, w is the fused [2 n, k] gate_up matrix
+ * and out is [m, n].  This is the batched-decode / speculative-verify form of
+ * the reference's F.linear calls (src/leanstack/runtime/qwen_explicit.py:748,
+ * :819-829) and of the cuTile GEMM it benchmarks
+ * (experiments/cutile/qwen_bf16_hot_kernels.py:19-36).  workspace:
+ * ls_gemm_bf16_tcgen05_workspace_bytes() bytes, zero-filled once before first
+ * use (tile counters are left at zero).
+ */
+int ls_gemm_bf16_tcgen05(const void* x, int64_t m, int64_t k, const void* w, int64_t n, int epilogue,
+                         const void* residual, void* out, void* workspace, int64_t workspace_bytes,
+                         ls_stream_t stream);
+int ls_gemm_bf16_tcgen05_workspace_bytes(int64_t m, int64_t k, int64_t n, int epilogue, int64_t* bytes);
 
 /* Standalone RMSNorm over the last dim, bf16((x * rsqrt(mean(x^2) + eps)) * w),
  * for m rows of length n (src/leanstack/runtime/qwen_explicit.py:621-637). */

@@ -52,7 +52,7 @@ SIGNATURES: dict[str, list] = {
     "ls_embed_gather": [_p, _i64, _p, _i64, _i64, _p, _p],
     "ls_linear_bf16": [_p, _i64, _i64, _p, _f32, _p, _i64, _int, _p, _p, _p],
     "ls_rmsnorm_qkv_rope_kvappend": [_p, _i64, _i64, _i64, _p, _f32, _p, _i64, _i64, _i64, _p, _p, _p, _p, _i64,
-                                     _p, _i64, _p, _p, _i64, _p, _p, _p, _p, _p],
+                                     _i64, _p, _i64, _p, _p, _i64, _p, _p, _p, _p, _p],
     "ls_decode_attention": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _p, _i64, _p],
     "ls_decode_attention_workspace_bytes": [_i64, _i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_i64)],
     "ls_oproj_residual": [_p, _i64, _i64, _p, _i64, _p, _p, _p],
@@ -61,6 +61,12 @@ SIGNATURES: dict[str, list] = {
     "ls_lmhead_argmax": [_p, _i64, _i64, _p, _f32, _p, _i64, _p, _p, _i64, _p],
     "ls_lmhead_workspace_bytes": [_i64, _i64, ctypes.POINTER(_i64)],
     "ls_rmsnorm": [_p, _i64, _i64, _p, _f32, _p, _p],
+    "ls_qk_norm_rope_kvappend": [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _f32, _p, _p, _i64, _i64, _p, _i64, _p,
+                                 _p, _i64, _p, _p, _p, _p],
+    "ls_argmax_rows": [_p, _i64, _i64, _p, _p, _i64, _p],
+    "ls_argmax_rows_workspace_bytes": [_i64, _i64, ctypes.POINTER(_i64)],
+    "ls_gemm_bf16_tcgen05": [_p, _i64, _i64, _p, _i64, _int, _p, _p, _p, _i64, _p],
+    "ls_gemm_bf16_tcgen05_workspace_bytes": [_i64, _i64, _i64, _int, ctypes.POINTER(_i64)],
     "ls_advance_cursors": [_p, _p, _i64, _i64, _p],
 }
 _RESTYPES = {"ls_last_error": ctypes.c_char_p}

@@ -32,12 +32,13 @@ struct QkRopeParams {
   __nv_bfloat16* k_out;      // [M, Hkv, D] or null
   __nv_bfloat16* v_out;
   int* err;
-  int q_len, Hq, Hkv, rope_len, max_seq;
+  int q_len, Hq, Hkv, rope_len, rope_offset, max_seq;
   float eps;
 };
 
 __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(QkRopeParams p) {
   grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int h = blockIdx.y * 4 + warp;
   if (h >= p.Hq + p.Hkv) return;
@@ -50,7 +51,8 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(QkRopeParams p
   const __nv_bfloat16* src = p.qkv + (size_t)t * qkv_dim + (size_t)h * kHeadDim;
   const int e0 = lane * 4;
 
-  if (pos < 0 || pos >= p.rope_len || (!is_q && (p.k_cache != nullptr) && pos >= p.max_seq)) {
+  const int row = pos - p.rope_offset;  // row of the cos/sin table
+  if (pos < 0 || row < 0 || row >= p.rope_len || (!is_q && (p.k_cache != nullptr) && pos >= p.max_seq)) {
     if (lane == 0) raise_device_error(p.err, LS_ERR_KV_OVERFLOW);
     return;
   }
@@ -70,8 +72,8 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(QkRopeParams p
   for (int j = 0; j < 4; ++j) other[j] = __shfl_xor_sync(0xffffffffu, n[j], 16);
   const bool first_half = lane < 16;
   const int idx = first_half ? e0 : e0 - kHeadDim / 2;
-  const uint2 c_u = *reinterpret_cast<const uint2*>(p.cos + (size_t)pos * (kHeadDim / 2) + idx);
-  const uint2 s_u = *reinterpret_cast<const uint2*>(p.sin + (size_t)pos * (kHeadDim / 2) + idx);
+  const uint2 c_u = *reinterpret_cast<const uint2*>(p.cos + (size_t)row * (kHeadDim / 2) + idx);
+  const uint2 s_u = *reinterpret_cast<const uint2*>(p.sin + (size_t)row * (kHeadDim / 2) + idx);
   const float c[4] = {bf16_lo(c_u.x), bf16_hi(c_u.x), bf16_lo(c_u.y), bf16_hi(c_u.y)};
   const float s[4] = {bf16_lo(s_u.x), bf16_hi(s_u.x), bf16_lo(s_u.y), bf16_hi(s_u.y)};
 #pragma unroll
@@ -101,11 +103,20 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(QkRopeParams p
 
 // ---------------------------------------------------------------------------
 // Split-KV decode / verify attention
+//
+// Grid (splits, Hkv * RG, B) with thread-block clusters of `splits` CTAs along
+// x: the splits of one (sequence, kv head, row group) form one cluster.  Each
+// CTA runs an online softmax over its share of the keys, leaves its partial
+// (max, sum, output) in its own shared memory, and cluster rank 0 merges the
+// partials through distributed shared memory after a cluster barrier.  No
+// global workspace, fences or atomics are involved.
 // ---------------------------------------------------------------------------
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * 32;
-constexpr int kRT = 4;   // query rows per CTA
-constexpr int kUK = 4;   // keys per warp per iteration (loads in flight)
+constexpr int kRT = 4;        // query rows per CTA
+constexpr int kUK = 4;        // keys per warp per iteration (loads in flight)
+constexpr int kMinChunk = 16; // keys per split at least
+constexpr int kMaxSplits = 16;
 
 struct AttnParams {
   const __nv_bfloat16* q;        // [M, Hq, D]
@@ -114,38 +125,54 @@ struct AttnParams {
   const int* cache_pos;          // [B] or null (then uniform_past)
   int uniform_past;
   __nv_bfloat16* out;            // [M, Hq * D]
-  float* part;                   // [B, Hkv * RG, splits, kRT, D + 2]
-  unsigned int* counters;        // [B, Hkv * RG]
   int* err;
   int q_len, Hq, Hkv, G, R, RG, splits, max_seq;
   float scale_log2;
 };
 
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_dsmem_f32(const float* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
 __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(AttnParams p) {
   __shared__ float sm_m[kAttnWarps][kRT];
   __shared__ float sm_l[kAttnWarps][kRT];
   __shared__ __align__(16) float sm_o[kAttnWarps][kRT][kHeadDim];
-  __shared__ float fin_m[kRT], fin_l[kRT];
-  __shared__ bool is_last;
+  // This CTA's merged partial, read by cluster rank 0.
+  __shared__ float part_m[kRT], part_l[kRT];
+  __shared__ __align__(16) float part_o[kRT][kHeadDim];
 
   grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int b = blockIdx.z;
   const int y = blockIdx.y;
   const int hkv = y / p.RG, rg = y - hkv * p.RG;
-  const int s = blockIdx.x;
+  const int s = (int)cluster_rank();  // split index == rank in the cluster
   const int cp = p.cache_pos ? p.cache_pos[b] : p.uniform_past;
   int L = cp + p.q_len;  // keys visible to the last token of this sequence
   if (L > p.max_seq || cp < 0) {
-    if (threadIdx.x == 0) raise_device_error(p.err, LS_ERR_KV_OVERFLOW);
-    L = min(max(L, 0), p.max_seq);
+    if (threadIdx.x == 0 && s == 0) raise_device_error(p.err, LS_ERR_KV_OVERFLOW);
+    L = min(max(L, 1), p.max_seq);
   }
-  const int chunk = (L + p.splits - 1) / p.splits;
-  const int j0 = min(s * chunk, L), j1 = min(j0 + chunk, L);
+  int chunk = (L + p.splits - 1) / p.splits;
+  chunk = max(chunk, kMinChunk);
+  const int j0 = min(s * chunk, L), j1 = min(j0 + chunk, L);  // empty for idle splits
   const int r0 = rg * kRT;
   const int nrows = min(kRT, p.R - r0);
 
-  // Load this CTA's query rows (4 dims per lane), pre-scaled into log2 units.
   float qf[kRT][4];
   int lim[kRT];
 #pragma unroll
@@ -217,7 +244,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(AttnPara
     }
   }
 
-  // Merge the warps of this CTA.
+  // Merge the warps of this CTA into part_*.
 #pragma unroll
   for (int rr = 0; rr < kRT; ++rr) {
     if (lane == 0) { sm_m[warp][rr] = m[rr]; sm_l[warp][rr] = l[rr]; }
@@ -231,20 +258,18 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(AttnPara
     float ls = 0.f;
     if (mx != -INFINITY)
       for (int w = 0; w < kAttnWarps; ++w) ls += sm_l[w][rr] * exp2f(sm_m[w][rr] - mx);
-    fin_m[rr] = mx;
-    fin_l[rr] = ls;
+    part_m[rr] = mx;
+    part_l[rr] = ls;
   }
   __syncthreads();
-  // Each thread owns one dimension of each row.
-  const int d = threadIdx.x;  // kAttnThreads == kHeadDim
-  float ov[kRT];
+  const int d = threadIdx.x;  // kAttnThreads == kHeadDim: one dimension per thread
 #pragma unroll
   for (int rr = 0; rr < kRT; ++rr) {
     float acc = 0.f;
-    const float mx = fin_m[rr];
+    const float mx = part_m[rr];
     if (mx != -INFINITY)
       for (int w = 0; w < kAttnWarps; ++w) acc += sm_o[w][rr][d] * exp2f(sm_m[w][rr] - mx);
-    ov[rr] = acc;
+    part_o[rr][d] = acc;
   }
 
   auto store_row = [&](int rr, float value) {
@@ -255,43 +280,27 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(AttnPara
   };
 
   if (p.splits == 1) {
-    for (int rr = 0; rr < nrows; ++rr) store_row(rr, ov[rr] / fin_l[rr]);
+    __syncthreads();
+    for (int rr = 0; rr < nrows; ++rr) store_row(rr, part_o[rr][d] / part_l[rr]);
     return;
   }
-  const size_t pair = (size_t)b * (p.Hkv * p.RG) + y;
-  float* mypart = p.part + ((pair * p.splits + s) * kRT) * (kHeadDim + 2);
-  for (int rr = 0; rr < kRT; ++rr) {
-    mypart[rr * (kHeadDim + 2) + d] = ov[rr];
-    if (d == 0) {
-      mypart[rr * (kHeadDim + 2) + kHeadDim] = fin_m[rr];
-      mypart[rr * (kHeadDim + 2) + kHeadDim + 1] = fin_l[rr];
+  cluster_sync_all();  // every split's partial is in its shared memory
+  if (s == 0) {
+    for (int rr = 0; rr < nrows; ++rr) {
+      float mx = -INFINITY;
+      for (int c = 0; c < p.splits; ++c) mx = fmaxf(mx, ld_dsmem_f32(&part_m[rr], (uint32_t)c));
+      float ls = 0.f, acc = 0.f;
+      for (int c = 0; c < p.splits; ++c) {
+        const float mc = ld_dsmem_f32(&part_m[rr], (uint32_t)c);
+        if (mc == -INFINITY) continue;
+        const float w = exp2f(mc - mx);
+        ls += ld_dsmem_f32(&part_l[rr], (uint32_t)c) * w;
+        acc += ld_dsmem_f32(&part_o[rr][d], (uint32_t)c) * w;
+      }
+      store_row(rr, acc / ls);
     }
   }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned int prev = atomicAdd(p.counters + pair, 1u);
-    is_last = (prev == (unsigned int)p.splits - 1);
-  }
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  const float* base = p.part + (pair * p.splits * kRT) * (kHeadDim + 2);
-  for (int rr = 0; rr < nrows; ++rr) {
-    float mx = -INFINITY;
-    for (int sp = 0; sp < p.splits; ++sp) mx = fmaxf(mx, __ldcg(base + (sp * kRT + rr) * (kHeadDim + 2) + kHeadDim));
-    float ls = 0.f, acc = 0.f;
-    for (int sp = 0; sp < p.splits; ++sp) {
-      const float* e = base + (sp * kRT + rr) * (kHeadDim + 2);
-      const float ms = __ldcg(e + kHeadDim);
-      if (ms == -INFINITY) continue;
-      const float sc = exp2f(ms - mx);
-      ls += __ldcg(e + kHeadDim + 1) * sc;
-      acc += __ldcg(e + d) * sc;
-    }
-    store_row(rr, acc / ls);
-  }
-  if (threadIdx.x == 0) p.counters[pair] = 0u;
+  cluster_sync_all();  // keep every CTA's shared memory alive until rank 0 has read it
 }
 
 }  // namespace lsb
@@ -314,8 +323,8 @@ static cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStr
 }
 
 int launch_qk_norm_rope(const void* qkv, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, const void* qn,
-                        const void* kn, const void* cos, const void* sin, int64_t rope_len, const int32_t* cache_pos,
-                        int64_t uniform_past, void* k_cache, void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* q_out,
+                        const void* kn, const void* cos, const void* sin, int64_t rope_len, int64_t rope_offset,
+                        const int32_t* cache_pos, int64_t uniform_past, void* k_cache, void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* q_out,
                         float eps, cudaStream_t stream) {
   QkRopeParams p = {};
   p.qkv = static_cast<const __nv_bfloat16*>(qkv);
@@ -334,6 +343,7 @@ int launch_qk_norm_rope(const void* qkv, int64_t batch, int64_t q_len, int64_t h
   p.Hq = (int)hq;
   p.Hkv = (int)hkv;
   p.rope_len = (int)rope_len;
+  p.rope_offset = (int)rope_offset;
   p.max_seq = (int)max_seq;
   p.eps = eps;
   p.err = device_error_ptr();
@@ -347,40 +357,38 @@ int launch_qk_norm_rope(const void* qkv, int64_t batch, int64_t q_len, int64_t h
 
 struct AttnPlan {
   int G, R, RG, splits;
-  size_t counter_bytes, part_bytes;
 };
 
+// Splits per (sequence, kv head, row group): a power of two up to 16, enough
+// for about two CTAs per SM, and no more than the cache has 16-key chunks.
 static AttnPlan attn_plan(int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int64_t max_seq) {
   AttnPlan pl;
   pl.G = (int)(hq / hkv);
   pl.R = (int)(q_len * pl.G);
   pl.RG = (pl.R + kRT - 1) / kRT;
   const int64_t pairs = batch * hkv * pl.RG;
-  int64_t splits = (4 * (int64_t)sm_count() + pairs - 1) / pairs;
-  const int64_t by_len = (max_seq + 31) / 32;
-  if (splits > by_len) splits = by_len;
-  if (splits > 64) splits = 64;
-  if (splits < 1) splits = 1;
-  pl.splits = (int)splits;
-  pl.counter_bytes = ((size_t)pairs * sizeof(unsigned int) + 255) / 256 * 256;
-  pl.part_bytes = pl.splits > 1 ? (size_t)pairs * pl.splits * kRT * (kHeadDim + 2) * sizeof(float) : 0;
+  int splits = 1;
+  while (splits < kMaxSplits && pairs * splits < 2 * (int64_t)sm_count() &&
+         (int64_t)(splits * 2) * kMinChunk <= max_seq)
+    splits *= 2;
+  pl.splits = splits;
   return pl;
 }
 
 int attention_workspace_bytes(int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int64_t max_seq,
                               int64_t* bytes) {
-  AttnPlan pl = attn_plan(batch, q_len, hq, hkv, max_seq);
-  *bytes = (int64_t)(pl.counter_bytes + pl.part_bytes);
+  (void)attn_plan(batch, q_len, hq, hkv, max_seq);
+  *bytes = 0;  // partials are merged through distributed shared memory
   return LS_OK;
 }
 
 int launch_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
-                            int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int64_t max_seq, float scale,
-                            void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
+                            int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv,
+                            int64_t max_seq, float scale, void* out, void* workspace, int64_t workspace_bytes,
+                            cudaStream_t stream) {
+  (void)workspace;
+  (void)workspace_bytes;
   AttnPlan pl = attn_plan(batch, q_len, hq, hkv, max_seq);
-  if (pl.splits > 1 && (!workspace || workspace_bytes < (int64_t)(pl.counter_bytes + pl.part_bytes)))
-    return set_error(LS_ERR_WORKSPACE, "decode_attention: workspace needs %zu bytes",
-                     pl.counter_bytes + pl.part_bytes);
   AttnParams p = {};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k_cache = static_cast<const __nv_bfloat16*>(k_cache);
@@ -388,8 +396,6 @@ int launch_decode_attention(const void* q, const void* k_cache, const void* v_ca
   p.cache_pos = cache_pos;
   p.uniform_past = (int)uniform_past;
   p.out = static_cast<__nv_bfloat16*>(out);
-  p.counters = static_cast<unsigned int*>(workspace);
-  p.part = pl.splits > 1 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.counter_bytes) : nullptr;
   p.q_len = (int)q_len;
   p.Hq = (int)hq;
   p.Hkv = (int)hkv;
@@ -400,9 +406,30 @@ int launch_decode_attention(const void* q, const void* k_cache, const void* v_ca
   p.max_seq = (int)max_seq;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = device_error_ptr();
-  cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg =
-      pdl_config(dim3(pl.splits, (unsigned)(hkv * pl.RG), (unsigned)batch), dim3(kAttnThreads), 0, stream, attr);
+  static bool nonportable_set = false;
+  if (pl.splits > 8 && !nonportable_set) {
+    cudaError_t e = cudaFuncSetAttribute(decode_attention_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "cluster size attribute: %s", cudaGetErrorString(e));
+    nonportable_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.splits, (unsigned)(hkv * pl.RG), (unsigned)batch);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeClusterDimension;
+  attr[na].val.clusterDim.x = pl.splits;
+  attr[na].val.clusterDim.y = 1;
+  attr[na].val.clusterDim.z = 1;
+  ++na;
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
   cudaError_t e = cudaLaunchKernelEx(&cfg, decode_attention_kernel, p);
   if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "decode_attention launch: %s", cudaGetErrorString(e));
   return LS_OK;

@@ -48,6 +48,63 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, in
     out[(size_t)blockIdx.x * n + i] = f_to_bf16((bf16_to_f(xr[i]) * r) * bf16_to_f(w[i]));
 }
 
+// Row argmax over bf16 logits: grid (chunks, m); each CTA reduces one chunk of
+// one row, the last CTA of the row reduces the chunk winners.
+constexpr int kArgmaxThreads = 256;
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const __nv_bfloat16* logits, int n, int chunks,
+                                                                     float* part_val, int* part_idx,
+                                                                     unsigned int* counters, int64_t* out_ids) {
+  grid_dep_wait();
+  __shared__ float bv[kArgmaxThreads / 32];
+  __shared__ int bi[kArgmaxThreads / 32];
+  __shared__ bool is_last;
+  const int row = blockIdx.y, c = blockIdx.x;
+  const int lo = (int)(((long long)n * c) / chunks), hi = (int)(((long long)n * (c + 1)) / chunks);
+  const __nv_bfloat16* r = logits + (size_t)row * n;
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  for (int i = lo + threadIdx.x; i < hi; i += kArgmaxThreads) {
+    const float v = bf16_to_f(r[i]);
+    if (v > best || (v == best && i < besti)) { best = v; besti = i; }
+  }
+  auto reduce = [&]() {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+      if (ov > best || (ov == best && oi < besti)) { best = ov; besti = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { bv[threadIdx.x >> 5] = best; bi[threadIdx.x >> 5] = besti; }
+    __syncthreads();
+    if (threadIdx.x == 0)
+      for (int w = 1; w < kArgmaxThreads / 32; ++w)
+        if (bv[w] > best || (bv[w] == best && bi[w] < besti)) { best = bv[w]; besti = bi[w]; }
+  };
+  reduce();
+  if (threadIdx.x == 0) {
+    part_val[(size_t)row * chunks + c] = best;
+    part_idx[(size_t)row * chunks + c] = besti;
+    __threadfence();
+    is_last = atomicAdd(counters + row, 1u) == (unsigned int)chunks - 1;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  best = -INFINITY;
+  besti = 0x7fffffff;
+  for (int i = threadIdx.x; i < chunks; i += kArgmaxThreads) {
+    const float v = __ldcg(part_val + (size_t)row * chunks + i);
+    const int idx = __ldcg(part_idx + (size_t)row * chunks + i);
+    if (v > best || (v == best && idx < besti)) { best = v; besti = idx; }
+  }
+  __syncthreads();
+  reduce();
+  if (threadIdx.x == 0) {
+    out_ids[row] = (int64_t)besti;
+    counters[row] = 0u;
+  }
+}
+
 __global__ void advance_cursors_kernel(int* cache_pos, const int* delta, int batch, int q_len) {
   grid_dep_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -111,14 +168,18 @@ int launch_linear(const void* x, int64_t m, int64_t k, const void* norm_w, float
                   unsigned int* counter, int64_t* out_ids, int grid_override);
 int lmhead_grid(int64_t vocab, int64_t m);
 int launch_qk_norm_rope(const void* qkv, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, const void* qn,
-                        const void* kn, const void* cos, const void* sin, int64_t rope_len, const int32_t* cache_pos,
-                        int64_t uniform_past, void* k_cache, void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* q_out,
+                        const void* kn, const void* cos, const void* sin, int64_t rope_len, int64_t rope_offset,
+                        const int32_t* cache_pos, int64_t uniform_past, void* k_cache, void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* q_out,
                         float eps, cudaStream_t stream);
 int attention_workspace_bytes(int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int64_t max_seq,
                               int64_t* bytes);
 int launch_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
                             int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int64_t max_seq, float scale,
                             void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream);
+
+int tc_workspace_bytes(int64_t m, int64_t k, int64_t n_out, int epi, int64_t* bytes);
+int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n_out, int epi, const void* residual,
+                   void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream);
 
 }  // namespace lsb_host
 
@@ -185,7 +246,8 @@ int ls_rmsnorm_qkv_rope_kvappend(const void* x, int64_t batch, int64_t q_len, in
                                  const void* input_norm_w, float eps, const void* qkv_w, int64_t num_heads,
                                  int64_t num_kv_heads, int64_t head_dim, const void* q_norm_w,
                                  const void* k_norm_w, const void* rope_cos, const void* rope_sin,
-                                 int64_t rope_len, const int32_t* cache_pos, int64_t uniform_past, void* k_cache,
+                                 int64_t rope_len, int64_t rope_offset, const int32_t* cache_pos,
+                                 int64_t uniform_past, void* k_cache,
                                  void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* qkv_scratch,
                                  void* q_out, ls_stream_t stream) {
   LS_REQUIRE(x && qkv_w && q_norm_w && k_norm_w && rope_cos && rope_sin && qkv_scratch && q_out,
@@ -195,9 +257,11 @@ int ls_rmsnorm_qkv_rope_kvappend(const void* x, int64_t batch, int64_t q_len, in
   LS_REQUIRE(batch > 0 && q_len > 0 && num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
              LS_ERR_INVALID_ARGUMENT, "ls_rmsnorm_qkv_rope_kvappend: bad head counts / sizes");
   LS_REQUIRE(rope_len > 0, LS_ERR_INVALID_ARGUMENT, "rope_len must be positive");
-  LS_REQUIRE(cache_pos || (uniform_past >= 0 && uniform_past + q_len <= rope_len), LS_ERR_KV_OVERFLOW,
-             "uniform_past=%lld + q_len=%lld beyond rope_len=%lld", (long long)uniform_past, (long long)q_len,
-             (long long)rope_len);
+  LS_REQUIRE(rope_offset >= 0, LS_ERR_INVALID_ARGUMENT, "rope_offset must be non-negative");
+  LS_REQUIRE(cache_pos || (uniform_past >= rope_offset && uniform_past + q_len <= rope_offset + rope_len),
+             LS_ERR_KV_OVERFLOW, "positions %lld..%lld outside the rope table rows %lld..%lld",
+             (long long)uniform_past, (long long)(uniform_past + q_len - 1), (long long)rope_offset,
+             (long long)(rope_offset + rope_len - 1));
   LS_REQUIRE(cache_pos || !k_cache || uniform_past + q_len <= max_seq, LS_ERR_KV_OVERFLOW,
              "cache overflow: %lld tokens with max_seq=%lld", (long long)(uniform_past + q_len), (long long)max_seq);
   LS_REQUIRE((k_cache == nullptr) == (v_cache == nullptr) && (k_out == nullptr) == (v_out == nullptr),
@@ -210,7 +274,7 @@ int ls_rmsnorm_qkv_rope_kvappend(const void* x, int64_t batch, int64_t q_len, in
                          (cudaStream_t)stream, nullptr, nullptr, nullptr, nullptr, 0);
   if (rc) return rc;
   return launch_qk_norm_rope(qkv_scratch, batch, q_len, num_heads, num_kv_heads, q_norm_w, k_norm_w, rope_cos,
-                             rope_sin, rope_len, cache_pos, uniform_past, k_cache, v_cache, max_seq, k_out, v_out, q_out, eps,
+                             rope_sin, rope_len, rope_offset, cache_pos, uniform_past, k_cache, v_cache, max_seq, k_out, v_out, q_out, eps,
                              (cudaStream_t)stream);
 }
 
@@ -288,6 +352,79 @@ int ls_lmhead_argmax(const void* h, int64_t m, int64_t hidden, const void* final
   int* part_idx = reinterpret_cast<int*>(ws + 256 + region);
   return launch_linear(h, m, hidden, final_norm_w, eps, lm_head_w, vocab, 3, nullptr, nullptr,
                        (cudaStream_t)stream, part_val, part_idx, counter, out_ids, g);
+}
+
+int ls_gemm_bf16_tcgen05_workspace_bytes(int64_t m, int64_t k, int64_t n, int epilogue, int64_t* bytes) {
+  LS_REQUIRE(bytes && m > 0 && m <= 128 && k > 0 && n > 0, LS_ERR_INVALID_ARGUMENT,
+             "ls_gemm_bf16_tcgen05_workspace_bytes: bad arguments");
+  LS_REQUIRE(epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL, LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d",
+             epilogue);
+  return tc_workspace_bytes(m, k, n, epilogue, bytes);
+}
+
+int ls_gemm_bf16_tcgen05(const void* x, int64_t m, int64_t k, const void* w, int64_t n, int epilogue,
+                         const void* residual, void* out, void* workspace, int64_t workspace_bytes,
+                         ls_stream_t stream) {
+  LS_REQUIRE(epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL, LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d",
+             epilogue);
+  return launch_gemm_tc(x, m, k, w, n, epilogue, residual, out, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int ls_qk_norm_rope_kvappend(const void* qkv, int64_t batch, int64_t q_len, int64_t num_heads, int64_t num_kv_heads,
+                             int64_t head_dim, const void* q_norm_w, const void* k_norm_w, float eps,
+                             const void* rope_cos, const void* rope_sin, int64_t rope_len, int64_t rope_offset,
+                             const int32_t* cache_pos, int64_t uniform_past, void* k_cache, void* v_cache,
+                             int64_t max_seq, void* k_out, void* v_out, void* q_out, ls_stream_t stream) {
+  LS_REQUIRE(qkv && q_norm_w && k_norm_w && rope_cos && rope_sin && q_out, LS_ERR_INVALID_ARGUMENT,
+             "ls_qk_norm_rope_kvappend: null pointer");
+  LS_REQUIRE(head_dim == 128, LS_ERR_UNSUPPORTED_SHAPE, "head_dim=%lld (only 128 is implemented)",
+             (long long)head_dim);
+  LS_REQUIRE(batch > 0 && q_len > 0 && num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0 &&
+                 batch * q_len <= 65535,
+             LS_ERR_INVALID_ARGUMENT, "ls_qk_norm_rope_kvappend: bad sizes");
+  LS_REQUIRE((k_cache == nullptr) == (v_cache == nullptr) && (k_out == nullptr) == (v_out == nullptr),
+             LS_ERR_INVALID_ARGUMENT, "k/v cache and k/v out come in pairs");
+  LS_REQUIRE(rope_len > 0 && rope_offset >= 0, LS_ERR_INVALID_ARGUMENT, "bad rope table");
+  LS_REQUIRE(cache_pos || (uniform_past >= rope_offset && uniform_past + q_len <= rope_offset + rope_len),
+             LS_ERR_KV_OVERFLOW, "positions outside the rope table");
+  LS_REQUIRE(cache_pos || !k_cache || uniform_past + q_len <= max_seq, LS_ERR_KV_OVERFLOW, "cache overflow");
+  return launch_qk_norm_rope(qkv, batch, q_len, num_heads, num_kv_heads, q_norm_w, k_norm_w, rope_cos, rope_sin,
+                             rope_len, rope_offset, cache_pos, uniform_past, k_cache, v_cache, max_seq, k_out, v_out,
+                             q_out, eps, (cudaStream_t)stream);
+}
+
+static int argmax_chunks(int64_t m, int64_t n) {
+  int64_t c = (2 * (int64_t)sm_count() + m - 1) / m;
+  const int64_t by_len = (n + 2047) / 2048;
+  if (c > by_len) c = by_len;
+  if (c < 1) c = 1;
+  return (int)c;
+}
+
+int ls_argmax_rows_workspace_bytes(int64_t m, int64_t n, int64_t* bytes) {
+  LS_REQUIRE(bytes && m > 0 && n > 0, LS_ERR_INVALID_ARGUMENT, "ls_argmax_rows_workspace_bytes: bad arguments");
+  const int64_t c = argmax_chunks(m, n);
+  *bytes = ((m * 4 + 255) / 256) * 256 + 2 * ((m * c * 4 + 255) / 256) * 256;
+  return LS_OK;
+}
+
+int ls_argmax_rows(const void* logits, int64_t m, int64_t n, int64_t* out_ids, void* workspace,
+                   int64_t workspace_bytes, ls_stream_t stream) {
+  LS_REQUIRE(logits && out_ids && workspace, LS_ERR_INVALID_ARGUMENT, "ls_argmax_rows: null pointer");
+  LS_REQUIRE(m > 0 && m <= 65535 && n > 0 && n < (1ll << 31), LS_ERR_INVALID_ARGUMENT, "ls_argmax_rows: bad sizes");
+  int64_t need = 0;
+  int rc = ls_argmax_rows_workspace_bytes(m, n, &need);
+  if (rc) return rc;
+  LS_REQUIRE(workspace_bytes >= need, LS_ERR_WORKSPACE, "ls_argmax_rows: workspace needs %lld bytes",
+             (long long)need);
+  const int c = argmax_chunks(m, n);
+  char* ws = static_cast<char*>(workspace);
+  const int64_t cnt_bytes = ((m * 4 + 255) / 256) * 256, region = ((m * c * 4 + 255) / 256) * 256;
+  lsb::argmax_rows_kernel<<<dim3((unsigned)c, (unsigned)m), lsb::kArgmaxThreads, 0, (cudaStream_t)stream>>>(
+      static_cast<const __nv_bfloat16*>(logits), (int)n, c, reinterpret_cast<float*>(ws + cnt_bytes),
+      reinterpret_cast<int*>(ws + cnt_bytes + region), reinterpret_cast<unsigned int*>(ws), out_ids);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "argmax_rows launch: %s", cudaGetErrorString(e));
 }
 
 int ls_rmsnorm(const void* x, int64_t m, int64_t n, const void* w, float eps, void* out, ls_stream_t stream) {

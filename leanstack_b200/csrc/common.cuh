@@ -67,6 +67,13 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
 
 __device__ __forceinline__ uint4 ldg16(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
+// Bulk prefetch of [p, p + bytes) into L2 (p and bytes multiples of 16).  Used
+// by a kernel launched early under PDL to pull its first weight bytes in while
+// the previous kernel finishes: weights never depend on the previous kernel.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Programmatic dependent launch.  A kernel launched with the PDL attribute may
 // start before its predecessor finishes; it must call grid_dep_wait() before
@@ -83,6 +90,62 @@ __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol
 __device__ __forceinline__ void raise_device_error(int* flag, int code) {
   if (flag) atomicCAS(flag, 0, code);
 }
+
+// ---------------------------------------------------------------------------
+// mbarrier + bulk-copy (TMA, non-tensor) helpers.  Every wait is bounded: it
+// gives up after kWaitCycles (about two seconds at the boost clock), records
+// LS_ERR_TIMEOUT and reports failure so the kernel can drain and return.
+// ---------------------------------------------------------------------------
+constexpr long long kWaitCycles = 4000000000LL;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with the given parity to complete.  On timeout
+// the error code is LS_ERR_TIMEOUT in the low byte and the wait site above it.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int site = 0) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      raise_device_error(err, 7 /* LS_ERR_TIMEOUT */ | (site << 8));
+      return false;
+    }
+  }
+  return true;
+}
+// Contiguous global -> shared bulk copy completing on `bar` (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+
 
 }  // namespace lsb
 

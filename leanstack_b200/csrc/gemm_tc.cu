@@ -1,0 +1,547 @@
+// Weight-streaming GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Y[b, n] = sum_k X[b, k] * W[n, k] for the decode / verify shapes: few
+// activation rows (b < 256) against large weight matrices that are read once.
+// The product is computed transposed ("swap AB"): the weight tile is the MMA's
+// A operand (128 rows = MMA M), the activations are the B operand (MMA N = the
+// batch rounded up to 16), and the fp32 accumulator D[n, b] lives in TMEM with
+// one TMEM lane per weight row.
+//
+// Work split ("stream-K"): the (128-row tile, 64-wide k-block) units of the
+// whole matrix are divided evenly over one CTA per SM, so every SM streams the
+// same number of weight bytes whatever the shape.  A tile whose k-blocks are
+// split between CTAs is finished by its last contributor, which sums the fp32
+// partials of all contributors in CTA order (deterministic).
+//
+// Warp roles (6 warps): warp 4 issues TMA loads of weight and activation
+// k-blocks into a shared-memory ring (128-byte swizzle, the canonical K-major
+// UMMA layout); warp 5 issues tcgen05.mma (one elected thread) and commits
+// stage releases and accumulator completion to mbarriers; warps 0-3 drain TMEM
+// with tcgen05.ld and run the epilogue.  Under programmatic dependent launch
+// the producer loads the first weight stages before waiting on the previous
+// kernel (weights never depend on it; activations do).
+//
+// Epilogues follow the reference's bf16 rounding points
+// (src/leanstack/runtime/qwen_explicit.py:809-852, :913, :932-949): STORE
+// rounds the fp32 sum once; RESIDUAL adds the rounded product to the residual
+// and rounds again; SILU_MUL pairs gate tile t with up tile t (two TMEM
+// accumulators) and rounds after the projection, after SiLU and after the
+// product.  Every mbarrier wait is bounded (LS_ERR_TIMEOUT).
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace lsb {
+
+constexpr int kTcTileN = 128;   // weight rows per tile (MMA M)
+constexpr int kTcBlockK = 64;   // K per stage: one 128-byte swizzle atom of bf16
+constexpr int kTcThreads = 192;
+constexpr int kTcEpiThreads = 128;
+constexpr int kTcMaxStages = 8;
+// Tile counters sit in a fixed-size region at the start of the workspace, so
+// one workspace can serve GEMMs of different shapes: partials of one call never
+// land on another call's counters.
+constexpr int kTcMaxTiles = 2048;
+constexpr size_t kTcCounterBytes = (size_t)2 * kTcMaxTiles * sizeof(unsigned int);
+
+enum { TEPI_STORE = 0, TEPI_RESIDUAL = 1, TEPI_SILU_MUL = 2 };
+
+struct TcParams {
+  const __nv_bfloat16* residual;  // [B, N]
+  __nv_bfloat16* out;             // [B, N]
+  float* partial;                 // [grid][2 slots][accs][BN][128]
+  unsigned int* counters;         // [2][tiles]: arrivals, departures; zero between calls
+  int* err;
+  int B;          // activation rows
+  int BN;         // MMA N (B rounded up to 16)
+  int N;          // output columns
+  int tiles;      // ceil(N / 128)
+  int kblocks;    // ceil(K / 64)
+  int stages;
+  int stage_bytes;
+  int acc_buffers;  // 2: the MMA fills one TMEM accumulator while the epilogue drains the other
+  uint32_t tmem_cols;
+};
+
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  // K-major, 128-byte swizzle: 8-row groups 1024 B apart (SBO), LBO unused,
+  // descriptor version 1, layout type 2 (SWIZZLE_128B).
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// First unit of CTA c and the CTA that owns unit u (units split evenly).
+__device__ __forceinline__ long long tc_unit_begin(long long U, int G, int c) { return U * c / G; }
+__device__ __forceinline__ int tc_unit_owner(long long U, int G, long long u) {
+  return (int)(((u + 1) * G + U - 1) / U - 1);
+}
+
+// Spin (bounded) until a global counter reaches `target`.
+__device__ __forceinline__ bool wait_counter(const unsigned int* ctr, unsigned int target, int* err, int site) {
+  const long long t0 = clock64();
+  while (true) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) return true;
+    if (clock64() - t0 > kWaitCycles) {
+      raise_device_error(err, 7 /* LS_ERR_TIMEOUT */ | (site << 8));
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ float tc_apply(const TcParams& p, size_t o, float y, float y2) {
+  if (EPI == TEPI_STORE) return y;
+  if (EPI == TEPI_RESIDUAL) return bf16_to_f(p.residual[o]) + round_bf16(y);
+  const float g = round_bf16(y);
+  return round_bf16(g / (1.0f + expf(-g))) * round_bf16(y2);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
+                   const __grid_constant__ CUtensorMap tm_x, TcParams p) {
+  constexpr bool SILU = (EPI == TEPI_SILU_MUL);
+  constexpr int ACCS = SILU ? 2 : 1;
+  constexpr uint32_t kWBytes = kTcTileN * kTcBlockK * 2;  // 16 KB per weight tile
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<size_t>(smem_raw) + 1023) & ~size_t(1023));
+  const int NS = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)NS * p.stage_bytes);
+  uint64_t* empty = full + NS;
+  uint64_t* acc_full = empty + NS;   // [2]
+  uint64_t* acc_empty = acc_full + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  __shared__ int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x, cta = blockIdx.x;
+  const int KB = p.kblocks;
+  const long long U = (long long)p.tiles * KB;
+  const long long ub = tc_unit_begin(U, G, cta), ue = tc_unit_begin(U, G, cta + 1);
+  const uint32_t x_bytes = (uint32_t)p.BN * kTcBlockK * 2;
+  const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.BN >> 3) << 17) |
+                         ((uint32_t)(kTcTileN >> 4) << 24);
+  const int nbuf = p.acc_buffers;
+  const uint32_t acc_cols = (uint32_t)(p.BN * ACCS);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], kTcEpiThreads);
+    }
+    s_abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(p.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  grid_dep_launch();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      const long long n_units = ue - ub;
+      const long long pre = n_units < NS ? n_units : NS;
+      // Weights first (independent of the previous kernel), then activations.
+      for (long long i = 0; i < pre; ++i) {
+        const long long u = ub + i;
+        const int t = (int)(u / KB), kb = (int)(u % KB);
+        unsigned char* st = smem + (size_t)i * p.stage_bytes;
+        mbar_arrive_expect_tx(&full[i], kWBytes * ACCS + x_bytes);
+        tma_load_2d(st, &tm_w, kb * kTcBlockK, t * kTcTileN, &full[i]);
+        if (SILU) tma_load_2d(st + kWBytes, &tm_w2, kb * kTcBlockK, t * kTcTileN, &full[i]);
+      }
+      grid_dep_wait();
+      for (long long i = 0; i < pre; ++i) {
+        const long long u = ub + i;
+        const int kb = (int)(u % KB);
+        tma_load_2d(smem + (size_t)i * p.stage_bytes + kWBytes * ACCS, &tm_x, kb * kTcBlockK, 0, &full[i]);
+      }
+      for (long long i = pre; i < n_units; ++i) {
+        const int s = (int)(i % NS);
+        if (!mbar_wait(&empty[s], (uint32_t)((i / NS) - 1) & 1u, p.err, 1)) {
+          s_abort = 1;
+          break;
+        }
+        const long long u = ub + i;
+        const int t = (int)(u / KB), kb = (int)(u % KB);
+        unsigned char* st = smem + (size_t)s * p.stage_bytes;
+        mbar_arrive_expect_tx(&full[s], kWBytes * ACCS + x_bytes);
+        tma_load_2d(st, &tm_w, kb * kTcBlockK, t * kTcTileN, &full[s]);
+        if (SILU) tma_load_2d(st + kWBytes, &tm_w2, kb * kTcBlockK, t * kTcTileN, &full[s]);
+        tma_load_2d(st + kWBytes * ACCS, &tm_x, kb * kTcBlockK, 0, &full[s]);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      long long i = 0;
+      int seg = 0;
+      long long u = ub;
+      while (u < ue && !*(volatile int*)&s_abort) {
+        const long long tile_end = (u / KB + 1) * KB;
+        const long long seg_end = ue < tile_end ? ue : tile_end;
+        const int a = seg % nbuf;
+        if (seg >= nbuf && !mbar_wait(&acc_empty[a], (uint32_t)((seg / nbuf) - 1) & 1u, p.err, 2)) {
+          s_abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc_tmem = tmem + (uint32_t)a * acc_cols;
+        for (long long v = u; v < seg_end; ++v, ++i) {
+          const int s = (int)(i % NS);
+          if (!mbar_wait(&full[s], (uint32_t)(i / NS) & 1u, p.err, 3)) {
+            s_abort = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sw = smem_u32(smem + (size_t)s * p.stage_bytes);
+          const uint32_t sx = sw + kWBytes * ACCS;
+#pragma unroll
+          for (int kk = 0; kk < kTcBlockK / 16; ++kk) {
+            const uint32_t acc = (v != u || kk > 0) ? 1u : 0u;
+            const uint64_t bdesc = umma_desc_sw128(sx + kk * 32);
+            umma_f16(acc_tmem, umma_desc_sw128(sw + kk * 32), bdesc, idesc, acc);
+            if (SILU)
+              umma_f16(acc_tmem + (uint32_t)p.BN, umma_desc_sw128(sw + kWBytes + kk * 32), bdesc, idesc, acc);
+          }
+          umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        }
+        umma_commit(&acc_full[a]);  // accumulator buffer a holds this segment
+        ++seg;
+        u = seg_end;
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 0-3: TMEM lanes 0-127) ----------------
+    grid_dep_wait();
+    const int row = warp * 32 + lane;  // weight row within the tile = TMEM lane
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    int seg = 0;
+    long long u = ub;
+    while (u < ue) {
+      const int t = (int)(u / KB);
+      const long long tile_begin = (long long)t * KB, tile_end = tile_begin + KB;
+      const long long seg_end = ue < tile_end ? ue : tile_end;
+      const bool whole = (u == tile_begin && seg_end == tile_end);
+      const int a = seg % nbuf;
+      if (!mbar_wait(&acc_full[a], (uint32_t)(seg / nbuf) & 1u, p.err, 4)) s_abort = 1;
+      named_bar_sync(1, kTcEpiThreads);
+      if (*(volatile int*)&s_abort) break;
+      tc_fence_after();
+      const uint32_t acc_addr = tmem + lane_off + (uint32_t)a * acc_cols;
+      const int n = t * kTcTileN + row;
+      const int slot = (t == (int)(ub / KB)) ? 0 : 1;
+      float* mypart = p.partial + (((size_t)cta * 2 + slot) * ACCS * p.BN) * kTcTileN;
+      for (int cb = 0; cb < p.BN; cb += 16) {
+        float v[16], w2[16];
+        tmem_ld16(acc_addr + (uint32_t)cb, v);
+        if (SILU) tmem_ld16(acc_addr + (uint32_t)(p.BN + cb), w2);
+        if (whole) {
+          if (n < p.N) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int b = cb + j;
+              if (b < p.B) {
+                const size_t o = (size_t)b * p.N + n;
+                p.out[o] = f_to_bf16(tc_apply<EPI>(p, o, v[j], SILU ? w2[j] : 0.f));
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            mypart[(size_t)(cb + j) * kTcTileN + row] = v[j];
+            if (SILU) mypart[((size_t)p.BN + cb + j) * kTcTileN + row] = w2[j];
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[a]);  // the MMA warp may reuse this accumulator buffer
+      if (!whole) {
+        // Publish this contributor's partial; the reduction waits until the
+        // whole mainloop is done (below), so no CTA ever waits mid-stream.
+        __threadfence();
+        named_bar_sync(1, kTcEpiThreads);
+        if (threadIdx.x == 0) atomicAdd(p.counters + t, 1u);
+      }
+      ++seg;
+      u = seg_end;
+    }
+
+    // ---- deferred stream-K reduction of this CTA's partial tiles ----
+    if (!*(volatile int*)&s_abort) {
+      const int t_first = (int)(ub / KB), t_last = (int)((ue - 1) / KB);
+      for (int which = 0; which < 2; ++which) {
+        const int t = which == 0 ? t_first : t_last;
+        if (which == 1 && t_last == t_first) break;
+        const long long tile_begin = (long long)t * KB, tile_end = tile_begin + KB;
+        const int c_lo = tc_unit_owner(U, G, tile_begin), c_hi = tc_unit_owner(U, G, tile_end - 1);
+        const int nc = c_hi - c_lo + 1;
+        if (nc == 1) continue;  // a whole tile: already written
+        if (threadIdx.x == 0 && !wait_counter(p.counters + t, (unsigned int)nc, p.err, 5 + which)) s_abort = 1;
+        named_bar_sync(1, kTcEpiThreads);
+        if (*(volatile int*)&s_abort) break;
+        __threadfence();
+        const int j = cta - c_lo;
+        const int b0 = (int)(((long long)p.B * j) / nc), b1 = (int)(((long long)p.B * (j + 1)) / nc);
+        const int n = t * kTcTileN + row;
+        if (n < p.N) {
+          // Columns in batches of 8 with all their partial loads issued before
+          // any is consumed (the loop is otherwise one L2 round trip per column).
+          for (int bb = b0; bb < b1; bb += 8) {
+            float y[8], y2[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) y[q] = y2[q] = 0.f;
+            for (int c = c_lo; c <= c_hi; ++c) {
+              const int sl = (t == (int)(tc_unit_begin(U, G, c) / KB)) ? 0 : 1;
+              const float* part = p.partial + (((size_t)c * 2 + sl) * ACCS * p.BN) * kTcTileN + row;
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                if (bb + q < b1) {
+                  y[q] += __ldcg(part + (size_t)(bb + q) * kTcTileN);
+                  if (SILU) y2[q] += __ldcg(part + ((size_t)p.BN + bb + q) * kTcTileN);
+                }
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              if (bb + q < b1) {
+                const size_t o = (size_t)(bb + q) * p.N + n;
+                p.out[o] = f_to_bf16(tc_apply<EPI>(p, o, y[q], y2[q]));
+              }
+            }
+          }
+        }
+        // The last contributor to finish reducing resets the tile's counters.
+        named_bar_sync(1, kTcEpiThreads);
+        if (threadIdx.x == 0) {
+          const unsigned int prev = atomicAdd(p.counters + p.tiles + t, 1u);
+          if (prev == (unsigned int)nc - 1) {
+            p.counters[t] = 0u;
+            p.counters[p.tiles + t] = 0u;
+          }
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols) : "memory");
+  }
+}
+
+}  // namespace lsb
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+namespace lsb_host {
+using namespace lsb;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix, box [box_rows, 64], 128-byte swizzle.
+static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(LS_ERR_NOT_SUPPORTED, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kTcBlockK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(LS_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return LS_OK;
+}
+
+struct TcPlan {
+  int grid, BN, tiles, kblocks, stages, stage_bytes, accs, acc_buffers;
+  uint32_t tmem_cols;
+  size_t smem, counter_bytes, partial_bytes;
+};
+
+static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
+  TcPlan pl = {};
+  pl.accs = (epi == TEPI_SILU_MUL) ? 2 : 1;
+  pl.BN = (int)((m + 15) / 16 * 16);
+  pl.tiles = (int)((n_out + kTcTileN - 1) / kTcTileN);
+  pl.kblocks = (int)((k + kTcBlockK - 1) / kTcBlockK);
+  const int64_t units = (int64_t)pl.tiles * pl.kblocks;
+  const int sms = sm_count();
+  pl.grid = (int)(units < sms ? units : sms);
+  pl.stage_bytes = (int)(((size_t)kTcTileN * kTcBlockK * 2 * pl.accs + (size_t)pl.BN * kTcBlockK * 2 + 1023) / 1024 *
+                         1024);
+  // ~112 KB of stages: deep enough to cover HBM latency, small enough that the
+  // next kernel's CTA fits beside this one on the SM (PDL overlap).
+  int stages = (int)((112 * 1024) / pl.stage_bytes);
+  if (stages > kTcMaxStages) stages = kTcMaxStages;
+  if (stages < 3) stages = 3;
+  pl.stages = stages;
+  // Two accumulator buffers while they fit in 256 TMEM columns (half the SM's
+  // TMEM, so a co-resident CTA of the next kernel can always allocate).
+  pl.acc_buffers = (2 * pl.BN * pl.accs <= 256) ? 2 : 1;
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(pl.acc_buffers * pl.BN * pl.accs)) cols <<= 1;
+  pl.tmem_cols = cols;
+  pl.smem = 1024 + (size_t)pl.stages * pl.stage_bytes + (size_t)(2 * pl.stages + 4) * 8 + 16;
+  pl.counter_bytes = kTcCounterBytes;
+  pl.partial_bytes = (size_t)pl.grid * 2 * pl.accs * pl.BN * kTcTileN * 4;
+  return pl;
+}
+
+int tc_workspace_bytes(int64_t m, int64_t k, int64_t n_out, int epi, int64_t* bytes) {
+  TcPlan pl = tc_plan(m, k, n_out, epi);
+  *bytes = (int64_t)(pl.counter_bytes + pl.partial_bytes);
+  return LS_OK;
+}
+
+template <int EPI>
+static int launch_tc_t(const CUtensorMap& w, const CUtensorMap& w2, const CUtensorMap& x, const TcParams& p,
+                       const TcPlan& pl, cudaStream_t stream) {
+  auto kern = gemm_tc_kernel<EPI>;
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && (int)pl.smem > configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+    if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "cudaFuncSetAttribute(gemm_tc): %s", cudaGetErrorString(e));
+    configured[dev] = (int)pl.smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, w, w2, x, p);
+  if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "gemm_tc launch: %s", cudaGetErrorString(e));
+  return LS_OK;
+}
+
+// out[m, n_out] = epilogue(x[m, k] . w^T); for SILU_MUL w is [2 n_out, k] (gate rows, then up rows).
+int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n_out, int epi, const void* residual,
+                   void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
+  if (!x || !w || !out) return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_tc: null pointer");
+  // m <= 128 keeps every CTA at <= 256 TMEM columns, so any two CTAs that
+  // share an SM can both allocate (a blocked allocation would stall the
+  // stream-K reduction of the CTA holding the columns).
+  if (m < 1 || m > 128) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "gemm_tc: m=%lld outside 1..128", (long long)m);
+  if (k < 8 || k % 8 || n_out < 1) return set_error(LS_ERR_MISALIGNED, "gemm_tc: k=%lld must be a positive multiple of 8",
+                                                    (long long)k);
+  if (!aligned16(x) || !aligned16(w)) return set_error(LS_ERR_MISALIGNED, "gemm_tc: x and w must be 16-byte aligned");
+  if (epi == TEPI_RESIDUAL && !residual) return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_tc: residual is null");
+  TcPlan pl = tc_plan(m, k, n_out, epi);
+  if (pl.tmem_cols > 256) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "gemm_tc: m=%lld too wide for TMEM", (long long)m);
+  if (pl.tiles > kTcMaxTiles)
+    return set_error(LS_ERR_UNSUPPORTED_SHAPE, "gemm_tc: n=%lld has more than %d row tiles", (long long)n_out,
+                     kTcMaxTiles);
+  if (!workspace || workspace_bytes < (int64_t)(pl.counter_bytes + pl.partial_bytes))
+    return set_error(LS_ERR_WORKSPACE, "gemm_tc: workspace needs %zu bytes", pl.counter_bytes + pl.partial_bytes);
+  if (epi == TEPI_SILU_MUL && ((n_out * k * 2) % 16))
+    return set_error(LS_ERR_MISALIGNED, "gemm_tc: up-projection view misaligned");
+  CUtensorMap mw, mw2, mx;
+  int rc = make_map(&mw, w, n_out, k, kTcTileN);
+  if (rc) return rc;
+  if (epi == TEPI_SILU_MUL) {
+    rc = make_map(&mw2, static_cast<const __nv_bfloat16*>(w) + n_out * k, n_out, k, kTcTileN);
+    if (rc) return rc;
+  } else {
+    mw2 = mw;
+  }
+  rc = make_map(&mx, x, m, k, pl.BN);
+  if (rc) return rc;
+  TcParams p = {};
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.counters = static_cast<unsigned int*>(workspace);
+  p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.counter_bytes);
+  p.err = device_error_ptr();
+  p.B = (int)m;
+  p.BN = pl.BN;
+  p.N = (int)n_out;
+  p.tiles = pl.tiles;
+  p.kblocks = pl.kblocks;
+  p.stages = pl.stages;
+  p.stage_bytes = pl.stage_bytes;
+  p.acc_buffers = pl.acc_buffers;
+  p.tmem_cols = pl.tmem_cols;
+  switch (epi) {
+    case TEPI_STORE: return launch_tc_t<TEPI_STORE>(mw, mw2, mx, p, pl, stream);
+    case TEPI_RESIDUAL: return launch_tc_t<TEPI_RESIDUAL>(mw, mw2, mx, p, pl, stream);
+    case TEPI_SILU_MUL: return launch_tc_t<TEPI_SILU_MUL>(mw, mw2, mx, p, pl, stream);
+    default: return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_tc: unknown epilogue %d", epi);
+  }
+}
+
+}  // namespace lsb_host

@@ -18,6 +18,8 @@
 // linear accumulate in fp32 and round once; the residual add, SiLU and the
 // gate*up product each round to bf16 (:809-852, :932-949).  The argmax
 // epilogue reproduces torch.argmax over bf16 logits (lowest index on ties).
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace lsb {
@@ -25,6 +27,7 @@ namespace lsb {
 constexpr int kLinThreads = 512;
 constexpr int kLinWarps = kLinThreads / 32;
 constexpr int kGranule = 256;  // bf16 elements per warp-wide 512-byte load
+constexpr uint32_t kPrefetchBytes = 64 * 1024;  // per CTA and weight range, issued before the PDL wait
 
 enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3 };
 
@@ -76,7 +79,20 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
   const int R = P * RPU;            // weight rows owned by this CTA
   const int ms = p.max_segs;
 
-  // Activations come from the previous kernel: wait for it (PDL) first.
+  // Weights do not depend on the previous kernel: start pulling this CTA's
+  // first weight bytes into L2, let the next kernel launch, and only then wait
+  // (PDL) for the activations the previous kernel writes.
+  if (tid == 0 && P > 0) {
+    const size_t range = (size_t)P * K * 2;
+    const uint32_t pf = (uint32_t)(range < kPrefetchBytes ? range : kPrefetchBytes);
+    const char* base = reinterpret_cast<const char*>(p.w + (size_t)u0 * K);
+    for (uint32_t off = 0; off < pf; off += 16384) prefetch_l2(base + off, min(16384u, pf - off));
+    if (RPU == 2) {
+      const char* up = reinterpret_cast<const char*>(p.w + ((size_t)u0 + p.N / 2) * K);
+      for (uint32_t off = 0; off < pf; off += 16384) prefetch_l2(up + off, min(16384u, pf - off));
+    }
+  }
+  grid_dep_launch();
   grid_dep_wait();
 
   // ---- prologue: (optional) RMSNorm of the M activation rows into smem ----
@@ -286,6 +302,10 @@ namespace lsb_host {
 
 using namespace lsb;
 
+// Two 512-thread CTAs per SM: 32 warps with 8 loads of 512 B in flight each
+// keep ~128 KB per SM in flight, what the measured 6 TB/s needs (one CTA per
+// SM reached only 4.5 TB/s on the lm_head).  m > 4 needs more registers and
+// runs one CTA per SM.
 static int linear_grid(int units, int m) {
   const int g = (m <= 4 ? 2 : 1) * sm_count();
   return units < g ? units : g;
@@ -346,6 +366,20 @@ static int dispatch_m(int M, LinearParams p, int grid, size_t smem, cudaStream_t
   }
 }
 
+bool stream_supported(int64_t m, int64_t k, int64_t n, int epi);
+int launch_linear_stream(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w, int64_t n,
+                         int epi, const void* residual, void* out, cudaStream_t stream, float* part_val,
+                         int* part_idx, unsigned int* counter, int64_t* out_ids);
+
+static bool stream_path_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("LEANB200_LINEAR");
+    v = (e && e[0] == 's') ? 1 : 0;  // "stream" selects the bulk-TMA variant; the default streams through registers
+  }
+  return v == 1;
+}
+
 int launch_linear(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w, int64_t n,
                   int epi, const void* residual, void* out, cudaStream_t stream, float* part_val, int* part_idx,
                   unsigned int* counter, int64_t* out_ids, int grid_override) {
@@ -358,6 +392,9 @@ int launch_linear(const void* x, int64_t m, int64_t k, const void* norm_w, float
     return set_error(LS_ERR_MISALIGNED, "linear: x/w/norm_w must be 16-byte aligned");
   if (epi == EPI_RESIDUAL && !residual) return set_error(LS_ERR_INVALID_ARGUMENT, "linear: residual is null");
   if (epi == EPI_SILU_MUL && (n % 2)) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "linear: gate_up rows odd");
+  if (stream_path_enabled() && stream_supported(m, k, n, epi))
+    return launch_linear_stream(x, m, k, norm_w, eps, w, n, epi, residual, out, stream, part_val, part_idx, counter,
+                                out_ids);
   LinearParams p = {};
   p.x = static_cast<const __nv_bfloat16*>(x);
   p.norm_w = static_cast<const __nv_bfloat16*>(norm_w);

@@ -21,21 +21,36 @@ from . import kernels as K
 from .leanserve import allocate_arenas, build_resident_buffer_plan, runtime_weight_bytes
 from .qwen_explicit import QwenSemanticStackRuntime, build_qwen_position_cache
 
-SMALL_M = 8
+SMALL_M = 8      # largest token count of the CUDA-core linear kernels
+TC_MAX_M = 128   # largest token count of one tcgen05 GEMM launch
+BACKENDS = ("auto", "tc", "cuda_core")
+
+
+def resolve_backend(backend: str, batch_size: int) -> str:
+    """``auto``: tensor cores from 3 sequences on, CUDA-core streaming below."""
+    if backend not in BACKENDS:
+        raise ValueError(f"unknown linear backend {backend!r}; choose from {BACKENDS}")
+    if backend == "auto":
+        return "tc" if batch_size >= 3 else "cuda_core"
+    return backend
 
 
 class DecodeEngine:
     def __init__(self, runtime: QwenSemanticStackRuntime, batch_size: int, max_seq_len: int,
-                 max_tokens_per_step: int = SMALL_M, use_graph: bool = True):
+                 max_tokens_per_step: int | None = None, use_graph: bool = True, linear_backend: str = "auto"):
         if runtime.final_norm_weight is None or runtime.lm_head_weight is None:
             raise ValueError("the engine needs the output head (include_output_head=True)")
-        if batch_size < 1 or batch_size > SMALL_M:
-            raise ValueError(f"batch_size {batch_size}: the CUDA-core step handles 1..{SMALL_M} sequences")
+        self.backend = resolve_backend(linear_backend, batch_size)
+        limit = TC_MAX_M if self.backend == "tc" else SMALL_M
+        if batch_size < 1 or batch_size > limit:
+            raise ValueError(f"batch_size {batch_size}: the {self.backend} step handles 1..{limit} sequences")
+        if max_tokens_per_step is None:
+            max_tokens_per_step = limit
         self.rt = runtime
         self.g = g = runtime.config
         self.B = batch_size
         self.max_seq = max_seq_len
-        self.T = max(max_tokens_per_step, batch_size)
+        self.T = min(limit, max(max_tokens_per_step, batch_size)) // batch_size * batch_size
         self.plan = build_resident_buffer_plan(g, weights_bytes=runtime_weight_bytes(runtime), batch_size=batch_size,
                                                max_seq_len=max_seq_len, max_tokens_per_step=self.T)
         self.arenas = allocate_arenas(self.plan, g, runtime.device, runtime.dtype)
@@ -47,7 +62,19 @@ class DecodeEngine:
         ws = max(K.attention_workspace_bytes(batch_size, q, g.num_attention_heads, g.num_key_value_heads, g.head_dim,
                                              self.S) for q in range(1, self.T // batch_size + 1))
         self.attn_ws = torch.zeros(max(ws, 256), device=dev, dtype=torch.uint8)
-        self.lm_ws = torch.zeros(K.lmhead_workspace_bytes(batch_size, g.vocab_size), device=dev, dtype=torch.uint8)
+        if self.backend == "tc":
+            T = self.T
+            shapes = [(T, g.hidden_size, g.qkv_dim, K.EPI_STORE), (T, g.q_dim, g.hidden_size, K.EPI_RESIDUAL),
+                      (T, g.hidden_size, g.intermediate_size, K.EPI_SILU_MUL),
+                      (T, g.intermediate_size, g.hidden_size, K.EPI_RESIDUAL),
+                      (batch_size, g.hidden_size, g.vocab_size, K.EPI_STORE)]
+            self.tc_ws = torch.zeros(max(K.gemm_workspace_bytes(*s_) for s_ in shapes), device=dev, dtype=torch.uint8)
+            self.xn = torch.zeros(T, g.hidden_size, device=dev, dtype=runtime.dtype)
+            self.logits = torch.zeros(batch_size, g.vocab_size, device=dev, dtype=runtime.dtype)
+            self.lm_ws = torch.zeros(K.argmax_workspace_bytes(batch_size, g.vocab_size), device=dev, dtype=torch.uint8)
+        else:
+            self.lm_ws = torch.zeros(K.lmhead_workspace_bytes(batch_size, g.vocab_size), device=dev,
+                                     dtype=torch.uint8)
         self.use_graph = use_graph
         self.graph: torch.cuda.CUDAGraph | None = None
 
@@ -58,29 +85,53 @@ class DecodeEngine:
         m = B * q_len
         eps = g.rms_norm_eps
         kv = self.kv
+        tc = self.backend == "tc"
         K.embed_gather(a.ids[:m], rt.embed_tokens_weight, out=a.x[:m])
         for li, layer in enumerate(rt.layers):
             att, mlp = layer.attention, layer.mlp
-            K.qkv_rope_append(a.x[:m], B, q_len, att.qkv_proj_weight, g.num_attention_heads, g.num_key_value_heads,
-                              g.head_dim, att.q_norm_weight, att.k_norm_weight, self.cos, self.sin,
-                              input_norm_w=layer.input_layernorm_weight, eps=eps, cache_pos=kv.cache_pos,
-                              k_cache=kv.key_cache[li], v_cache=kv.value_cache[li], max_seq=self.S,
-                              qkv_scratch=a.qkv[:m], q_out=a.q[:m])
+            if tc:
+                K.rmsnorm(a.x[:m], layer.input_layernorm_weight, eps, out=self.xn[:m])
+                K.gemm_tc(self.xn[:m], att.qkv_proj_weight, out=a.qkv[:m], workspace=self.tc_ws)
+                K.qk_norm_rope(a.qkv[:m], B, q_len, g.num_attention_heads, g.num_key_value_heads, g.head_dim,
+                               att.q_norm_weight, att.k_norm_weight, self.cos, self.sin, eps=eps,
+                               cache_pos=kv.cache_pos, k_cache=kv.key_cache[li], v_cache=kv.value_cache[li],
+                               max_seq=self.S, q_out=a.q[:m])
+            else:
+                K.qkv_rope_append(a.x[:m], B, q_len, att.qkv_proj_weight, g.num_attention_heads,
+                                  g.num_key_value_heads, g.head_dim, att.q_norm_weight, att.k_norm_weight, self.cos,
+                                  self.sin, input_norm_w=layer.input_layernorm_weight, eps=eps,
+                                  cache_pos=kv.cache_pos, k_cache=kv.key_cache[li], v_cache=kv.value_cache[li],
+                                  max_seq=self.S, qkv_scratch=a.qkv[:m], q_out=a.q[:m])
             K.decode_attention(a.q[:m], kv.key_cache[li], kv.value_cache[li], B, q_len, g.num_attention_heads,
                                g.num_key_value_heads, g.head_dim, self.S, att.attention_scale,
                                cache_pos=kv.cache_pos, out=a.attn[:m], workspace=self.attn_ws)
-            K.oproj_residual(a.attn[:m], att.o_proj_weight, a.x[:m], out=a.h[:m])
-            K.gateup_silu(a.h[:m], layer.post_attention_layernorm_weight, mlp.gate_up_proj_weight, eps,
-                          out=a.act[:m])
-            K.down_residual(a.act[:m], mlp.down_proj_weight, a.h[:m], out=a.x[:m])
+            if tc:
+                K.gemm_tc(a.attn[:m], att.o_proj_weight, epilogue=K.EPI_RESIDUAL, residual=a.x[:m], out=a.h[:m],
+                          workspace=self.tc_ws)
+                K.rmsnorm(a.h[:m], layer.post_attention_layernorm_weight, eps, out=self.xn[:m])
+                K.gemm_tc(self.xn[:m], mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=a.act[:m],
+                          workspace=self.tc_ws)
+                K.gemm_tc(a.act[:m], mlp.down_proj_weight, epilogue=K.EPI_RESIDUAL, residual=a.h[:m],
+                          out=a.x[:m], workspace=self.tc_ws)
+            else:
+                K.oproj_residual(a.attn[:m], att.o_proj_weight, a.x[:m], out=a.h[:m])
+                K.gateup_silu(a.h[:m], layer.post_attention_layernorm_weight, mlp.gate_up_proj_weight, eps,
+                              out=a.act[:m])
+                K.down_residual(a.act[:m], mlp.down_proj_weight, a.h[:m], out=a.x[:m])
         if head:
             if q_len == 1:
                 rows = a.x[:B]
             else:
                 a.head_rows.copy_(a.x[:m].view(B, q_len, -1)[:, -1])
                 rows = a.head_rows
-            K.lmhead_argmax(rows, rt.final_norm_weight, rt.lm_head_weight, eps, out_ids=a.ids[:B],
-                            workspace=self.lm_ws)
+            self._head_rows = rows
+            if tc:
+                K.rmsnorm(rows, rt.final_norm_weight, eps, out=self.xn[:B])
+                K.gemm_tc(self.xn[:B], rt.lm_head_weight, out=self.logits, workspace=self.tc_ws)
+                K.argmax_rows(self.logits, out_ids=a.ids[:B], workspace=self.lm_ws)
+            else:
+                K.lmhead_argmax(rows, rt.final_norm_weight, rt.lm_head_weight, eps, out_ids=a.ids[:B],
+                                workspace=self.lm_ws)
         K.advance_cursors(kv.cache_pos, q_len)
 
     # ------------------------------------------------------------------
@@ -142,6 +193,10 @@ class DecodeEngine:
             self._forward(1, head=True)
         self.kv.note_advanced(1)
 
+    def last_head_rows(self) -> torch.Tensor:
+        """The final-layer hidden rows ``[B, H]`` the greedy head consumed in the last step."""
+        return self._head_rows
+
     @property
     def current_ids(self) -> torch.Tensor:
         return self.arenas.ids[:self.B]
@@ -156,5 +211,7 @@ class DecodeEngine:
         return torch.stack(out, dim=1)
 
     def kernel_launches_per_step(self) -> int:
-        """Kernels one decode step launches: embed + per layer (2 QKV + attention + 3 linears) + head + cursor."""
-        return 1 + 6 * len(self.rt.layers) + 1 + 1
+        """Kernels one decode step launches (embedding, layers, head, cursor advance)."""
+        per_layer = 8 if self.backend == "tc" else 6
+        head = 3 if self.backend == "tc" else 1
+        return 1 + per_layer * len(self.rt.layers) + head + 1

@@ -98,6 +98,7 @@ def qkv_rope_append(x: torch.Tensor, batch: int, q_len: int, qkv_w: torch.Tensor
                     num_kv_heads: int, head_dim: int, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor,
                     cos: torch.Tensor, sin: torch.Tensor, *, input_norm_w: torch.Tensor | None = None,
                     eps: float = 1e-6, cache_pos: torch.Tensor | None = None, uniform_past: int = 0,
+                    rope_offset: int = 0,
                     k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None, max_seq: int = 0,
                     k_out: torch.Tensor | None = None, v_out: torch.Tensor | None = None,
                     qkv_scratch: torch.Tensor | None = None, q_out: torch.Tensor | None = None):
@@ -117,10 +118,52 @@ def qkv_rope_append(x: torch.Tensor, batch: int, q_len: int, qkv_w: torch.Tensor
         q_out = torch.empty((m, num_heads, head_dim), device=dev, dtype=BF16)
     nat.call("ls_rmsnorm_qkv_rope_kvappend", x.data_ptr(), batch, q_len, hidden, _ptr(input_norm_w), float(eps),
              qkv_w.data_ptr(), num_heads, num_kv_heads, head_dim, q_norm_w.data_ptr(), k_norm_w.data_ptr(),
-             cos.data_ptr(), sin.data_ptr(), cos.shape[0], _ptr(cache_pos), int(uniform_past), _ptr(k_cache),
+             cos.data_ptr(), sin.data_ptr(), cos.shape[0], int(rope_offset), _ptr(cache_pos), int(uniform_past),
+             _ptr(k_cache),
              _ptr(v_cache), int(max_seq), _ptr(k_out), _ptr(v_out), qkv_scratch.data_ptr(), q_out.data_ptr(),
              _stream())
     return q_out
+
+
+def qk_norm_rope(qkv: torch.Tensor, batch: int, q_len: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                 q_norm_w: torch.Tensor, k_norm_w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, *,
+                 eps: float = 1e-6, cache_pos: torch.Tensor | None = None, uniform_past: int = 0,
+                 rope_offset: int = 0, k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None,
+                 max_seq: int = 0, k_out: torch.Tensor | None = None, v_out: torch.Tensor | None = None,
+                 q_out: torch.Tensor | None = None) -> torch.Tensor:
+    """q/k RMSNorm + RoPE + K/V append on a precomputed fused projection ``qkv [m, (Hq+2Hkv) D]``."""
+    _check(qkv, "qkv")
+    m = batch * q_len
+    if cache_pos is not None:
+        _check(cache_pos, "cache_pos", torch.int32)
+    if q_out is None:
+        q_out = torch.empty((m, num_heads, head_dim), device=qkv.device, dtype=BF16)
+    nat.call("ls_qk_norm_rope_kvappend", qkv.data_ptr(), batch, q_len, num_heads, num_kv_heads, head_dim,
+             q_norm_w.data_ptr(), k_norm_w.data_ptr(), float(eps), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
+             int(rope_offset), _ptr(cache_pos), int(uniform_past), _ptr(k_cache), _ptr(v_cache), int(max_seq),
+             _ptr(k_out), _ptr(v_out), q_out.data_ptr(), _stream())
+    return q_out
+
+
+def argmax_workspace_bytes(m: int, n: int) -> int:
+    v = ctypes.c_int64(0)
+    nat.call("ls_argmax_rows_workspace_bytes", m, n, ctypes.byref(v))
+    return v.value
+
+
+def argmax_rows(logits: torch.Tensor, *, out_ids: torch.Tensor | None = None,
+                workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Row argmax of bf16 logits ``[m, n]``, lowest index on ties -> int64 ``[m]``."""
+    _check(logits, "logits")
+    n = logits.shape[-1]
+    m = logits.numel() // n
+    if out_ids is None:
+        out_ids = torch.empty((m,), device=logits.device, dtype=torch.int64)
+    if workspace is None:
+        workspace = torch.zeros(argmax_workspace_bytes(m, n), device=logits.device, dtype=torch.uint8)
+    nat.call("ls_argmax_rows", logits.data_ptr(), m, n, out_ids.data_ptr(), workspace.data_ptr(), workspace.numel(),
+             _stream())
+    return out_ids
 
 
 def attention_workspace_bytes(batch: int, q_len: int, num_heads: int, num_kv_heads: int, head_dim: int,
@@ -220,6 +263,34 @@ def lmhead_argmax(h: torch.Tensor, final_norm_w: torch.Tensor | None, lm_head_w:
     nat.call("ls_lmhead_argmax", h.data_ptr(), m, hidden, _ptr(final_norm_w), float(eps), lm_head_w.data_ptr(),
              vocab, out_ids.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
     return out_ids
+
+
+def gemm_workspace_bytes(m: int, k: int, n: int, epilogue: int) -> int:
+    v = ctypes.c_int64(0)
+    nat.call("ls_gemm_bf16_tcgen05_workspace_bytes", m, k, n, int(epilogue), ctypes.byref(v))
+    return v.value
+
+
+def gemm_tc(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,
+            out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """tcgen05 weight-streaming GEMM: ``out = epilogue(x @ w.T)`` for x ``[m, k]``, 1 <= m <= 128."""
+    _check(x, "x")
+    _check(w, "w")
+    k = x.shape[-1]
+    m = x.numel() // k
+    n = w.shape[0] // 2 if epilogue == EPI_SILU_MUL else w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"weight in-features {w.shape[1]} != activation width {k}")
+    if residual is not None:
+        _check(residual, "residual")
+    if out is None:
+        out = torch.empty((*x.shape[:-1], n), device=x.device, dtype=BF16)
+    need = gemm_workspace_bytes(m, k, n, epilogue)
+    if workspace is None:
+        workspace = torch.zeros(need, device=x.device, dtype=torch.uint8)
+    nat.call("ls_gemm_bf16_tcgen05", x.data_ptr(), m, k, w.data_ptr(), n, int(epilogue), _ptr(residual),
+             out.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
+    return out
 
 
 def advance_cursors(cache_pos: torch.Tensor, q_len: int, delta: torch.Tensor | None = None) -> None:

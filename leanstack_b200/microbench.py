@@ -1,0 +1,165 @@
+"""Per-kernel timing at the Qwen3-4B decode shapes (CUDA events, cold weights).
+
+``python -m leanstack_b200.microbench [--kernels a,b] [--reps N] [--m 1] [--seq 600]``
+
+Each kernel runs over ``--copies`` distinct weight sets (more bytes than the
+126 MB L2), rotating between them, so every launch streams its weights from
+HBM.  Prints one JSON line per kernel: average launch time, algorithmic bytes
+per launch and GB/s.  This is also the small case used for ncu captures.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import kernels as K
+from . import synth
+from .config import QWEN3_4B
+
+
+def _events():
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def _time(fn, reps: int) -> float:
+    """Average device time of ``fn`` over ``reps`` back-to-back launches captured
+    in one CUDA graph (no host launch overhead between them, as in the decode step)."""
+    fn(0)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(reps):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(stream)
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = _events()
+    a.record()
+    graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / 1000.0 / reps
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernels", default="qkv,attention,oproj,gateup,down,lmhead,qknorm,embed")
+    ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--seq", type=int, default=600, help="cached positions for attention")
+    ap.add_argument("--copies", type=int, default=4)
+    args = ap.parse_args(argv)
+    g = QWEN3_4B
+    dev = torch.device("cuda")
+    m, H, I = args.m, g.hidden_size, g.intermediate_size
+    C = args.copies
+
+    def w(shape, name):
+        return [synth.normal(shape, 0.02, c, name, device=dev) for c in range(C)]
+
+    x = synth.normal((m, H), 1.0, 0, "mb/x", device=dev)
+    nw = synth.norm_weight((H,), 0, "mb/nw", device=dev)
+    out = {}
+    wanted = set(args.kernels.split(","))
+    if "qkv" in wanted or "qknorm" in wanted:
+        qkv_w = w((g.qkv_dim, H), "mb/qkv")
+        qn = synth.norm_weight((g.head_dim,), 0, "mb/qn", device=dev)
+        cos, sin = (torch.randn(4096, 64, device=dev).bfloat16() for _ in range(2))
+        scratch = torch.empty(m, g.qkv_dim, device=dev, dtype=torch.bfloat16)
+        q = torch.empty(m, g.num_attention_heads, g.head_dim, device=dev, dtype=torch.bfloat16)
+        kc = torch.zeros(m, g.num_key_value_heads, 4096, g.head_dim, device=dev, dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        pos = torch.full((m,), 100, device=dev, dtype=torch.int32)
+        if "qkv" in wanted:
+            t = _time(lambda i: K.linear(x, qkv_w[i % C], norm_w=nw, out=scratch), args.reps)
+            out["qkv(norm+gemv)"] = (t, g.qkv_dim * H * 2)
+        if "qknorm" in wanted:
+            from . import _native as nat
+
+            def qk(i):
+                nat.call("ls_rmsnorm_qkv_rope_kvappend", x.data_ptr(), m, 1, H, nw.data_ptr(), 1e-6,
+                         qkv_w[i % C].data_ptr(), g.num_attention_heads, g.num_key_value_heads, g.head_dim,
+                         qn.data_ptr(), qn.data_ptr(), cos.data_ptr(), sin.data_ptr(), 4096, 0, pos.data_ptr(), 0,
+                         kc.data_ptr(), vc.data_ptr(), 4096, None, None, scratch.data_ptr(), q.data_ptr(),
+                         torch.cuda.current_stream().cuda_stream)
+            t = _time(qk, args.reps)
+            out["qkv+qknorm_rope_append (2 kernels)"] = (t, g.qkv_dim * H * 2)
+    if "attention" in wanted:
+        S = 4096
+        kcs = [synth.normal((m, g.num_key_value_heads, S, g.head_dim), 1.0, c, "mb/k", device=dev) for c in range(2)]
+        vcs = [synth.normal((m, g.num_key_value_heads, S, g.head_dim), 1.0, c, "mb/v", device=dev) for c in range(2)]
+        q = synth.normal((m, g.num_attention_heads, g.head_dim), 1.0, 0, "mb/q", device=dev)
+        pos = torch.full((m,), args.seq - 1, device=dev, dtype=torch.int32)
+        ws = torch.zeros(K.attention_workspace_bytes(m, 1, 32, 8, 128, S), device=dev, dtype=torch.uint8)
+        o = torch.empty(m, g.q_dim, device=dev, dtype=torch.bfloat16)
+        t = _time(lambda i: K.decode_attention(q, kcs[i % 2], vcs[i % 2], m, 1, 32, 8, 128, S, 128 ** -0.5,
+                                               cache_pos=pos, out=o, workspace=ws), args.reps)
+        out[f"attention(seq={args.seq})"] = (t, m * args.seq * g.kv_dim * 2 * 2)
+    if "oproj" in wanted:
+        ow = w((H, g.q_dim), "mb/o")
+        a = synth.normal((m, g.q_dim), 1.0, 0, "mb/a", device=dev)
+        h = torch.empty(m, H, device=dev, dtype=torch.bfloat16)
+        t = _time(lambda i: K.oproj_residual(a, ow[i % C], x, out=h), args.reps)
+        out["oproj+residual"] = (t, H * g.q_dim * 2)
+    if "gateup" in wanted:
+        guw = w((2 * I, H), "mb/gu")
+        act = torch.empty(m, I, device=dev, dtype=torch.bfloat16)
+        t = _time(lambda i: K.gateup_silu(x, nw, guw[i % C], 1e-6, out=act), args.reps)
+        out["norm+gateup+silu"] = (t, 2 * I * H * 2)
+    if "down" in wanted:
+        dw = w((H, I), "mb/d")
+        act = synth.normal((m, I), 1.0, 0, "mb/act", device=dev)
+        h = torch.empty(m, H, device=dev, dtype=torch.bfloat16)
+        t = _time(lambda i: K.down_residual(act, dw[i % C], x, out=h), args.reps)
+        out["down+residual"] = (t, H * I * 2)
+    if "lmhead" in wanted:
+        lm = synth.normal((g.vocab_size, H), 0.02, 0, "mb/lm", device=dev)
+        ids = torch.empty(m, device=dev, dtype=torch.int64)
+        ws = torch.zeros(K.lmhead_workspace_bytes(m, g.vocab_size), device=dev, dtype=torch.uint8)
+        t = _time(lambda i: K.lmhead_argmax(x, nw, lm, 1e-6, out_ids=ids, workspace=ws), args.reps)
+        out["norm+lmhead+argmax"] = (t, g.vocab_size * H * 2)
+    if "embed" in wanted:
+        emb = synth.normal((g.vocab_size, H), 0.02, 0, "mb/emb", device=dev)
+        ids = torch.tensor([5] * m, device=dev)
+        xe = torch.empty(m, H, device=dev, dtype=torch.bfloat16)
+        t = _time(lambda i: K.embed_gather(ids, emb, out=xe), args.reps)
+        out["embed"] = (t, m * H * 2)
+    tc = {k for k in wanted if k.startswith("tc_")}
+    if tc:
+        def tc_case(name, n_rows, k_dim, epi, n_out, extra=None):
+            ws_ = torch.zeros(K.gemm_workspace_bytes(m, k_dim, n_out, epi), device=dev, dtype=torch.uint8)
+            wts = w((n_rows, k_dim), "mb/" + name)
+            xa = synth.normal((m, k_dim), 1.0, 0, "mb/xa" + name, device=dev)
+            res = synth.normal((m, n_out), 1.0, 0, "mb/res" + name, device=dev)
+            o = torch.empty(m, n_out, device=dev, dtype=torch.bfloat16)
+            t = _time(lambda i: K.gemm_tc(xa, wts[i % C], epilogue=epi, residual=res, out=o, workspace=ws_),
+                      args.reps)
+            out[f"tc_{name}(m={m})"] = (t, n_rows * k_dim * 2)
+        if "tc_qkv" in tc:
+            tc_case("qkv", g.qkv_dim, H, K.EPI_STORE, g.qkv_dim)
+        if "tc_oproj" in tc:
+            tc_case("oproj", H, g.q_dim, K.EPI_RESIDUAL, H)
+        if "tc_gateup" in tc:
+            tc_case("gateup", 2 * I, H, K.EPI_SILU_MUL, I)
+        if "tc_down" in tc:
+            tc_case("down", H, I, K.EPI_RESIDUAL, H)
+        if "tc_lmhead" in tc:
+            tc_case("lmhead_logits", g.vocab_size, H, K.EPI_STORE, g.vocab_size)
+    if "rmsnorm" in wanted:
+        xr = synth.normal((m, H), 1.0, 0, "mb/xr", device=dev)
+        yr = torch.empty_like(xr)
+        t = _time(lambda i: K.rmsnorm(xr, nw, 1e-6, out=yr), args.reps)
+        out["rmsnorm"] = (t, 2 * m * H * 2)
+    for name, (t, nbytes) in out.items():
+        print(json.dumps({"kernel": name, "m": m, "us": round(t * 1e6, 2), "bytes": nbytes,
+                          "gbs": round(nbytes / t / 1e9, 1)}))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -173,7 +173,7 @@ def _qkv(hidden: torch.Tensor, batch: int, q_len: int, qkv_w, hq, hkv, d, qn, kn
     x = hidden.reshape(m, -1).contiguous()
     if kv is not None:
         q = K.qkv_rope_append(x, batch, q_len, qkv_w, hq, hkv, d, qn, kn, cos_t, sin_t, input_norm_w=input_norm,
-                              eps=eps, uniform_past=past, k_cache=kv.key_cache[layer_idx],
+                              eps=eps, uniform_past=past, rope_offset=past, k_cache=kv.key_cache[layer_idx],
                               v_cache=kv.value_cache[layer_idx], max_seq=kv.layout.max_seq_len)
         return q, None, None
     k_out = torch.empty((m, hkv, d), device=x.device, dtype=x.dtype)

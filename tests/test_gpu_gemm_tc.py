@@ -1,0 +1,134 @@
+"""tcgen05 weight-streaming GEMM (ls_gemm_bf16_tcgen05) against fp32 torch.
+
+Shapes cover the decode / verify linears of Qwen3-4B at m = 1..256 activation
+rows, ragged n and k (partial tiles and k-blocks), every epilogue, and both a
+whole-tile and a split (stream-K) reduction.  Bound: max-abs error <=
+2e-2 * max(1, max|ref|), and at least 99% of outputs equal to the fp32
+reference rounded to bf16.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import tol
+from leanstack_b200 import kernels as K
+from leanstack_b200 import synth
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _rand(shape, std, name, seed=21):
+    return synth.normal(shape, std, seed, name, device=DEV)
+
+
+def _check(out, ref):
+    err = (out.float() - ref).abs().max().item()
+    assert err <= tol(ref), err
+    assert (out == ref.bfloat16()).float().mean().item() > 0.99
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 256, 128), (1, 6144, 2560), (8, 2560, 4096), (16, 2560, 9728),
+                                   (32, 6144, 2560), (80, 2560, 4096), (64, 300, 264), (128, 1024, 2560),
+                                   (3, 151936 // 8, 2560)])
+def test_gemm_tc_store(m, n, k):
+    x = _rand((m, k), 1.0, f"x{m}")
+    w = _rand((n, k), 0.02, f"w{n}{k}")
+    out = K.gemm_tc(x, w)
+    _check(out, x.float() @ w.float().t())
+
+
+@pytest.mark.parametrize("m", [1, 16, 80])
+def test_gemm_tc_residual_and_silu(m):
+    x = _rand((m, 4096), 1.0, "xa")
+    w = _rand((2560, 4096), 0.02, "wo")
+    res = _rand((m, 2560), 1.0, "res")
+    out = K.gemm_tc(x, w, epilogue=K.EPI_RESIDUAL, residual=res)
+    _check(out, res.float() + (x.float() @ w.float().t()).bfloat16().float())
+    inter = 9728
+    h = _rand((m, 2560), 1.0, "hn")
+    gu = _rand((2 * inter, 2560), 0.02, "gu")
+    act = K.gemm_tc(h, gu, epilogue=K.EPI_SILU_MUL)
+    g_u = (h.float() @ gu.float().t()).bfloat16()
+    ref = F.silu(g_u[:, :inter].float()).bfloat16().float() * g_u[:, inter:].float()
+    assert act.shape == (m, inter)
+    _check(act, ref)
+
+
+def test_gemm_tc_deterministic_and_reusable_workspace():
+    x = _rand((8, 9728), 1.0, "xd")
+    w = _rand((2560, 9728), 0.02, "wd")
+    ws = torch.zeros(K.gemm_workspace_bytes(8, 9728, 2560, K.EPI_STORE), device=DEV, dtype=torch.uint8)
+    a = K.gemm_tc(x, w, workspace=ws)
+    for _ in range(3):
+        assert torch.equal(K.gemm_tc(x, w, workspace=ws), a)
+    # counters are left at zero for the next call
+    cnt = ws[:256].view(torch.int32)
+    assert int(cnt.abs().sum()) == 0
+
+
+def test_gemm_tc_one_workspace_across_shapes():
+    """Calls of different shapes share one workspace (as the decode engine does):
+    every result matches a fresh-workspace call and the counters stay zero."""
+    shapes = [(128, 6144, 2560, K.EPI_STORE), (128, 2560, 4096, K.EPI_RESIDUAL), (128, 9728, 2560, K.EPI_SILU_MUL),
+              (128, 2560, 9728, K.EPI_RESIDUAL), (1, 151936, 2560, K.EPI_STORE), (1, 6144, 2560, K.EPI_STORE)]
+    ws = torch.zeros(max(K.gemm_workspace_bytes(m, k, n, e) for m, n, k, e in shapes), device=DEV, dtype=torch.uint8)
+    for rep in range(2):
+        for i, (m, n, k, e) in enumerate(shapes):
+            x = _rand((m, k), 1.0, f"sx{i}")
+            w = _rand((2 * n if e == K.EPI_SILU_MUL else n, k), 0.02, f"sw{i}")
+            res = _rand((m, n), 1.0, f"sr{i}") if e == K.EPI_RESIDUAL else None
+            K.device_error(clear=True)
+            got = K.gemm_tc(x, w, epilogue=e, residual=res, workspace=ws)
+            want = K.gemm_tc(x, w, epilogue=e, residual=res)
+            assert K.device_error(clear=True) == 0
+            assert torch.equal(got, want), (rep, i)
+    assert int(ws[:16384].view(torch.int32).abs().sum()) == 0
+
+
+def test_gemm_tc_rejects_m_beyond_128():
+    x = _rand((129, 256), 1.0, "x129")
+    w = _rand((256, 256), 0.02, "w129")
+    with pytest.raises(Exception, match="1..128|bad arguments"):
+        K.gemm_tc(x, w, workspace=torch.zeros(1 << 20, device=DEV, dtype=torch.uint8))
+
+
+def test_argmax_rows_lowest_index_on_ties():
+    logits = torch.full((3, 151936), -1.0, device=DEV, dtype=torch.bfloat16)
+    logits[0, 77] = 2.0
+    logits[1, 150000] = 3.0
+    logits[1, 9] = 3.0
+    logits[2] = _rand((151936,), 1.0, "lg")
+    ids = K.argmax_rows(logits)
+    assert ids[0].item() == 77 and ids[1].item() == 9
+    row = logits[2].float()
+    assert ids[2].item() == int(torch.nonzero(row == row.max())[0])
+
+
+@pytest.mark.parametrize("batch", [1, 4, 32])
+def test_tc_engine_matches_cuda_core_engine(batch):  # noqa: C901
+    """The tensor-core decode step agrees with the CUDA-core one (hidden state after
+    prefill within the bound, same first token), and every row of a batch equals
+    the batch-1 run of the same sequence exactly."""
+    from leanstack_b200.config import TINY
+    from leanstack_b200.engine import DecodeEngine
+    from leanstack_b200.leanserve import materialize_from_tensors
+
+    rt = materialize_from_tensors(TINY, synth.synth_checkpoint(TINY, 3, device=DEV), device=DEV)
+    prompt = synth.token_ids((batch, 21), TINY.vocab_size, 5, "tc/prompt")
+    tc_eng = DecodeEngine(rt, batch_size=batch, max_seq_len=96, linear_backend="tc")
+    tc_first = tc_eng.prefill(prompt)
+    tc_hidden = tc_eng.last_head_rows().clone()
+    if batch <= 8:
+        cc_eng = DecodeEngine(rt, batch_size=batch, max_seq_len=96, linear_backend="cuda_core")
+        cc_first = cc_eng.prefill(prompt)
+        cc_hidden = cc_eng.last_head_rows().clone()
+        assert (tc_hidden.float() - cc_hidden.float()).abs().max().item() <= tol(cc_hidden.float())
+        assert torch.equal(tc_first, cc_first)
+    tc = DecodeEngine(rt, batch_size=batch, max_seq_len=96, linear_backend="tc").generate(prompt, 16)
+    for r in range(min(batch, 2)):
+        one = DecodeEngine(rt, batch_size=1, max_seq_len=96, linear_backend="tc").generate(prompt[r:r + 1], 16)
+        assert torch.equal(one[0], tc[r])

@@ -96,9 +96,9 @@ def test_rmsnorm_and_embed():
     assert torch.equal(K.embed_gather(ids, emb), emb[ids])
 
 
-@pytest.mark.parametrize("q_len", [1, 2, 5])
-def test_qkv_rope_append_matches_oracle(q_len):
-    hq, hkv, d, hidden, batch, past = 32, 8, 128, 2560, 2, 37
+@pytest.mark.parametrize("batch,q_len", [(2, 1), (2, 2), (1, 5), (2, 4)])
+def test_qkv_rope_append_matches_oracle(batch, q_len):
+    hq, hkv, d, hidden, past = 32, 8, 128, 2560, 37
     x = _rand((batch * q_len, hidden), 1.0, "qx")
     qkv_w = _rand(((hq + 2 * hkv) * d, hidden), 0.02, "qkvw")
     qn = synth.norm_weight((d,), 2, "qn", device=DEV)
@@ -107,7 +107,7 @@ def test_qkv_rope_append_matches_oracle(q_len):
     cos, sin = qo.rope_cache(qo.rope_inv_freq(d, 1e6), 128, torch.bfloat16)
     kc = torch.zeros(batch, hkv, 128, d, device=DEV, dtype=torch.bfloat16)
     vc = torch.zeros_like(kc)
-    cache_pos = torch.tensor([past, past + 3], device=DEV, dtype=torch.int32)
+    cache_pos = torch.tensor([past + 3 * b for b in range(batch)], device=DEV, dtype=torch.int32)
     q = K.qkv_rope_append(x, batch, q_len, qkv_w, hq, hkv, d, qn, kn, cos.to(DEV), sin.to(DEV), input_norm_w=ln,
                           cache_pos=cache_pos, k_cache=kc, v_cache=vc, max_seq=128)
     # oracle on the CPU with the same inputs, per sequence (positions differ)

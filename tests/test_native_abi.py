@@ -48,7 +48,7 @@ def test_version_and_argument_errors_without_gpu(lib):
     assert rc == 1  # LS_ERR_INVALID_ARGUMENT
     assert "null" in nat.last_error()
     rc = lib.ls_rmsnorm_qkv_rope_kvappend(*([None] + [1, 1, 2560, None, ctypes.c_float(1e-6), None, 32, 8, 64]
-                                            + [None] * 4 + [16, None, 0, None, None, 16, None, None, None, None,
+                                            + [None] * 4 + [16, 0, None, 0, None, None, 16, None, None, None, None,
                                                             None]))
     assert rc != 0
     with pytest.raises(nat.LeanB200Error):
