@@ -58,7 +58,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
     ap.add_argument("--e2e-steps", type=int, default=64)
-    ap.add_argument("--linear-backend", choices=("auto", "tc", "cuda_core"), default="auto",
+    ap.add_argument("--linear-backend", choices=("auto", "persistent", "tc", "cuda_core"), default="auto",
                     help="tensor-core (tcgen05) or CUDA-core streaming linears for the decode step")
     return ap.parse_args()
 
@@ -348,7 +348,7 @@ def run_ours(args, world, rank, local):
             "config": {"workload": WORKLOAD, "model": "Qwen3-4B (random init)", "global_batch": world,
                        "seq_len": PROMPT, "max_seq": MAX_SEQ, "parallelism": f"replicas x{world}" if world > 1
                        else "single GPU", "l2": "not flushed: each step streams 8.05 GB of weights (> 126 MB L2)",
-                       "linear_backend": eng.backend},
+                       "linear_backend": "persistent" if eng.persistent else eng.backend},
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
             "gpu_launches": args.steps * eng.kernel_launches_per_step(),
         }

@@ -65,6 +65,9 @@ SIGNATURES: dict[str, list] = {
                                  _p, _i64, _p, _p, _p, _p],
     "ls_argmax_rows": [_p, _i64, _i64, _p, _p, _i64, _p],
     "ls_argmax_rows_workspace_bytes": [_i64, _i64, ctypes.POINTER(_i64)],
+    "ls_decode_step": [_p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+                       _p, _p, _p, _p, _i64, _p],
+    "ls_decode_step_workspace_bytes": [_i64, ctypes.POINTER(_i64)],
     "ls_gemm_bf16_tcgen05": [_p, _i64, _i64, _p, _i64, _int, _p, _p, _p, _i64, _p],
     "ls_gemm_bf16_tcgen05_workspace_bytes": [_i64, _i64, _i64, _int, ctypes.POINTER(_i64)],
     "ls_advance_cursors": [_p, _p, _i64, _i64, _p],

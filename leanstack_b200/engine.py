@@ -23,13 +23,19 @@ from .qwen_explicit import QwenSemanticStackRuntime, build_qwen_position_cache
 
 SMALL_M = 8      # largest token count of the CUDA-core linear kernels
 TC_MAX_M = 128   # largest token count of one tcgen05 GEMM launch
-BACKENDS = ("auto", "tc", "cuda_core")
+BACKENDS = ("auto", "persistent", "tc", "cuda_core")
 
 
 def resolve_backend(backend: str, batch_size: int) -> str:
-    """``auto``: tensor cores from 3 sequences on, CUDA-core streaming below."""
+    """``auto``: tensor cores from 3 sequences on, CUDA-core streaming below.
+
+    ``persistent`` (batch 1 only) runs each decode step as one cooperative
+    kernel (``ls_decode_step``) and the prefill on the tensor cores.
+    """
     if backend not in BACKENDS:
         raise ValueError(f"unknown linear backend {backend!r}; choose from {BACKENDS}")
+    if backend == "persistent" and batch_size != 1:
+        raise ValueError("the persistent decode step handles batch 1 only")
     if backend == "auto":
         return "tc" if batch_size >= 3 else "cuda_core"
     return backend
@@ -41,6 +47,9 @@ class DecodeEngine:
         if runtime.final_norm_weight is None or runtime.lm_head_weight is None:
             raise ValueError("the engine needs the output head (include_output_head=True)")
         self.backend = resolve_backend(linear_backend, batch_size)
+        self.persistent = self.backend == "persistent"
+        if self.persistent:
+            self.backend = "tc"  # prefill path; decode steps use the persistent kernel
         limit = TC_MAX_M if self.backend == "tc" else SMALL_M
         if batch_size < 1 or batch_size > limit:
             raise ValueError(f"batch_size {batch_size}: the {self.backend} step handles 1..{limit} sequences")
@@ -77,6 +86,18 @@ class DecodeEngine:
                                      dtype=torch.uint8)
         self.use_graph = use_graph
         self.graph: torch.cuda.CUDAGraph | None = None
+        if self.persistent:
+            rows = []
+            for li, layer in enumerate(runtime.layers):
+                att, mlp = layer.attention, layer.mlp
+                rows.append([layer.input_layernorm_weight.data_ptr(), att.qkv_proj_weight.data_ptr(),
+                             att.q_norm_weight.data_ptr(), att.k_norm_weight.data_ptr(), att.o_proj_weight.data_ptr(),
+                             layer.post_attention_layernorm_weight.data_ptr(), mlp.gate_up_proj_weight.data_ptr(),
+                             mlp.down_proj_weight.data_ptr(), self.kv.key_cache[li].data_ptr(),
+                             self.kv.value_cache[li].data_ptr()])
+            self.layer_table = torch.tensor(rows, dtype=torch.int64, device=dev)
+            self.ds_ws = torch.zeros(K.decode_step_workspace_bytes(g.num_key_value_heads), device=dev,
+                                     dtype=torch.uint8)
 
     # ------------------------------------------------------------------
     def _forward(self, q_len: int, head: bool) -> None:
@@ -163,12 +184,25 @@ class DecodeEngine:
     def set_next_ids(self, ids: torch.Tensor) -> None:
         self.arenas.ids[:self.B].copy_(ids.reshape(-1).to(self.arenas.ids.device))
 
+    def _persistent_step(self) -> None:
+        g, a, rt = self.g, self.arenas, self.rt
+        K.decode_step(self.layer_table, len(rt.layers), g.hidden_size, g.intermediate_size, g.num_attention_heads,
+                      g.num_key_value_heads, g.head_dim, g.vocab_size, self.S, g.rms_norm_eps, rt.embed_tokens_weight,
+                      rt.final_norm_weight, rt.lm_head_weight, self.cos, self.sin, a.ids[:1], self.kv.cache_pos,
+                      a.x[:1], a.h[:1], a.qkv[:1], a.attn[:1], a.act[:1], self.ds_ws)
+
+    def _decode_once(self) -> None:
+        if self.persistent:
+            self._persistent_step()
+        else:
+            self._forward(1, head=True)
+
     def capture(self) -> None:
         """Capture one decode step (q_len 1 + head + cursor advance) as a CUDA graph."""
         a = self.arenas
         saved_pos = self.kv.cache_pos.clone()
         saved_ids = a.ids[:self.B].clone()
-        self._forward(1, head=True)  # eager warm-up: sets kernel attributes, resolves symbols
+        self._decode_once()  # eager warm-up: sets kernel attributes, resolves symbols
         torch.cuda.synchronize()
         self.kv.cache_pos.copy_(saved_pos)
         a.ids[:self.B].copy_(saved_ids)
@@ -176,7 +210,7 @@ class DecodeEngine:
         stream = torch.cuda.Stream()
         stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.graph(graph, stream=stream):
-            self._forward(1, head=True)
+            self._decode_once()
         torch.cuda.current_stream().wait_stream(stream)
         torch.cuda.synchronize()
         self.graph = graph
@@ -190,7 +224,7 @@ class DecodeEngine:
         if self.graph is not None:
             self.graph.replay()
         else:
-            self._forward(1, head=True)
+            self._decode_once()
         self.kv.note_advanced(1)
 
     def last_head_rows(self) -> torch.Tensor:
@@ -212,6 +246,8 @@ class DecodeEngine:
 
     def kernel_launches_per_step(self) -> int:
         """Kernels one decode step launches (embedding, layers, head, cursor advance)."""
+        if self.persistent:
+            return 1
         per_layer = 8 if self.backend == "tc" else 6
         head = 3 if self.backend == "tc" else 1
         return 1 + per_layer * len(self.rt.layers) + head + 1
