@@ -18,8 +18,12 @@ Arms:
 * ``--impl reference``: the reference's CPU implementation of the path (the
   oracle port; the reference cannot travel to the GPU box) timed alone.
 
-Multi-GPU (torchrun, N > 1): every rank runs an independent bs1 replica
-(``scaling: weak``); tensor parallelism is not in this build yet.
+Multi-GPU (torchrun, N > 1): Megatron tensor parallelism over the N GPUs
+(``--parallel tp``, the default; ``scaling: strong``): column-split QKV and
+gate_up, row-split o_proj and down_proj with an NCCL all-reduce of their fp32
+partials, a vocab-split greedy head with a MAX all-reduce of argmax keys.  The
+same bs1 sequence is decoded by all ranks; ``value`` is its tok/s.
+``--parallel replicas`` runs N independent bs1 replicas instead (weak scaling).
 """
 
 from __future__ import annotations
@@ -60,6 +64,8 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--linear-backend", choices=("auto", "persistent", "tc", "cuda_core"), default="auto",
                     help="tensor-core (tcgen05) or CUDA-core streaming linears for the decode step")
+    ap.add_argument("--parallel", choices=("tp", "replicas"), default="tp",
+                    help="with N > 1 GPUs: tensor parallelism (one sequence) or independent replicas")
     return ap.parse_args()
 
 
@@ -233,6 +239,7 @@ def run_reference(args, world, rank):
 
 def run_ours(args, world, rank, local):
     from leanstack_b200 import kernels as K
+    from leanstack_b200 import tp as tpm
     from leanstack_b200.engine import DecodeEngine
     from leanstack_b200.leanserve import materialize_from_tensors
 
@@ -240,12 +247,19 @@ def run_ours(args, world, rank, local):
     torch.cuda.set_device(dev)
     g = QWEN3_4B
     peaks = measured_peaks()
+    tp_mode = world > 1 and args.parallel == "tp"
     tensors = synth.synth_checkpoint(g, SEED, device=dev)
-    rt = materialize_from_tensors(g, tensors, device=dev, free_source=True)
+    if tp_mode:
+        rt, shard = tpm.materialize_tp_shard(g, tensors, rank, world, device=dev)
+        comm = tpm.TPComm(rank, world)
+    else:
+        rt = materialize_from_tensors(g, tensors, device=dev, free_source=True)
+        shard = comm = None
     del tensors
     torch.cuda.empty_cache()
     prompt = synth.token_ids((1, PROMPT), g.vocab_size, SEED, "cfg2/prompt")
-    eng = DecodeEngine(rt, batch_size=1, max_seq_len=MAX_SEQ, linear_backend=args.linear_backend)
+    eng = DecodeEngine(rt, batch_size=1, max_seq_len=MAX_SEQ, linear_backend=args.linear_backend, tp=comm,
+                       shard=shard)
     eng.prefill(prompt)
     eng.capture()
     total_steps = args.warmup + args.steps + args.e2e_steps + 2
@@ -271,7 +285,8 @@ def run_ours(args, world, rank, local):
     barrier(world)
     elapsed_ms = max_over_ranks(elapsed_ms, world)
     ms_per_step = elapsed_ms / args.steps
-    value = world * args.steps * eng.B / (elapsed_ms / 1000.0)
+    seqs = 1 if tp_mode else world  # sequences decoded by the whole job
+    value = seqs * args.steps * eng.B / (elapsed_ms / 1000.0)
 
     # --- e2e through the public API: host ids in, host ids out, every step ---
     pin_in = torch.empty((1,), dtype=torch.int64, pin_memory=True)
@@ -288,7 +303,7 @@ def run_ours(args, world, rank, local):
         stream.synchronize()
     e2e_s = time.perf_counter() - t0
     e2e_s = max_over_ranks(e2e_s, world)
-    e2e = {"value": world * args.e2e_steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 8,
+    e2e = {"value": seqs * args.e2e_steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 8,
            "d2h_bytes_per_step": 8, "steps": args.e2e_steps}
 
     # --- roofline of the dominant kernel: gate_up + SiLU*up (with its norm on the CUDA-core path) ---
@@ -314,14 +329,16 @@ def run_ours(args, world, rank, local):
     ev3.record(stream)
     torch.cuda.synchronize()
     per_launch_s = ev2.elapsed_time(ev3) / 1000.0 / (reps * len(rt.layers))
-    gu_bytes = 2 * g.intermediate_size * g.hidden_size * 2 + g.hidden_size * 2 * 2 + g.intermediate_size * 2
+    gl = eng.g  # this rank's geometry (intermediate split under tensor parallelism)
+    gu_bytes = 2 * gl.intermediate_size * g.hidden_size * 2 + g.hidden_size * 2 * 2 + gl.intermediate_size * 2
     achieved = gu_bytes / per_launch_s / 1e9
     traffic = None
     tp = REPO / "profiles" / "traffic.json"
-    if tp.exists():
+    if tp.exists() and not tp_mode:
         traffic = json.loads(tp.read_text()).get("gateup_silu_per_launch_bytes")
-    step_bytes = g.num_hidden_layers * g.layer_weight_bytes() + g.lm_head_bytes() + \
-        (PROMPT + args.warmup + args.steps // 2) * g.kv_bytes_per_token()
+    # per-GPU step bytes: this rank's weight shard, vocab shard of the head and KV heads
+    step_bytes = g.num_hidden_layers * gl.layer_weight_bytes() + eng.vocab_rows * g.hidden_size * 2 + \
+        (PROMPT + args.warmup + args.steps // 2) * gl.kv_bytes_per_token()
     roofline = {"kernel": kernel_name, "bound": "hbm",
                 "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                 "traffic": traffic, "algorithmic_bytes_per_launch": gu_bytes,
@@ -343,17 +360,23 @@ def run_ours(args, world, rank, local):
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong" if tp_mode else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights, uniform ids)",
-            "config": {"workload": WORKLOAD, "model": "Qwen3-4B (random init)", "global_batch": world,
-                       "seq_len": PROMPT, "max_seq": MAX_SEQ, "parallelism": f"replicas x{world}" if world > 1
+            "config": {"workload": WORKLOAD, "model": "Qwen3-4B (random init)", "global_batch": seqs,
+                       "seq_len": PROMPT, "max_seq": MAX_SEQ,
+                       "parallelism": (f"tp{world}" if tp_mode else f"replicas x{world}") if world > 1
                        else "single GPU", "l2": "not flushed: each step streams 8.05 GB of weights (> 126 MB L2)",
                        "linear_backend": "persistent" if eng.persistent else eng.backend},
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
             "gpu_launches": args.steps * eng.kernel_launches_per_step(),
         }
+        if tp_mode:
+            line["collectives_per_step"] = eng.collectives_per_step()
         print(json.dumps(line), flush=True)
     barrier(world)
+    eng.graph = None  # release the graph (it holds NCCL work) before the process group goes
+    torch.cuda.synchronize()
     return 0
 
 

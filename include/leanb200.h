@@ -54,7 +54,8 @@ typedef enum ls_status {
 typedef enum ls_epilogue {
   LS_EPI_STORE = 0,     /* out = bf16(W x) */
   LS_EPI_RESIDUAL = 1,  /* out = bf16(residual + bf16(W x)) */
-  LS_EPI_SILU_MUL = 2   /* W = [gate; up] (2I rows): out[I] = bf16(bf16(silu(bf16 g)) * bf16 u) */
+  LS_EPI_SILU_MUL = 2,  /* W = [gate; up] (2I rows): out[I] = bf16(bf16(silu(bf16 g)) * bf16 u) */
+  LS_EPI_STORE_F32 = 4  /* out (float*) = W x unrounded: the partial of a tensor-parallel row-split linear */
 } ls_epilogue;
 
 typedef void* ls_stream_t; /* a cudaStream_t */
@@ -134,12 +135,13 @@ int ls_argmax_rows_workspace_bytes(int64_t m, int64_t n, int64_t* bytes);
 
 /*
  * GQA attention of q [m, Hq, D] over the cache (keys 0..cache_pos[b]+i for
- * token i of sequence b), split over the sequence and combined in-kernel.
- * Covers decode (q_len 1, unmasked) and verify (q_len k+1 with the decode
- * mask of src/leanstack/runtime/qwen_explicit.py:551-563).  Replaces the
- * SDPA calls at src/leanstack/runtime/qwen_explicit.py:886-903 and :1000-1039.
- * workspace: ls_decode_attention_workspace_bytes() bytes, zero-filled once
- * before first use (the kernel leaves its counters at zero).
+ * token i of sequence b), split over the sequence on the tensor cores and
+ * merged inside a thread-block cluster.  Covers decode (q_len 1, unmasked) and
+ * verify (q_len k+1 with the decode mask of
+ * src/leanstack/runtime/qwen_explicit.py:551-563).  Replaces the SDPA calls at
+ * src/leanstack/runtime/qwen_explicit.py:886-903 and :1000-1039.
+ * workspace: ls_decode_attention_workspace_bytes() bytes (currently 0; the
+ * argument is kept so that a caller's buffer plan stays valid).
  */
 int ls_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
                         int64_t uniform_past, int64_t batch, int64_t q_len, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
@@ -228,6 +230,25 @@ int ls_decode_step(const ls_decode_layer* layers, int64_t num_layers, int64_t hi
                    const void* rope_cos, const void* rope_sin, int64_t* ids, int32_t* cache_pos, void* x, void* h,
                    void* qkv, void* attn, void* act, void* workspace, int64_t workspace_bytes, ls_stream_t stream);
 int ls_decode_step_workspace_bytes(int64_t num_kv_heads, int64_t* bytes);
+
+/* Tensor-parallel greedy head.  Each rank holds a vocab shard (rows
+ * [vocab_offset, vocab_offset + vocab_rows) of lm_head) and writes, per row, an
+ * int64 key of its best (bf16 logit, vocab id): a signed MAX over the ranks'
+ * keys (one all-reduce of m int64) selects the largest logit and, on equal
+ * logits, the lowest id -- the tie rule of torch.argmax in
+ * select_semantic_greedy_token (src/leanstack/runtime/qwen_explicit.py:952-960).
+ * ls_argmax_keys_to_ids turns the reduced keys back into ids. */
+int ls_lmhead_argmax_keys(const void* h, int64_t m, int64_t hidden, const void* final_norm_w, float eps,
+                          const void* lm_head_w, int64_t vocab_rows, int64_t vocab_offset, int64_t* out_keys,
+                          void* workspace, int64_t workspace_bytes, ls_stream_t stream);
+int ls_argmax_rows_keys(const void* logits, int64_t m, int64_t n, int64_t vocab_offset, int64_t* out_keys,
+                        void* workspace, int64_t workspace_bytes, ls_stream_t stream);
+int ls_argmax_keys_to_ids(const int64_t* keys, int64_t m, int64_t* out_ids, ls_stream_t stream);
+
+/* out = bf16(residual + bf16(y)) over n elements, y fp32: the residual epilogue
+ * of o_proj / down applied after the tensor-parallel all-reduce of their
+ * fp32 partials (src/leanstack/runtime/qwen_explicit.py:819-829, :1262). */
+int ls_residual_add_f32(const void* residual, const float* y, int64_t n, void* out, ls_stream_t stream);
 
 /* Standalone RMSNorm over the last dim, bf16((x * rsqrt(mean(x^2) + eps)) * w),
  * for m rows of length n (src/leanstack/runtime/qwen_explicit.py:621-637). */

@@ -24,7 +24,7 @@ STATUS_NAMES = {
     8: "LS_ERR_NOT_SUPPORTED",
 }
 
-EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL = 0, 1, 2
+EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_STORE_F32 = 0, 1, 2, 4
 
 
 class NativeLibraryMissing(RuntimeError):
@@ -61,6 +61,10 @@ SIGNATURES: dict[str, list] = {
     "ls_lmhead_argmax": [_p, _i64, _i64, _p, _f32, _p, _i64, _p, _p, _i64, _p],
     "ls_lmhead_workspace_bytes": [_i64, _i64, ctypes.POINTER(_i64)],
     "ls_rmsnorm": [_p, _i64, _i64, _p, _f32, _p, _p],
+    "ls_residual_add_f32": [_p, _p, _i64, _p, _p],
+    "ls_lmhead_argmax_keys": [_p, _i64, _i64, _p, _f32, _p, _i64, _i64, _p, _p, _i64, _p],
+    "ls_argmax_rows_keys": [_p, _i64, _i64, _i64, _p, _p, _i64, _p],
+    "ls_argmax_keys_to_ids": [_p, _i64, _p, _p],
     "ls_qk_norm_rope_kvappend": [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _f32, _p, _p, _i64, _i64, _p, _i64, _p,
                                  _p, _i64, _p, _p, _p, _p],
     "ls_argmax_rows": [_p, _i64, _i64, _p, _p, _i64, _p],

@@ -53,7 +53,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, in
 constexpr int kArgmaxThreads = 256;
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const __nv_bfloat16* logits, int n, int chunks,
                                                                      float* part_val, int* part_idx,
-                                                                     unsigned int* counters, int64_t* out_ids) {
+                                                                     unsigned int* counters, int64_t* out_ids,
+                                                                     int64_t id_offset, int out_keys) {
   grid_dep_wait();
   __shared__ float bv[kArgmaxThreads / 32];
   __shared__ int bi[kArgmaxThreads / 32];
@@ -100,9 +101,24 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const __nv_
   __syncthreads();
   reduce();
   if (threadIdx.x == 0) {
-    out_ids[row] = (int64_t)besti;
+    const int64_t id = (int64_t)besti + id_offset;
+    out_ids[row] = out_keys ? argmax_key(best, id) : id;
     counters[row] = 0u;
   }
+}
+
+// ids[i] = the vocab id carried by the winning key of row i.
+__global__ void argmax_keys_to_ids_kernel(const int64_t* keys, int64_t m, int64_t* ids) {
+  grid_dep_wait();
+  for (int64_t i = threadIdx.x; i < m; i += blockDim.x) ids[i] = argmax_key_id(keys[i]);
+}
+
+// out = bf16(residual + bf16(y)) for fp32 y: the residual epilogue applied
+// after a tensor-parallel all-reduce of row-split partials.
+__global__ void residual_add_kernel(const __nv_bfloat16* residual, const float* y, __nv_bfloat16* out, int64_t n) {
+  grid_dep_wait();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = f_to_bf16(bf16_to_f(residual[i]) + round_bf16(y[i]));
 }
 
 __global__ void advance_cursors_kernel(int* cache_pos, const int* delta, int batch, int q_len) {
@@ -167,6 +183,9 @@ int launch_linear(const void* x, int64_t m, int64_t k, const void* norm_w, float
                   int epi, const void* residual, void* out, cudaStream_t stream, float* part_val, int* part_idx,
                   unsigned int* counter, int64_t* out_ids, int grid_override);
 int lmhead_grid(int64_t vocab, int64_t m);
+int launch_lmhead_keys(const void* h, int64_t m, int64_t k, const void* norm_w, float eps, const void* w,
+                       int64_t rows, int64_t vocab_offset, int64_t* out_keys, cudaStream_t stream, float* part_val,
+                       int* part_idx, unsigned int* counter, int grid);
 int launch_qk_norm_rope(const void* qkv, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, const void* qn,
                         const void* kn, const void* cos, const void* sin, int64_t rope_len, int64_t rope_offset,
                         const int32_t* cache_pos, int64_t uniform_past, void* k_cache, void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* q_out,
@@ -243,8 +262,8 @@ int ls_embed_gather(const int64_t* ids, int64_t m, const void* embed, int64_t vo
 
 int ls_linear_bf16(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w, int64_t n,
                    int epilogue, const void* residual, void* out, ls_stream_t stream) {
-  LS_REQUIRE(epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL, LS_ERR_INVALID_ARGUMENT,
-             "ls_linear_bf16: unknown epilogue %d", epilogue);
+  LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32,
+             LS_ERR_INVALID_ARGUMENT, "ls_linear_bf16: unknown epilogue %d", epilogue);
   return launch_linear(x, m, k, norm_w, eps, w, n, epilogue, residual, out, (cudaStream_t)stream, nullptr, nullptr,
                        nullptr, nullptr, 0);
 }
@@ -364,16 +383,16 @@ int ls_lmhead_argmax(const void* h, int64_t m, int64_t hidden, const void* final
 int ls_gemm_bf16_tcgen05_workspace_bytes(int64_t m, int64_t k, int64_t n, int epilogue, int64_t* bytes) {
   LS_REQUIRE(bytes && m > 0 && m <= 128 && k > 0 && n > 0, LS_ERR_INVALID_ARGUMENT,
              "ls_gemm_bf16_tcgen05_workspace_bytes: bad arguments");
-  LS_REQUIRE(epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL, LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d",
-             epilogue);
+  LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32,
+             LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d", epilogue);
   return tc_workspace_bytes(m, k, n, epilogue, bytes);
 }
 
 int ls_gemm_bf16_tcgen05(const void* x, int64_t m, int64_t k, const void* w, int64_t n, int epilogue,
                          const void* residual, void* out, void* workspace, int64_t workspace_bytes,
                          ls_stream_t stream) {
-  LS_REQUIRE(epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL, LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d",
-             epilogue);
+  LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32,
+             LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d", epilogue);
   return launch_gemm_tc(x, m, k, w, n, epilogue, residual, out, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
@@ -429,9 +448,57 @@ int ls_argmax_rows(const void* logits, int64_t m, int64_t n, int64_t* out_ids, v
   const int64_t cnt_bytes = ((m * 4 + 255) / 256) * 256, region = ((m * c * 4 + 255) / 256) * 256;
   lsb::argmax_rows_kernel<<<dim3((unsigned)c, (unsigned)m), lsb::kArgmaxThreads, 0, (cudaStream_t)stream>>>(
       static_cast<const __nv_bfloat16*>(logits), (int)n, c, reinterpret_cast<float*>(ws + cnt_bytes),
-      reinterpret_cast<int*>(ws + cnt_bytes + region), reinterpret_cast<unsigned int*>(ws), out_ids);
+      reinterpret_cast<int*>(ws + cnt_bytes + region), reinterpret_cast<unsigned int*>(ws), out_ids, 0, 0);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "argmax_rows launch: %s", cudaGetErrorString(e));
+}
+
+int ls_argmax_rows_keys(const void* logits, int64_t m, int64_t n, int64_t vocab_offset, int64_t* out_keys,
+                        void* workspace, int64_t workspace_bytes, ls_stream_t stream) {
+  LS_REQUIRE(logits && out_keys && workspace, LS_ERR_INVALID_ARGUMENT, "ls_argmax_rows_keys: null pointer");
+  LS_REQUIRE(m > 0 && m <= 65535 && n > 0 && n < (1ll << 31) && vocab_offset >= 0 && vocab_offset + n <= (1ll << 31),
+             LS_ERR_INVALID_ARGUMENT, "ls_argmax_rows_keys: bad sizes");
+  int64_t need = 0;
+  int rc = ls_argmax_rows_workspace_bytes(m, n, &need);
+  if (rc) return rc;
+  LS_REQUIRE(workspace_bytes >= need, LS_ERR_WORKSPACE, "ls_argmax_rows_keys: workspace needs %lld bytes",
+             (long long)need);
+  const int c = argmax_chunks(m, n);
+  char* ws = static_cast<char*>(workspace);
+  const int64_t cnt_bytes = ((m * 4 + 255) / 256) * 256, region = ((m * c * 4 + 255) / 256) * 256;
+  lsb::argmax_rows_kernel<<<dim3((unsigned)c, (unsigned)m), lsb::kArgmaxThreads, 0, (cudaStream_t)stream>>>(
+      static_cast<const __nv_bfloat16*>(logits), (int)n, c, reinterpret_cast<float*>(ws + cnt_bytes),
+      reinterpret_cast<int*>(ws + cnt_bytes + region), reinterpret_cast<unsigned int*>(ws), out_keys, vocab_offset,
+      1);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "argmax_rows_keys launch: %s", cudaGetErrorString(e));
+}
+
+int ls_lmhead_argmax_keys(const void* h, int64_t m, int64_t hidden, const void* final_norm_w, float eps,
+                          const void* lm_head_w, int64_t vocab_rows, int64_t vocab_offset, int64_t* out_keys,
+                          void* workspace, int64_t workspace_bytes, ls_stream_t stream) {
+  LS_REQUIRE(out_keys && workspace, LS_ERR_INVALID_ARGUMENT, "ls_lmhead_argmax_keys: null pointer");
+  LS_REQUIRE(m >= 1 && m <= 8, LS_ERR_UNSUPPORTED_SHAPE, "ls_lmhead_argmax_keys: m=%lld outside 1..8", (long long)m);
+  LS_REQUIRE(vocab_offset >= 0 && vocab_offset + vocab_rows <= (1ll << 31), LS_ERR_INVALID_ARGUMENT,
+             "ls_lmhead_argmax_keys: vocab shard beyond 2^31");
+  int64_t need = 0;
+  int rc = ls_lmhead_workspace_bytes(m, vocab_rows, &need);
+  if (rc) return rc;
+  LS_REQUIRE(workspace_bytes >= need, LS_ERR_WORKSPACE, "ls_lmhead_argmax_keys: workspace needs %lld bytes",
+             (long long)need);
+  const int g = lmhead_grid(vocab_rows, m);
+  char* ws = static_cast<char*>(workspace);
+  const int64_t region = ((m * g * 4 + 255) / 256) * 256;
+  return launch_lmhead_keys(h, m, hidden, final_norm_w, eps, lm_head_w, vocab_rows, vocab_offset, out_keys,
+                            (cudaStream_t)stream, reinterpret_cast<float*>(ws + 256),
+                            reinterpret_cast<int*>(ws + 256 + region), reinterpret_cast<unsigned int*>(ws), g);
+}
+
+int ls_argmax_keys_to_ids(const int64_t* keys, int64_t m, int64_t* out_ids, ls_stream_t stream) {
+  LS_REQUIRE(keys && out_ids && m > 0 && m <= 65535, LS_ERR_INVALID_ARGUMENT, "ls_argmax_keys_to_ids: bad arguments");
+  lsb::argmax_keys_to_ids_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(keys, m, out_ids);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "argmax_keys_to_ids launch: %s", cudaGetErrorString(e));
 }
 
 int ls_decode_step_workspace_bytes(int64_t num_kv_heads, int64_t* bytes) {
@@ -456,6 +523,17 @@ int ls_decode_step(const ls_decode_layer* layers, int64_t num_layers, int64_t hi
   return decode_step(layers, num_layers, hidden, intermediate, num_heads, num_kv_heads, head_dim, vocab, max_seq, eps,
                      embed, final_norm_w, lm_head_w, rope_cos, rope_sin, ids, cache_pos, x, h, qkv, attn, act,
                      workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int ls_residual_add_f32(const void* residual, const float* y, int64_t n, void* out, ls_stream_t stream) {
+  LS_REQUIRE(residual && y && out && n > 0, LS_ERR_INVALID_ARGUMENT, "ls_residual_add_f32: bad arguments");
+  const int threads = 256;
+  int64_t blocks = (n + threads - 1) / threads;
+  if (blocks > 4 * sm_count()) blocks = 4 * sm_count();
+  lsb::residual_add_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(
+      static_cast<const __nv_bfloat16*>(residual), y, static_cast<__nv_bfloat16*>(out), n);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "residual_add launch: %s", cudaGetErrorString(e));
 }
 
 int ls_rmsnorm(const void* x, int64_t m, int64_t n, const void* w, float eps, void* out, ls_stream_t stream) {

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <cstring>
 
 #include "../../include/leanb200.h"
 
@@ -146,6 +147,22 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
 }
 
 
+
+// Orderable 64-bit key of a (logit, vocab id) candidate: a signed max over
+// keys picks the largest logit and, among equal logits, the lowest id, so the
+// winners of vocab shards on different GPUs combine with one MAX all-reduce.
+// -0 is folded into +0 so that the two compare equal, as floats do.
+__host__ __device__ __forceinline__ int64_t argmax_key(float v, int64_t id) {
+  v += 0.0f;
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  const uint64_t k = ((uint64_t)u << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)id);
+  return (int64_t)(k ^ 0x8000000000000000ull);
+}
+__host__ __device__ __forceinline__ int64_t argmax_key_id(int64_t key) {
+  return (int64_t)(0xFFFFFFFFu - (uint32_t)((uint64_t)key & 0xFFFFFFFFull));
+}
 
 }  // namespace lsb
 

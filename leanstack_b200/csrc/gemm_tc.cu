@@ -44,7 +44,7 @@ constexpr int kTcMaxStages = 8;
 constexpr int kTcMaxTiles = 2048;
 constexpr size_t kTcCounterBytes = (size_t)2 * kTcMaxTiles * sizeof(unsigned int);
 
-enum { TEPI_STORE = 0, TEPI_RESIDUAL = 1, TEPI_SILU_MUL = 2 };
+enum { TEPI_STORE = 0, TEPI_RESIDUAL = 1, TEPI_SILU_MUL = 2, TEPI_STORE_F32 = 4 };
 
 struct TcParams {
   const __nv_bfloat16* residual;  // [B, N]
@@ -128,10 +128,16 @@ __device__ __forceinline__ bool wait_counter(const unsigned int* ctr, unsigned i
 
 template <int EPI>
 __device__ __forceinline__ float tc_apply(const TcParams& p, size_t o, float y, float y2) {
-  if (EPI == TEPI_STORE) return y;
+  if (EPI == TEPI_STORE || EPI == TEPI_STORE_F32) return y;
   if (EPI == TEPI_RESIDUAL) return bf16_to_f(p.residual[o]) + round_bf16(y);
   const float g = round_bf16(y);
   return round_bf16(g / (1.0f + expf(-g))) * round_bf16(y2);
+}
+
+template <int EPI>
+__device__ __forceinline__ void tc_store(const TcParams& p, size_t o, float v) {
+  if (EPI == TEPI_STORE_F32) reinterpret_cast<float*>(p.out)[o] = v;
+  else p.out[o] = f_to_bf16(v);
 }
 
 template <int EPI>
@@ -293,7 +299,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               const int b = cb + j;
               if (b < p.B) {
                 const size_t o = (size_t)b * p.N + n;
-                p.out[o] = f_to_bf16(tc_apply<EPI>(p, o, v[j], SILU ? w2[j] : 0.f));
+                tc_store<EPI>(p, o, tc_apply<EPI>(p, o, v[j], SILU ? w2[j] : 0.f));
               }
             }
           }
@@ -357,7 +363,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int q = 0; q < 8; ++q) {
               if (bb + q < b1) {
                 const size_t o = (size_t)(bb + q) * p.N + n;
-                p.out[o] = f_to_bf16(tc_apply<EPI>(p, o, y[q], y2[q]));
+                tc_store<EPI>(p, o, tc_apply<EPI>(p, o, y[q], y2[q]));
               }
             }
           }
@@ -540,6 +546,7 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
     case TEPI_STORE: return launch_tc_t<TEPI_STORE>(mw, mw2, mx, p, pl, stream);
     case TEPI_RESIDUAL: return launch_tc_t<TEPI_RESIDUAL>(mw, mw2, mx, p, pl, stream);
     case TEPI_SILU_MUL: return launch_tc_t<TEPI_SILU_MUL>(mw, mw2, mx, p, pl, stream);
+    case TEPI_STORE_F32: return launch_tc_t<TEPI_STORE_F32>(mw, mw2, mx, p, pl, stream);
     default: return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_tc: unknown epilogue %d", epi);
   }
 }

@@ -29,7 +29,7 @@ constexpr int kLinWarps = kLinThreads / 32;
 constexpr int kGranule = 256;  // bf16 elements per warp-wide 512-byte load
 constexpr uint32_t kPrefetchBytes = 64 * 1024;  // per CTA and weight range, issued before the PDL wait
 
-enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3 };
+enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3, EPI_STORE_F32 = 4 };
 
 struct LinearParams {
   const __nv_bfloat16* x;      // [M, K]
@@ -47,7 +47,9 @@ struct LinearParams {
   float* part_val;       // [M, gridDim.x]
   int* part_idx;         // [M, gridDim.x]
   unsigned int* counter; // 1 int, zero between calls
-  int64_t* out_ids;      // [M]
+  int64_t* out_ids;      // [M]: winning row index, or its argmax_key when out_keys
+  int64_t id_offset;     // added to the winning row index (vocab shard offset)
+  int out_keys;
 };
 
 template <int M>
@@ -213,7 +215,12 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
   grid_dep_launch();
 
   // ---- epilogue ----
-  if (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
+  if (EPI == EPI_STORE_F32) {  // unrounded fp32 partial (tensor-parallel row-split linears)
+    for (int i = tid; i < M * P; i += kLinThreads) {
+      const int m = i / P, t = i - m * P;
+      reinterpret_cast<float*>(p.out)[(size_t)m * p.N + u0 + t] = row_sum(m, t);
+    }
+  } else if (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
     for (int i = tid; i < M * P; i += kLinThreads) {
       const int m = i / P, t = i - m * P;
       const size_t o = (size_t)m * p.N + u0 + t;
@@ -284,7 +291,8 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
         if (tid == 0) {
           for (int w = 1; w < kLinWarps; ++w)
             if (bv[w] > best || (bv[w] == best && bi[w] < besti)) { best = bv[w]; besti = bi[w]; }
-          p.out_ids[m] = (int64_t)besti;
+          const int64_t id = (int64_t)besti + p.id_offset;
+          p.out_ids[m] = p.out_keys ? argmax_key(best, id) : id;
         }
         __syncthreads();
       }
@@ -380,9 +388,10 @@ static bool stream_path_enabled() {
   return v == 1;
 }
 
-int launch_linear(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w, int64_t n,
-                  int epi, const void* residual, void* out, cudaStream_t stream, float* part_val, int* part_idx,
-                  unsigned int* counter, int64_t* out_ids, int grid_override) {
+static int launch_linear_impl(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w,
+                              int64_t n, int epi, const void* residual, void* out, cudaStream_t stream,
+                              float* part_val, int* part_idx, unsigned int* counter, int64_t* out_ids,
+                              int grid_override, int64_t id_offset, bool out_keys) {
   if (!x || !w || (epi != EPI_ARGMAX && !out)) return set_error(LS_ERR_INVALID_ARGUMENT, "linear: null pointer");
   if (m < 1 || m > 8) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "linear: m=%lld outside 1..8", (long long)m);
   if (k < 8 || n < 1 || k > 32768 || n > (int64_t)1 << 30)
@@ -392,7 +401,7 @@ int launch_linear(const void* x, int64_t m, int64_t k, const void* norm_w, float
     return set_error(LS_ERR_MISALIGNED, "linear: x/w/norm_w must be 16-byte aligned");
   if (epi == EPI_RESIDUAL && !residual) return set_error(LS_ERR_INVALID_ARGUMENT, "linear: residual is null");
   if (epi == EPI_SILU_MUL && (n % 2)) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "linear: gate_up rows odd");
-  if (stream_path_enabled() && stream_supported(m, k, n, epi))
+  if (stream_path_enabled() && epi <= EPI_ARGMAX && !out_keys && id_offset == 0 && stream_supported(m, k, n, epi))
     return launch_linear_stream(x, m, k, norm_w, eps, w, n, epi, residual, out, stream, part_val, part_idx, counter,
                                 out_ids);
   LinearParams p = {};
@@ -413,6 +422,8 @@ int launch_linear(const void* x, int64_t m, int64_t k, const void* norm_w, float
   p.part_idx = part_idx;
   p.counter = counter;
   p.out_ids = out_ids;
+  p.id_offset = id_offset;
+  p.out_keys = out_keys ? 1 : 0;
   const size_t smem = linear_smem((int)m, (int)k, p.max_segs);
   if (smem > 200 * 1024)
     return set_error(LS_ERR_UNSUPPORTED_SHAPE, "linear: m=%lld k=%lld needs %zu B of shared memory", (long long)m,
@@ -427,8 +438,25 @@ int launch_linear(const void* x, int64_t m, int64_t k, const void* norm_w, float
                                    : dispatch_m<EPI_SILU_MUL, false>((int)m, p, grid, smem, stream);
     case EPI_ARGMAX: return norm ? dispatch_m<EPI_ARGMAX, true>((int)m, p, grid, smem, stream)
                                  : dispatch_m<EPI_ARGMAX, false>((int)m, p, grid, smem, stream);
+    case EPI_STORE_F32: return norm ? dispatch_m<EPI_STORE_F32, true>((int)m, p, grid, smem, stream)
+                                    : dispatch_m<EPI_STORE_F32, false>((int)m, p, grid, smem, stream);
     default: return set_error(LS_ERR_INVALID_ARGUMENT, "linear: unknown epilogue %d", epi);
   }
+}
+
+int launch_linear(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w, int64_t n,
+                  int epi, const void* residual, void* out, cudaStream_t stream, float* part_val, int* part_idx,
+                  unsigned int* counter, int64_t* out_ids, int grid_override) {
+  return launch_linear_impl(x, m, k, norm_w, eps, w, n, epi, residual, out, stream, part_val, part_idx, counter,
+                            out_ids, grid_override, 0, false);
+}
+
+// Greedy head over one vocab shard: out_keys[m] = argmax_key(best logit, shard row + vocab_offset).
+int launch_lmhead_keys(const void* h, int64_t m, int64_t k, const void* norm_w, float eps, const void* w,
+                       int64_t rows, int64_t vocab_offset, int64_t* out_keys, cudaStream_t stream, float* part_val,
+                       int* part_idx, unsigned int* counter, int grid) {
+  return launch_linear_impl(h, m, k, norm_w, eps, w, rows, EPI_ARGMAX, nullptr, nullptr, stream, part_val, part_idx,
+                            counter, out_keys, grid, vocab_offset, true);
 }
 
 int lmhead_grid(int64_t vocab, int64_t m) { return linear_grid((int)vocab, (int)m); }

@@ -11,6 +11,12 @@ the host only replays it.
 Token flow: the step's input ids live in ``arenas.ids[:B]``; the greedy head
 writes the next ids back into the same slots, so consecutive replays decode
 autoregressively with no host round trip.
+
+Tensor parallelism (``tp`` given, world > 1): the runtime is this rank's shard
+(``tp.materialize_tp_shard``).  o_proj and down_proj write fp32 partials that
+one NCCL all-reduce sums before the residual-add kernel; the head reduces its
+vocab shard to int64 argmax keys and a MAX all-reduce picks the token.  The
+collectives are captured into the step's CUDA graph with the kernels.
 """
 
 from __future__ import annotations
@@ -20,6 +26,7 @@ import torch
 from . import kernels as K
 from .leanserve import allocate_arenas, build_resident_buffer_plan, runtime_weight_bytes
 from .qwen_explicit import QwenSemanticStackRuntime, build_qwen_position_cache
+from .tp import TPComm, TPShard
 
 SMALL_M = 8      # largest token count of the CUDA-core linear kernels
 TC_MAX_M = 128   # largest token count of one tcgen05 GEMM launch
@@ -43,10 +50,18 @@ def resolve_backend(backend: str, batch_size: int) -> str:
 
 class DecodeEngine:
     def __init__(self, runtime: QwenSemanticStackRuntime, batch_size: int, max_seq_len: int,
-                 max_tokens_per_step: int | None = None, use_graph: bool = True, linear_backend: str = "auto"):
+                 max_tokens_per_step: int | None = None, use_graph: bool = True, linear_backend: str = "auto",
+                 tp: TPComm | None = None, shard: TPShard | None = None):
         if runtime.final_norm_weight is None or runtime.lm_head_weight is None:
             raise ValueError("the engine needs the output head (include_output_head=True)")
+        self.tp = tp if (tp is not None and tp.world > 1) else None
+        if self.tp is not None and shard is None:
+            raise ValueError("a tensor-parallel engine needs its TPShard")
+        self.vocab_offset = shard.vocab_offset if self.tp is not None else 0
+        self.vocab_rows = runtime.lm_head_weight.shape[0]
         self.backend = resolve_backend(linear_backend, batch_size)
+        if self.tp is not None and self.backend == "persistent":
+            raise ValueError("the persistent decode step runs on one GPU only")
         self.persistent = self.backend == "persistent"
         if self.persistent:
             self.backend = "tc"  # prefill path; decode steps use the persistent kernel
@@ -73,17 +88,22 @@ class DecodeEngine:
         self.attn_ws = torch.zeros(max(ws, 256), device=dev, dtype=torch.uint8)
         if self.backend == "tc":
             T = self.T
-            shapes = [(T, g.hidden_size, g.qkv_dim, K.EPI_STORE), (T, g.q_dim, g.hidden_size, K.EPI_RESIDUAL),
+            row_epi = K.EPI_STORE_F32 if self.tp is not None else K.EPI_RESIDUAL
+            shapes = [(T, g.hidden_size, g.qkv_dim, K.EPI_STORE), (T, g.q_dim, g.hidden_size, row_epi),
                       (T, g.hidden_size, g.intermediate_size, K.EPI_SILU_MUL),
-                      (T, g.intermediate_size, g.hidden_size, K.EPI_RESIDUAL),
-                      (batch_size, g.hidden_size, g.vocab_size, K.EPI_STORE)]
+                      (T, g.intermediate_size, g.hidden_size, row_epi),
+                      (batch_size, g.hidden_size, self.vocab_rows, K.EPI_STORE)]
             self.tc_ws = torch.zeros(max(K.gemm_workspace_bytes(*s_) for s_ in shapes), device=dev, dtype=torch.uint8)
             self.xn = torch.zeros(T, g.hidden_size, device=dev, dtype=runtime.dtype)
-            self.logits = torch.zeros(batch_size, g.vocab_size, device=dev, dtype=runtime.dtype)
-            self.lm_ws = torch.zeros(K.argmax_workspace_bytes(batch_size, g.vocab_size), device=dev, dtype=torch.uint8)
-        else:
-            self.lm_ws = torch.zeros(K.lmhead_workspace_bytes(batch_size, g.vocab_size), device=dev,
+            self.logits = torch.zeros(batch_size, self.vocab_rows, device=dev, dtype=runtime.dtype)
+            self.lm_ws = torch.zeros(K.argmax_workspace_bytes(batch_size, self.vocab_rows), device=dev,
                                      dtype=torch.uint8)
+        else:
+            self.lm_ws = torch.zeros(K.lmhead_workspace_bytes(batch_size, self.vocab_rows), device=dev,
+                                     dtype=torch.uint8)
+        if self.tp is not None:
+            self.part = torch.zeros(self.T, g.hidden_size, device=dev, dtype=torch.float32)
+            self.keys = torch.zeros(batch_size, device=dev, dtype=torch.int64)
         self.use_graph = use_graph
         self.graph: torch.cuda.CUDAGraph | None = None
         if self.persistent:
@@ -126,7 +146,17 @@ class DecodeEngine:
             K.decode_attention(a.q[:m], kv.key_cache[li], kv.value_cache[li], B, q_len, g.num_attention_heads,
                                g.num_key_value_heads, g.head_dim, self.S, att.attention_scale,
                                cache_pos=kv.cache_pos, out=a.attn[:m], workspace=self.attn_ws)
-            if tc:
+            if self.tp is not None:
+                self._row_split(a.attn[:m], att.o_proj_weight, a.x[:m], a.h[:m], tc)
+                if tc:
+                    K.rmsnorm(a.h[:m], layer.post_attention_layernorm_weight, eps, out=self.xn[:m])
+                    K.gemm_tc(self.xn[:m], mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=a.act[:m],
+                              workspace=self.tc_ws)
+                else:
+                    K.gateup_silu(a.h[:m], layer.post_attention_layernorm_weight, mlp.gate_up_proj_weight, eps,
+                                  out=a.act[:m])
+                self._row_split(a.act[:m], mlp.down_proj_weight, a.h[:m], a.x[:m], tc)
+            elif tc:
                 K.gemm_tc(a.attn[:m], att.o_proj_weight, epilogue=K.EPI_RESIDUAL, residual=a.x[:m], out=a.h[:m],
                           workspace=self.tc_ws)
                 K.rmsnorm(a.h[:m], layer.post_attention_layernorm_weight, eps, out=self.xn[:m])
@@ -146,7 +176,17 @@ class DecodeEngine:
                 a.head_rows.copy_(a.x[:m].view(B, q_len, -1)[:, -1])
                 rows = a.head_rows
             self._head_rows = rows
-            if tc:
+            if self.tp is not None:
+                if tc:
+                    K.rmsnorm(rows, rt.final_norm_weight, eps, out=self.xn[:B])
+                    K.gemm_tc(self.xn[:B], rt.lm_head_weight, out=self.logits, workspace=self.tc_ws)
+                    K.argmax_rows_keys(self.logits, self.vocab_offset, out_keys=self.keys, workspace=self.lm_ws)
+                else:
+                    K.lmhead_argmax_keys(rows, rt.final_norm_weight, rt.lm_head_weight, eps, self.vocab_offset,
+                                         out_keys=self.keys, workspace=self.lm_ws)
+                self.tp.all_reduce_max(self.keys)
+                K.argmax_keys_to_ids(self.keys, out_ids=a.ids[:B])
+            elif tc:
                 K.rmsnorm(rows, rt.final_norm_weight, eps, out=self.xn[:B])
                 K.gemm_tc(self.xn[:B], rt.lm_head_weight, out=self.logits, workspace=self.tc_ws)
                 K.argmax_rows(self.logits, out_ids=a.ids[:B], workspace=self.lm_ws)
@@ -154,6 +194,17 @@ class DecodeEngine:
                 K.lmhead_argmax(rows, rt.final_norm_weight, rt.lm_head_weight, eps, out_ids=a.ids[:B],
                                 workspace=self.lm_ws)
         K.advance_cursors(kv.cache_pos, q_len)
+
+    def _row_split(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor, out: torch.Tensor,
+                   tc: bool) -> None:
+        """Row-split linear of tensor parallelism: fp32 partial, all-reduce, residual add."""
+        part = self.part[:x.shape[0]]
+        if tc:
+            K.gemm_tc(x, w, epilogue=K.EPI_STORE_F32, out=part, workspace=self.tc_ws)
+        else:
+            K.linear(x, w, epilogue=K.EPI_STORE_F32, out=part)
+        self.tp.all_reduce_sum(part)
+        K.residual_add_f32(residual, part, out=out)
 
     # ------------------------------------------------------------------
     def reset(self) -> None:
@@ -250,4 +301,11 @@ class DecodeEngine:
             return 1
         per_layer = 8 if self.backend == "tc" else 6
         head = 3 if self.backend == "tc" else 1
+        if self.tp is not None:  # + residual-add after each row-split linear, + keys-to-ids
+            per_layer += 2
+            head += 1
         return 1 + per_layer * len(self.rt.layers) + head + 1
+
+    def collectives_per_step(self) -> int:
+        """NCCL all-reduces one decode step issues (0 on one GPU)."""
+        return 0 if self.tp is None else 2 * len(self.rt.layers) + 1

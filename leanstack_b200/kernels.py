@@ -13,7 +13,7 @@ import ctypes
 import torch
 
 from . import _native as nat
-from ._native import EPI_RESIDUAL, EPI_SILU_MUL, EPI_STORE  # noqa: F401
+from ._native import EPI_RESIDUAL, EPI_SILU_MUL, EPI_STORE, EPI_STORE_F32  # noqa: F401
 
 BF16 = torch.bfloat16
 
@@ -88,7 +88,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, *, norm_w: torch.Tensor | None = No
         _check(residual, "residual")
     cols = n // 2 if epilogue == EPI_SILU_MUL else n
     if out is None:
-        out = torch.empty((*x.shape[:-1], cols), device=x.device, dtype=BF16)
+        out = torch.empty((*x.shape[:-1], cols), device=x.device,
+                          dtype=torch.float32 if epilogue == EPI_STORE_F32 else BF16)
     nat.call("ls_linear_bf16", x.data_ptr(), m, k, _ptr(norm_w), float(eps), w.data_ptr(), n, int(epilogue),
              _ptr(residual), out.data_ptr(), _stream())
     return out
@@ -265,6 +266,47 @@ def lmhead_argmax(h: torch.Tensor, final_norm_w: torch.Tensor | None, lm_head_w:
     return out_ids
 
 
+def lmhead_argmax_keys(h: torch.Tensor, final_norm_w: torch.Tensor | None, lm_head_shard: torch.Tensor, eps: float,
+                       vocab_offset: int, *, out_keys: torch.Tensor | None = None,
+                       workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Greedy head over one vocab shard; int64 keys (see ``tp.argmax_key``) per row."""
+    _check(h, "h")
+    _check(lm_head_shard, "lm_head_shard")
+    hidden = h.shape[-1]
+    m = h.numel() // hidden
+    rows = lm_head_shard.shape[0]
+    if out_keys is None:
+        out_keys = torch.empty((m,), device=h.device, dtype=torch.int64)
+    need = lmhead_workspace_bytes(m, rows)
+    if workspace is None:
+        workspace = torch.zeros(need, device=h.device, dtype=torch.uint8)
+    nat.call("ls_lmhead_argmax_keys", h.data_ptr(), m, hidden, _ptr(final_norm_w), float(eps),
+             lm_head_shard.data_ptr(), rows, int(vocab_offset), out_keys.data_ptr(), workspace.data_ptr(),
+             workspace.numel(), _stream())
+    return out_keys
+
+
+def argmax_rows_keys(logits: torch.Tensor, vocab_offset: int, *, out_keys: torch.Tensor | None = None,
+                     workspace: torch.Tensor | None = None) -> torch.Tensor:
+    _check(logits, "logits")
+    m, n = logits.shape
+    if out_keys is None:
+        out_keys = torch.empty((m,), device=logits.device, dtype=torch.int64)
+    if workspace is None:
+        workspace = torch.zeros(argmax_workspace_bytes(m, n), device=logits.device, dtype=torch.uint8)
+    nat.call("ls_argmax_rows_keys", logits.data_ptr(), m, n, int(vocab_offset), out_keys.data_ptr(),
+             workspace.data_ptr(), workspace.numel(), _stream())
+    return out_keys
+
+
+def argmax_keys_to_ids(keys: torch.Tensor, *, out_ids: torch.Tensor | None = None) -> torch.Tensor:
+    _check(keys, "keys", torch.int64)
+    if out_ids is None:
+        out_ids = torch.empty_like(keys)
+    nat.call("ls_argmax_keys_to_ids", keys.data_ptr(), keys.numel(), out_ids.data_ptr(), _stream())
+    return out_ids
+
+
 def gemm_workspace_bytes(m: int, k: int, n: int, epilogue: int) -> int:
     v = ctypes.c_int64(0)
     nat.call("ls_gemm_bf16_tcgen05_workspace_bytes", m, k, n, int(epilogue), ctypes.byref(v))
@@ -284,7 +326,8 @@ def gemm_tc(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = EPI_STORE, resi
     if residual is not None:
         _check(residual, "residual")
     if out is None:
-        out = torch.empty((*x.shape[:-1], n), device=x.device, dtype=BF16)
+        out = torch.empty((*x.shape[:-1], n), device=x.device,
+                          dtype=torch.float32 if epilogue == EPI_STORE_F32 else BF16)
     need = gemm_workspace_bytes(m, k, n, epilogue)
     if workspace is None:
         workspace = torch.zeros(need, device=x.device, dtype=torch.uint8)
@@ -316,6 +359,16 @@ def decode_step(layer_table: torch.Tensor, num_layers: int, hidden: int, interme
              head_dim, vocab, max_seq, float(eps), embed.data_ptr(), final_norm_w.data_ptr(), lm_head_w.data_ptr(),
              cos.data_ptr(), sin.data_ptr(), ids.data_ptr(), cache_pos.data_ptr(), x.data_ptr(), h.data_ptr(),
              qkv.data_ptr(), attn.data_ptr(), act.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
+
+
+def residual_add_f32(residual: torch.Tensor, y: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``out = bf16(residual + bf16(y))`` for an fp32 ``y`` (after a tensor-parallel all-reduce)."""
+    _check(residual, "residual")
+    _check(y, "y", torch.float32)
+    if out is None:
+        out = torch.empty_like(residual)
+    nat.call("ls_residual_add_f32", residual.data_ptr(), y.data_ptr(), residual.numel(), out.data_ptr(), _stream())
+    return out
 
 
 def advance_cursors(cache_pos: torch.Tensor, q_len: int, delta: torch.Tensor | None = None) -> None:

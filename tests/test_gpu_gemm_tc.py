@@ -132,3 +132,16 @@ def test_tc_engine_matches_cuda_core_engine(batch):  # noqa: C901
     for r in range(min(batch, 2)):
         one = DecodeEngine(rt, batch_size=1, max_seq_len=96, linear_backend="tc").generate(prompt[r:r + 1], 16)
         assert torch.equal(one[0], tc[r])
+
+
+@pytest.mark.parametrize("m", [1, 32, 128])
+def test_gemm_tc_f32_partials(m):
+    """fp32 epilogue (tensor-parallel row-split partials) equals the bf16 store
+    epilogue before its rounding."""
+    x = _rand((m, 4864), 1.0, "xf")
+    w = _rand((2560, 4864), 0.02, "wf")
+    out = K.gemm_tc(x, w, epilogue=K.EPI_STORE_F32)
+    assert out.dtype == torch.float32
+    ref = x.float() @ w.float().t()
+    assert (out - ref).abs().max().item() <= 1e-3 * max(1.0, ref.abs().max().item())
+    assert torch.equal(out.bfloat16(), K.gemm_tc(x, w))

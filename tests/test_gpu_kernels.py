@@ -207,3 +207,26 @@ def test_kv_overflow_sets_device_flag_without_fault():
     assert K.device_error(clear=True) == 6  # LS_ERR_KV_OVERFLOW
     assert kc.abs().sum().item() == 0
     assert K.device_error(clear=True) == 0
+
+
+@pytest.mark.parametrize("m", [1, 3, 8])
+def test_linear_f32_partials_and_residual_add(m):
+    """Row-split (tensor-parallel) form of o_proj / down: the fp32 partials of two
+    halves of the in-features, summed and passed to the residual-add kernel,
+    match the unsplit residual linear within the bound."""
+    k, n = 4096, 2560
+    x = _rand((m, k), 1.0, "xp")
+    w = _rand((n, k), 0.02, "wp")
+    res = _rand((m, n), 1.0, "resp")
+    parts = [K.linear(x[:, h * k // 2:(h + 1) * k // 2].contiguous(), w[:, h * k // 2:(h + 1) * k // 2].contiguous(),
+                      epilogue=K.EPI_STORE_F32) for h in range(2)]
+    assert parts[0].dtype == torch.float32
+    full = K.linear(x, w, epilogue=K.EPI_STORE_F32)
+    ref = x.float() @ w.float().t()
+    assert (full - ref).abs().max().item() <= 1e-3 * max(1.0, ref.abs().max().item())
+    y = K.residual_add_f32(res, parts[0] + parts[1])
+    ref_y = res.float() + ref.bfloat16().float()
+    assert (y.float() - ref_y).abs().max().item() <= tol(ref_y)
+    # Same rounding points as the fused residual epilogue.
+    y1 = K.residual_add_f32(res, full)
+    assert (y1 == K.oproj_residual(x, w, res)).float().mean().item() > 0.99
