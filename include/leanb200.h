@@ -177,6 +177,18 @@ int ls_lmhead_argmax(const void* h, int64_t m, int64_t hidden, const void* final
                      int64_t workspace_bytes, ls_stream_t stream);
 int ls_lmhead_workspace_bytes(int64_t m, int64_t vocab, int64_t* bytes);
 
+/* ls_lmhead_argmax without a caller workspace; it allocates no device memory.
+ * No counterpart in the reference: it is for callers that cannot allocate on
+ * the token-selection path (an FFI host with no device allocator of its own, or
+ * a server whose HBM plan is fixed at start-up).  Its scratch is a fixed 16 KiB
+ * array per device inside this library; a call that would need more (m rows x
+ * head-grid CTAs) fails with LS_ERR_WORKSPACE.  The first call on a device does
+ * set-up (address lookup, counter cleared on `stream`): make it before any
+ * stream capture.  Calls that overlap on the GPU share the scratch and race:
+ * serialise them on one stream. */
+int ls_lmhead_argmax_noalloc(const void* h, int64_t m, int64_t hidden, const void* final_norm_w, float eps,
+                             const void* lm_head_w, int64_t vocab, int64_t* out_ids, ls_stream_t stream);
+
 /*
  * Weight-streaming GEMM on the tcgen05 tensor cores for 1 <= m <= 128
  * activation rows (larger batches run as several launches): out[m, n] = epilogue(x[m, k] . w[n, k]^T) with epilogue one

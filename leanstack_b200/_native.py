@@ -59,6 +59,7 @@ SIGNATURES: dict[str, list] = {
     "ls_rmsnorm_gateup_silu": [_p, _i64, _i64, _p, _f32, _p, _i64, _p, _p],
     "ls_down_residual": [_p, _i64, _i64, _p, _i64, _p, _p, _p],
     "ls_lmhead_argmax": [_p, _i64, _i64, _p, _f32, _p, _i64, _p, _p, _i64, _p],
+    "ls_lmhead_argmax_noalloc": [_p, _i64, _i64, _p, _f32, _p, _i64, _p, _p],
     "ls_lmhead_workspace_bytes": [_i64, _i64, ctypes.POINTER(_i64)],
     "ls_rmsnorm": [_p, _i64, _i64, _p, _f32, _p, _p],
     "ls_residual_add_f32": [_p, _p, _i64, _p, _p],
