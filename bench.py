@@ -66,6 +66,13 @@ def parse_args():
                     help="tensor-core (tcgen05) or CUDA-core streaming linears for the decode step")
     ap.add_argument("--parallel", choices=("tp", "replicas"), default="tp",
                     help="with N > 1 GPUs: tensor parallelism (one sequence) or independent replicas")
+    ap.add_argument("--batched", default="32",
+                    help="comma-separated batch sizes of the config-3 batched-decode section ('' to skip)")
+    ap.add_argument("--batched-cached", type=int, default=2048, help="cached positions per sequence (config 3)")
+    ap.add_argument("--batched-steps", type=int, default=128)
+    ap.add_argument("--no-verify", action="store_true", help="skip the config-4 speculative-verify section")
+    ap.add_argument("--allreduce", choices=("fused", "nccl"), default="fused",
+                    help="tensor parallelism: fused one-shot P2P all-reduce in the CUDA-core linears, or NCCL")
     return ap.parse_args()
 
 
@@ -237,6 +244,110 @@ def run_reference(args, world, rank):
 # native arm
 # ---------------------------------------------------------------------------
 
+def _timed(fn, steps: int, warmup: int, world: int) -> float:
+    """Seconds for ``steps`` calls of ``fn`` after ``warmup`` (CUDA events, max over ranks)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    barrier(world)
+    return max_over_ranks(ms, world) / 1000.0
+
+
+def run_batched(rt, comm, shard, batch: int, cached: int, steps: int, warmup: int, world: int, peaks) -> dict:
+    """``batch`` sequences with ``cached`` prompt positions each, greedy decode."""
+    from leanstack_b200.engine import DecodeEngine
+
+    g = QWEN3_4B
+    eng = DecodeEngine(rt, batch_size=batch, max_seq_len=cached + warmup + steps + 8, tp=comm, shard=shard)
+    eng.prefill(synth.token_ids((batch, cached), g.vocab_size, SEED, f"cfg3/prompt{batch}"))
+    eng.capture()
+    t = _timed(eng.decode_step, steps, warmup, world)
+    gl = eng.g
+    kv_bytes = batch * (cached + warmup + steps // 2) * gl.kv_bytes_per_token()
+    step_bytes = g.num_hidden_layers * gl.layer_weight_bytes() + eng.vocab_rows * g.hidden_size * 2 + kv_bytes
+    out = {"batch": batch, "cached_per_seq": cached, "steps": steps, "tok_per_s": batch * steps / t,
+           "ms_per_step": 1000.0 * t / steps, "linear_backend": eng.backend,
+           "step_bytes_per_gpu": step_bytes, "step_frac_of_hbm": step_bytes / (t / steps) / 1e9 / peaks["hbm_gbs"],
+           "kv_share_of_bytes": kv_bytes / step_bytes}
+    eng.graph = None
+    del eng
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_verify(rt, comm, shard, steps: int, warmup: int, world: int, peaks) -> dict:
+    """target verify at batch 16, k = 4 uniform proposals, 1024 cached (M = 80)."""
+    from leanstack_b200 import kernels as K
+    from leanstack_b200.engine import DecodeEngine
+
+    g = QWEN3_4B
+    B, k, cached = 16, 4, 1024
+    eng = DecodeEngine(rt, batch_size=B, max_seq_len=cached + (warmup + steps + 2) * (k + 1) + 8,
+                       linear_backend="tc", tp=comm, shard=shard)
+    eng.prefill(synth.token_ids((B, cached), g.vocab_size, SEED, "cfg4/prompt"))
+    props = synth.token_ids((warmup + steps + 1, B, k), g.vocab_size, SEED, "cfg4/proposals").to(rt.device)
+    inp = eng.verify_inputs(k)
+    it = iter(range(props.shape[0]))
+
+    def step():
+        inp[:, 1:].copy_(props[next(it)])
+        eng.verify_step(k)
+
+    step()  # capture
+    pos0 = None
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    pos0 = eng.kv.cache_pos.clone()
+    t = _timed(step, steps, 0, world)
+    committed = int((eng.kv.cache_pos - pos0).sum().item())
+    eng.sync_cursors()
+    # the dominant verify GEMM alone: gate_up + SiLU*up at M = 80 on tcgen05
+    gl = eng.g
+    m = B * (k + 1)
+    layer = rt.layers[0]
+    xs = eng.xn[:m]
+    reps = 8
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    K.gemm_tc(xs, layer.mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=eng.arenas.act[:m],
+              workspace=eng.tc_ws)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(reps):
+        for lay in rt.layers:
+            K.gemm_tc(xs, lay.mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=eng.arenas.act[:m],
+                      workspace=eng.tc_ws)
+    e1.record()
+    torch.cuda.synchronize()
+    per = e0.elapsed_time(e1) / 1000.0 / (reps * len(rt.layers))
+    w_bytes = 2 * gl.intermediate_size * g.hidden_size * 2
+    flops = 2.0 * m * 2 * gl.intermediate_size * g.hidden_size
+    out = {"batch": B, "proposal_len": k, "m": m, "cached_per_seq": cached, "steps": steps,
+           "verify_steps_per_s": steps / t, "ms_per_verify": 1000.0 * t / steps,
+           "positions_per_s": steps * m / t, "committed_tok_per_s": committed / t,
+           "proposals": "uniform random ids (accept rate ~0)",
+           "dominant_gemm": {"kernel": "gemm_tc_kernel<SILU_MUL> (gate_up + SiLU*up, M=80)", "us": per * 1e6,
+                             "gbs": w_bytes / per / 1e9, "hbm_frac": w_bytes / per / 1e9 / peaks["hbm_gbs"],
+                             "tflops": flops / per / 1e12,
+                             "tensor_frac": flops / per / 1e12 / peaks.get("bf16_tflops", 1663.3),
+                             "hbm_bound_tensor_frac": (peaks["hbm_gbs"] * 1e9 * flops / w_bytes) / 1e12
+                             / peaks.get("bf16_tflops", 1663.3)}}
+    for gph in eng.verify_graphs.values():
+        del gph
+    eng.verify_graphs.clear()
+    del eng
+    torch.cuda.empty_cache()
+    return out
+
 def run_ours(args, world, rank, local):
     from leanstack_b200 import kernels as K
     from leanstack_b200 import tp as tpm
@@ -252,6 +363,8 @@ def run_ours(args, world, rank, local):
     if tp_mode:
         rt, shard = tpm.materialize_tp_shard(g, tensors, rank, world, device=dev)
         comm = tpm.TPComm(rank, world)
+        if args.allreduce == "fused":
+            comm.enable_p2p(g.hidden_size)
     else:
         rt = materialize_from_tensors(g, tensors, device=dev, free_source=True)
         shard = comm = None
@@ -347,6 +460,14 @@ def run_ours(args, world, rank, local):
                 "step_frac": step_bytes / (ms_per_step / 1000.0) / 1e9 / peaks["hbm_gbs"],
                 "step_bytes": step_bytes}
 
+    # --- config 3 (batched decode) and config 4 (speculative verify) sections ---
+    extra = {}
+    for bs in [int(x) for x in args.batched.split(",") if x.strip()]:
+        extra[f"bs{bs}"] = run_batched(rt, comm, shard, bs, args.batched_cached, args.batched_steps, 4, world,
+                                       peaks)
+    if not args.no_verify:
+        extra["verify_cfg4"] = run_verify(rt, comm, shard, 64, 4, world, peaks)
+
     # --- CPU baseline (rank 0, N == 1 only) ---
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -365,7 +486,8 @@ def run_ours(args, world, rank, local):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights, uniform ids)",
             "config": {"workload": WORKLOAD, "model": "Qwen3-4B (random init)", "global_batch": seqs,
                        "seq_len": PROMPT, "max_seq": MAX_SEQ,
-                       "parallelism": (f"tp{world}" if tp_mode else f"replicas x{world}") if world > 1
+                       "parallelism": (f"tp{world}" + ("" if args.allreduce == "nccl" else " fused-allreduce")
+                                       if tp_mode else f"replicas x{world}") if world > 1
                        else "single GPU", "l2": "not flushed: each step streams 8.05 GB of weights (> 126 MB L2)",
                        "linear_backend": "persistent" if eng.persistent else eng.backend},
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
@@ -373,10 +495,13 @@ def run_ours(args, world, rank, local):
         }
         if tp_mode:
             line["collectives_per_step"] = eng.collectives_per_step()
+        line.update(extra)
         print(json.dumps(line), flush=True)
     barrier(world)
     eng.graph = None  # release the graph (it holds NCCL work) before the process group goes
     torch.cuda.synchronize()
+    if comm is not None:
+        comm.close()
     return 0
 
 

@@ -50,6 +50,21 @@ typedef enum ls_status {
   LS_ERR_NOT_SUPPORTED = 8      /* feature not available on this device */
 } ls_status;
 
+/* Exchange regions of the fused one-shot tensor-parallel all-reduce: every
+ * rank's region (its own at index `rank`), mapped into this process with
+ * ls_ipc_open.  Region layout: per-(source rank, CTA) flags, per-CTA call
+ * counters, then two slots of [world][max_rows][width] fp32 partials. */
+#define LS_MAX_TP_RANKS 8
+typedef struct ls_p2p_exchange {
+  void* peer[LS_MAX_TP_RANKS];
+  int32_t rank;
+  int32_t world;
+  int32_t max_ctas;
+  int32_t max_rows;
+  int64_t width;
+  unsigned long long* trace;  /* optional (NULL): per CTA 4 globaltimer stamps of the last call, for profiling */
+} ls_p2p_exchange;
+
 /* Epilogues of ls_linear_bf16. */
 typedef enum ls_epilogue {
   LS_EPI_STORE = 0,     /* out = bf16(W x) */
@@ -243,6 +258,47 @@ int ls_decode_step(const ls_decode_layer* layers, int64_t num_layers, int64_t hi
                    void* qkv, void* attn, void* act, void* workspace, int64_t workspace_bytes, ls_stream_t stream);
 int ls_decode_step_workspace_bytes(int64_t num_kv_heads, int64_t* bytes);
 
+/* Fused one-shot all-reduce over NVLink peer memory (no counterpart in the
+ * reference, which runs on one GPU; it replaces the NCCL all-reduce of the
+ * tensor-parallel row-split o_proj / down_proj, whose reference-side linear +
+ * residual is src/leanstack/runtime/qwen_explicit.py:1262 and :819-829).
+ * out = bf16(residual + bf16(sum over ranks of W_r x_r)), m <= 8 rows: each CTA
+ * computes its slice of the fp32 partial, stores it into every rank's region
+ * (plain peer stores), raises its flag on every rank (release, system scope),
+ * waits for the same CTA of every rank (acquire; gives up after ~2 s with
+ * LS_ERR_TIMEOUT in the device error flag) and sums the partials in rank
+ * order, so every rank holds the same bits.  All ranks must issue the same
+ * sequence of these calls with the same m, and each rank must own its GPU. */
+int ls_p2p_region_bytes(int64_t max_rows, int64_t width, int64_t max_ctas, int64_t* bytes);
+int ls_p2p_alloc(int64_t bytes, void** region);   /* cudaMalloc + zero, at set-up */
+int ls_p2p_free(void* region);
+int ls_ipc_get_handle(void* region, void* handle64);  /* 64-byte cudaIpcMemHandle_t */
+int ls_ipc_open(const void* handle64, void** region);
+int ls_ipc_close(void* region);
+int ls_linear_allreduce_residual(const void* x, int64_t m, int64_t k, const void* w, int64_t n,
+                                 const void* residual, void* out, const ls_p2p_exchange* ex, ls_stream_t stream);
+/* Latency probe of the exchange: `iters` flag round trips between rank 0 and
+ * rank 1 through two 4-byte words (my_flag in this rank's region, peer_flag in
+ * the other's, both zero and unused by the all-reduce), one thread, bounded
+ * waits.  times_dev (device, 2 x u64): total ns, and 1 if a wait gave up. */
+int ls_p2p_pingpong(void* my_flag, void* peer_flag, int rank, int iters, unsigned long long* times_dev,
+                    ls_stream_t stream);
+
+/* Skinny-M linears on the tensor cores over pre-tiled weights (mma.sync
+ * m16n8k16 with the activations as A, 1 <= m <= 8).  Same contract as
+ * ls_linear_bf16 (epilogues LS_EPI_STORE / RESIDUAL / SILU_MUL, optional
+ * RMSNorm prologue; reference: qwen_explicit.py:913-949, :1247-1272) but the
+ * weight is first rewritten once by ls_gemv_tile_weight into 512-byte tiles
+ * of 8 rows x 32 k in MMA fragment order (for SILU_MUL, gate and up rows of
+ * the same 8 outputs adjacent).  k must be a multiple of 32, n_rows of 8 (16
+ * for SILU_MUL).  workspace: ls_gemv_workspace_bytes() bytes, zero-filled once
+ * (the kernel leaves it zeroed).  Deterministic: no result depends on timing. */
+int ls_gemv_tile_weight(const void* w, int64_t n_rows, int64_t k, int silu, void* out, ls_stream_t stream);
+int ls_gemv_workspace_bytes(int64_t m, int64_t n_rows, int epilogue, int64_t* bytes);
+int ls_gemv_bf16(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w_tiled,
+                 int64_t n_rows, int epilogue, const void* residual, void* out, void* workspace,
+                 int64_t workspace_bytes, ls_stream_t stream);
+
 /* Tensor-parallel greedy head.  Each rank holds a vocab shard (rows
  * [vocab_offset, vocab_offset + vocab_rows) of lm_head) and writes, per row, an
  * int64 key of its best (bf16 logit, vocab id): a signed MAX over the ranks'
@@ -270,6 +326,22 @@ int ls_rmsnorm(const void* x, int64_t m, int64_t n, const void* w, float eps, vo
  * after a step, the device-side counterpart of the reference's host cursor
  * bookkeeping (src/leanstack/runtime/kv_cache.py:239-245, :298-318). */
 int ls_advance_cursors(int32_t* cache_pos, const int32_t* delta, int64_t batch, int64_t q_len, ls_stream_t stream);
+
+/* Greedy-exact accept / reject after a speculative verify pass, on the device
+ * (experiments/models/qwen_explicit_runtime_loop.py:804-862).  ids: int64
+ * [batch, k+1] = [current, d1..dk] per sequence (the verify input); verdict:
+ * int64 [batch, k+1], the target's greedy token after each input position.
+ * Per sequence: n = length of the prefix with d(i+1) == verdict[i]; the next
+ * current token is verdict[n] (correction, or bonus when n == k), written to
+ * next_ids[b] and to ids[b][0]; accepted[b] = n; cache_pos[b] += n + 1 (the
+ * verifier cursor rollback of :836-838); draft_cache_pos[b] -= k - min(n+1, k)
+ * (the draft consumed current, d1..d(k-1) while proposing and keeps current
+ * plus the accepted proposals, :833); the committed tokens d1..dn, next are
+ * appended to out_tokens[b][out_len[b]...] up to out_cap (:856-866).  Every
+ * output pointer may be NULL. */
+int ls_spec_accept(int64_t* ids, const int64_t* verdict, int64_t batch, int64_t k, int64_t* next_ids,
+                   int32_t* accepted, int32_t* cache_pos, int32_t* draft_cache_pos, int64_t* out_tokens,
+                   int32_t* out_len, int64_t out_cap, ls_stream_t stream);
 
 #ifdef __cplusplus
 }

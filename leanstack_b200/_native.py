@@ -41,6 +41,16 @@ class LeanB200Error(RuntimeError):
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _f32 = ctypes.c_float
+
+MAX_TP_RANKS = 8
+
+
+class P2PExchangeDesc(ctypes.Structure):
+    """``ls_p2p_exchange`` of include/leanb200.h."""
+
+    _fields_ = [("peer", ctypes.c_void_p * MAX_TP_RANKS), ("rank", ctypes.c_int32), ("world", ctypes.c_int32),
+                ("max_ctas", ctypes.c_int32), ("max_rows", ctypes.c_int32), ("width", ctypes.c_int64),
+                ("trace", ctypes.c_void_p)]
 _int = ctypes.c_int
 
 # name -> argtypes (all return int status unless listed in _RESTYPES)
@@ -63,6 +73,18 @@ SIGNATURES: dict[str, list] = {
     "ls_lmhead_workspace_bytes": [_i64, _i64, ctypes.POINTER(_i64)],
     "ls_rmsnorm": [_p, _i64, _i64, _p, _f32, _p, _p],
     "ls_residual_add_f32": [_p, _p, _i64, _p, _p],
+    "ls_spec_accept": [_p, _p, _i64, _i64, _p, _p, _p, _p, _p, _p, _i64, _p],
+    "ls_gemv_tile_weight": [_p, _i64, _i64, ctypes.c_int, _p, _p],
+    "ls_gemv_workspace_bytes": [_i64, _i64, ctypes.c_int, _p],
+    "ls_gemv_bf16": [_p, _i64, _i64, _p, _f32, _p, _i64, ctypes.c_int, _p, _p, _p, _i64, _p],
+    "ls_p2p_region_bytes": [_i64, _i64, _i64, _p],
+    "ls_p2p_alloc": [_i64, _p],
+    "ls_p2p_free": [_p],
+    "ls_ipc_get_handle": [_p, _p],
+    "ls_ipc_open": [_p, _p],
+    "ls_ipc_close": [_p],
+    "ls_linear_allreduce_residual": [_p, _i64, _i64, _p, _i64, _p, _p, _p, _p],
+    "ls_p2p_pingpong": [_p, _p, ctypes.c_int, ctypes.c_int, _p, _p],
     "ls_lmhead_argmax_keys": [_p, _i64, _i64, _p, _f32, _p, _i64, _i64, _p, _p, _i64, _p],
     "ls_argmax_rows_keys": [_p, _i64, _i64, _i64, _p, _p, _i64, _p],
     "ls_argmax_keys_to_ids": [_p, _i64, _p, _p],

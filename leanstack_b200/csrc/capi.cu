@@ -126,6 +126,40 @@ __global__ void advance_cursors_kernel(int* cache_pos, const int* delta, int bat
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < batch) cache_pos[b] += delta ? delta[b] : q_len;
 }
+// Greedy-exact accept / reject of one speculative verify step, per sequence b:
+// ids[b] = [current, d1..dk] went through the target, verdict[b][i] is the
+// target's greedy token after input position i.  Accept the longest prefix of
+// proposals with d(i+1) == verdict[i]; the next current token is the target's
+// token after the last accepted position (the correction, or the bonus when
+// all k agree); the cursor keeps current + the accepted proposals.
+// The draft model consumed current, d1..d(k-1) while proposing; it keeps
+// current and the accepted proposals: min(n + 1, k) of its k new positions.
+// The tokens the cycle commits (d1..dn, then the next current) are appended to
+// a per-sequence output log of capacity out_cap.
+__global__ void spec_accept_kernel(int64_t* ids, const int64_t* verdict, int batch, int k, int64_t* next_ids,
+                                   int32_t* accepted, int32_t* cache_pos, int32_t* draft_cache_pos,
+                                   int64_t* out_tokens, int32_t* out_len, int out_cap) {
+  grid_dep_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  int64_t* in = ids + (size_t)b * (k + 1);
+  const int64_t* v = verdict + (size_t)b * (k + 1);
+  int n = 0;
+  while (n < k && in[1 + n] == v[n]) ++n;
+  const int64_t next = v[n];
+  if (next_ids) next_ids[b] = next;
+  if (accepted) accepted[b] = n;
+  if (cache_pos) cache_pos[b] += n + 1;
+  if (draft_cache_pos) draft_cache_pos[b] -= k - min(n + 1, k);
+  if (out_tokens && out_len) {
+    int len = out_len[b];
+    int64_t* o = out_tokens + (size_t)b * out_cap;
+    for (int i = 0; i < n && len < out_cap; ++i) o[len++] = in[1 + i];
+    if (len < out_cap) o[len++] = next;
+    out_len[b] = len;
+  }
+  in[0] = next;  // the next step's first input token
+}
 }  // namespace lsb
 
 namespace lsb_host {
@@ -553,6 +587,21 @@ int ls_advance_cursors(int32_t* cache_pos, const int32_t* delta, int64_t batch, 
       cache_pos, delta, (int)batch, (int)q_len);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "advance_cursors launch: %s", cudaGetErrorString(e));
+}
+
+int ls_spec_accept(int64_t* ids, const int64_t* verdict, int64_t batch, int64_t k, int64_t* next_ids,
+                   int32_t* accepted, int32_t* cache_pos, int32_t* draft_cache_pos, int64_t* out_tokens,
+                   int32_t* out_len, int64_t out_cap, ls_stream_t stream) {
+  LS_REQUIRE(ids && verdict && batch > 0 && batch <= (1 << 20) && k >= 1 && k <= 64, LS_ERR_INVALID_ARGUMENT,
+             "ls_spec_accept: bad arguments");
+  LS_REQUIRE(!(out_tokens || out_len) || (out_tokens && out_len && out_cap > 0 && out_cap < (1 << 30)),
+             LS_ERR_INVALID_ARGUMENT, "ls_spec_accept: output log needs out_tokens, out_len and out_cap > 0");
+  const int threads = 128;
+  lsb::spec_accept_kernel<<<(unsigned)((batch + threads - 1) / threads), threads, 0, (cudaStream_t)stream>>>(
+      ids, verdict, (int)batch, (int)k, next_ids, accepted, cache_pos, draft_cache_pos, out_tokens, out_len,
+      (int)out_cap);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "spec_accept launch: %s", cudaGetErrorString(e));
 }
 
 }  // extern "C"

@@ -164,6 +164,47 @@ __host__ __device__ __forceinline__ int64_t argmax_key_id(int64_t key) {
   return (int64_t)(0xFFFFFFFFu - (uint32_t)((uint64_t)key & 0xFFFFFFFFull));
 }
 
+// ---- fused tensor-parallel all-reduce: exchange region layout ----
+struct P2PExchange {
+  unsigned char* peer[LS_MAX_TP_RANKS];
+  int rank, world, max_ctas, max_rows;
+  int width;
+  unsigned long long* trace;  // optional: [max_ctas][4] timestamps (main loop done, pushed, flags seen, end)
+};
+__host__ __device__ __forceinline__ size_t p2p_ctr_offset(int max_ctas) {
+  return ((size_t)LS_MAX_TP_RANKS * max_ctas * 4 + 255) / 256 * 256;
+}
+__host__ __device__ __forceinline__ size_t p2p_recv_offset(int max_ctas) {
+  return p2p_ctr_offset(max_ctas) + ((size_t)max_ctas * 4 + 255) / 256 * 256;
+}
+// Receive area: 2 slots x [LS_MAX_TP_RANKS][max_rows][width] pairs {fp32 bits, call number}.
+__host__ __device__ __forceinline__ size_t p2p_region_bytes(int max_ctas, int max_rows, int width) {
+  return p2p_recv_offset(max_ctas) + (size_t)2 * LS_MAX_TP_RANKS * max_rows * width * 8;
+}
+constexpr unsigned long long kP2PWaitNs = 2000000000ull;  // bounded flag wait: 2 s
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// One 8-byte store / load that peers see whole: the value travels with its call number.
+__device__ __forceinline__ void st_pair_sys(uint2* p, uint32_t a, uint32_t b) {
+  asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ uint2 ld_pair_sys(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 }  // namespace lsb
 
 // Host-side helpers shared by the C-ABI translation units.

@@ -29,7 +29,7 @@ constexpr int kLinWarps = kLinThreads / 32;
 constexpr int kGranule = 256;  // bf16 elements per warp-wide 512-byte load
 constexpr uint32_t kPrefetchBytes = 64 * 1024;  // per CTA and weight range, issued before the PDL wait
 
-enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3, EPI_STORE_F32 = 4 };
+enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3, EPI_STORE_F32 = 4, EPI_AR_RESIDUAL = 5 };
 
 struct LinearParams {
   const __nv_bfloat16* x;      // [M, K]
@@ -50,6 +50,10 @@ struct LinearParams {
   int64_t* out_ids;      // [M]: winning row index, or its argmax_key when out_keys
   int64_t id_offset;     // added to the winning row index (vocab shard offset)
   int out_keys;
+  // EPI_AR_RESIDUAL: tensor-parallel exchange regions
+  P2PExchange ex;
+  int* err;
+  int pf_rows;  // > 0: each warp keeps its weight rows this many rows ahead in L2 (bulk prefetch)
 };
 
 template <int M>
@@ -84,7 +88,22 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
   // Weights do not depend on the previous kernel: start pulling this CTA's
   // first weight bytes into L2, let the next kernel launch, and only then wait
   // (PDL) for the activations the previous kernel writes.
-  if (tid == 0 && P > 0) {
+  if (p.pf_rows > 0) {
+    // Each warp starts its first pf_rows rows toward L2; the main loop keeps that distance.
+    const int total_g = R * ((K + kGranule - 1) / kGranule);
+    const int gb = (int)(((int64_t)total_g * warp) / kLinWarps), ge = (int)(((int64_t)total_g * (warp + 1)) / kLinWarps);
+    const int gpr0 = (K + kGranule - 1) / kGranule;
+    if (lane == 0 && gb < ge) {
+      for (int ta = gb / gpr0; ta <= min((ge - 1) / gpr0, gb / gpr0 + p.pf_rows - 1); ++ta) {
+        const int ra = (RPU == 2) ? ((ta < P) ? (u0 + ta) : (u0 + (ta - P) + p.N / 2)) : (u0 + ta);
+        const int k0 = (ta == gb / gpr0) ? (gb - ta * gpr0) * kGranule : 0;
+        const int k1 = (ta == (ge - 1) / gpr0) ? min(K, (ge - ta * gpr0) * kGranule) : K;
+        const uint32_t bytes = (uint32_t)((k1 - k0) * 2) & ~15u;
+        const char* base = reinterpret_cast<const char*>(p.w + (size_t)ra * K + k0);
+        for (uint32_t off = 0; off < bytes; off += 16384) prefetch_l2(base + off, min(16384u, bytes - off));
+      }
+    }
+  } else if (tid == 0 && P > 0) {
     const size_t range = (size_t)P * K * 2;
     const uint32_t pf = (uint32_t)(range < kPrefetchBytes ? range : kPrefetchBytes);
     const char* base = reinterpret_cast<const char*>(p.w + (size_t)u0 * K);
@@ -96,6 +115,12 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
   }
   grid_dep_launch();
   grid_dep_wait();
+  __shared__ uint32_t s_epoch;
+  if (EPI == EPI_AR_RESIDUAL && tid == 0) {  // per-CTA call counter of the fused all-reduce
+    uint32_t* ctr = reinterpret_cast<uint32_t*>(p.ex.peer[p.ex.rank] + p2p_ctr_offset(p.ex.max_ctas)) + blockIdx.x;
+    s_epoch = *ctr + 1u;
+    *ctr = s_epoch;
+  }
 
   // ---- prologue: (optional) RMSNorm of the M activation rows into smem ----
   const int kvec = K >> 3;  // 16-byte vectors per activation row
@@ -166,6 +191,18 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
     if (RPU == 2) row = (t < P) ? (u0 + t) : (u0 + (t - P) + half_rows);
     else row = u0 + t;
     const __nv_bfloat16* wrow = p.w + (size_t)row * K;
+    if (p.pf_rows > 0 && lane == 0) {  // keep this warp's stream pf_rows rows ahead in L2
+      const int ta = t + p.pf_rows;
+      const int t_last = (g_end - 1) / gpr;
+      if (ta <= t_last) {
+        const int ra = (RPU == 2) ? ((ta < P) ? (u0 + ta) : (u0 + (ta - P) + half_rows)) : (u0 + ta);
+        const int k0 = (ta == t_first) ? (g_begin - ta * gpr) * kGranule : 0;
+        const int k1 = (ta == t_last) ? min(K, (g_end - ta * gpr) * kGranule) : K;
+        const uint32_t bytes = (uint32_t)((k1 - k0) * 2) & ~15u;
+        const char* base = reinterpret_cast<const char*>(p.w + (size_t)ra * K + k0);
+        for (uint32_t off = 0; off < bytes; off += 16384) prefetch_l2(base + off, min(16384u, bytes - off));
+      }
+    }
     float a[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) a[m] = 0.f;
@@ -219,6 +256,53 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
     for (int i = tid; i < M * P; i += kLinThreads) {
       const int m = i / P, t = i - m * P;
       reinterpret_cast<float*>(p.out)[(size_t)m * p.N + u0 + t] = row_sum(m, t);
+    }
+  } else if (EPI == EPI_AR_RESIDUAL) {
+    // Fused one-shot all-reduce of the row-split partials (see ls_linear_allreduce_residual).
+    // Every fp32 partial travels to every rank together with this CTA's call
+    // number in one 8-byte store; a reader polls its own elements until the
+    // call number matches, so no fence, flag or barrier sits between the push
+    // and the sum.
+    const P2PExchange& ex = p.ex;
+    unsigned char* mine = ex.peer[ex.rank];
+    const uint32_t epoch = s_epoch;  // this CTA's call number, read in the prologue
+    unsigned long long* trace = ex.trace ? ex.trace + (size_t)blockIdx.x * 4 : nullptr;
+    if (trace && tid == 0) trace[0] = global_timer_ns();
+    const size_t slot_base = (size_t)(epoch & 1u) * LS_MAX_TP_RANKS * ex.max_rows * ex.width;
+    const size_t recv_off = p2p_recv_offset(ex.max_ctas);
+    for (int i = tid; i < M * P; i += kLinThreads) {
+      const int m = i / P, t = i - m * P;
+      const float v = row_sum(m, t);
+      const size_t off = slot_base + ((size_t)ex.rank * ex.max_rows + m) * ex.width + u0 + t;
+      for (int q = 0; q < ex.world; ++q)
+        st_pair_sys(reinterpret_cast<uint2*>(ex.peer[q] + recv_off) + off, __float_as_uint(v), epoch);
+    }
+    if (trace && tid == 0) trace[1] = global_timer_ns();
+    const uint2* recv = reinterpret_cast<const uint2*>(mine + recv_off) + slot_base;
+    for (int i = tid; i < M * P; i += kLinThreads) {
+      const int m = i / P, t = i - m * P;
+      float y = 0.f;
+      for (int q = 0; q < ex.world; ++q) {
+        const uint2* src = recv + ((size_t)q * ex.max_rows + m) * ex.width + u0 + t;
+        uint2 v = ld_pair_sys(src);
+        if (v.y != epoch) {
+          const unsigned long long t0 = global_timer_ns();
+          do {
+            v = ld_pair_sys(src);
+            if (v.y != epoch && global_timer_ns() - t0 > kP2PWaitNs) {
+              raise_device_error(p.err, LS_ERR_TIMEOUT | (0x30 << 8));
+              break;
+            }
+          } while (v.y != epoch);
+        }
+        y += __uint_as_float(v.x);
+      }
+      const size_t o = (size_t)m * p.N + u0 + t;
+      p.out[o] = f_to_bf16(bf16_to_f(p.residual[o]) + round_bf16(y));
+    }
+    if (trace && tid == 0) {
+      trace[2] = global_timer_ns();
+      trace[3] = trace[2];
     }
   } else if (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
     for (int i = tid; i < M * P; i += kLinThreads) {
@@ -314,8 +398,21 @@ using namespace lsb;
 // keep ~128 KB per SM in flight, what the measured 6 TB/s needs (one CTA per
 // SM reached only 4.5 TB/s on the lm_head).  m > 4 needs more registers and
 // runs one CTA per SM.
+// LEANB200_LIN_PF=<rows>: one CTA per SM that keeps its weight stream <rows>
+// rows ahead in L2 (leaving room on the SM for the next kernel's CTA, which
+// starts its own prefetch under PDL); unset: two CTAs per SM for m <= 4.
+static int lin_pf_rows() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("LEANB200_LIN_PF");
+    v = e ? atoi(e) : 0;
+    if (v < 0) v = 0;
+  }
+  return v;
+}
+
 static int linear_grid(int units, int m) {
-  const int g = (m <= 4 ? 2 : 1) * sm_count();
+  const int g = (lin_pf_rows() == 0 && m <= 4 ? 2 : 1) * sm_count();
   return units < g ? units : g;
 }
 
@@ -391,7 +488,8 @@ static bool stream_path_enabled() {
 static int launch_linear_impl(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w,
                               int64_t n, int epi, const void* residual, void* out, cudaStream_t stream,
                               float* part_val, int* part_idx, unsigned int* counter, int64_t* out_ids,
-                              int grid_override, int64_t id_offset, bool out_keys) {
+                              int grid_override, int64_t id_offset, bool out_keys,
+                              const P2PExchange* ex = nullptr) {
   if (!x || !w || (epi != EPI_ARGMAX && !out)) return set_error(LS_ERR_INVALID_ARGUMENT, "linear: null pointer");
   if (m < 1 || m > 8) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "linear: m=%lld outside 1..8", (long long)m);
   if (k < 8 || n < 1 || k > 32768 || n > (int64_t)1 << 30)
@@ -399,7 +497,9 @@ static int launch_linear_impl(const void* x, int64_t m, int64_t k, const void* n
   if (k % 8) return set_error(LS_ERR_MISALIGNED, "linear: k=%lld not a multiple of 8", (long long)k);
   if (!aligned16(x) || !aligned16(w) || (norm_w && !aligned16(norm_w)))
     return set_error(LS_ERR_MISALIGNED, "linear: x/w/norm_w must be 16-byte aligned");
-  if (epi == EPI_RESIDUAL && !residual) return set_error(LS_ERR_INVALID_ARGUMENT, "linear: residual is null");
+  if ((epi == EPI_RESIDUAL || epi == EPI_AR_RESIDUAL) && !residual)
+    return set_error(LS_ERR_INVALID_ARGUMENT, "linear: residual is null");
+  if (epi == EPI_AR_RESIDUAL && (!ex || norm_w)) return set_error(LS_ERR_INVALID_ARGUMENT, "linear: bad all-reduce call");
   if (epi == EPI_SILU_MUL && (n % 2)) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "linear: gate_up rows odd");
   if (stream_path_enabled() && epi <= EPI_ARGMAX && !out_keys && id_offset == 0 && stream_supported(m, k, n, epi))
     return launch_linear_stream(x, m, k, norm_w, eps, w, n, epi, residual, out, stream, part_val, part_idx, counter,
@@ -424,6 +524,16 @@ static int launch_linear_impl(const void* x, int64_t m, int64_t k, const void* n
   p.out_ids = out_ids;
   p.id_offset = id_offset;
   p.out_keys = out_keys ? 1 : 0;
+  p.err = device_error_ptr();
+  p.pf_rows = lin_pf_rows() > 0 ? (lin_pf_rows() * 2560 + (int)k - 1) / (int)k : 0;  // scale with row length
+  if (epi == EPI_AR_RESIDUAL) {
+    p.ex = *ex;
+    const int g_ar = grid_override > 0 ? grid_override : linear_grid(p.units, (int)m);
+    if (g_ar > ex->max_ctas || m > ex->max_rows || n != ex->width)
+      return set_error(LS_ERR_UNSUPPORTED_SHAPE, "linear all-reduce: grid %d / m %lld / n %lld beyond the exchange "
+                       "region (%d CTAs, %d rows, width %d)", g_ar, (long long)m, (long long)n, ex->max_ctas,
+                       ex->max_rows, ex->width);
+  }
   const size_t smem = linear_smem((int)m, (int)k, p.max_segs);
   if (smem > 200 * 1024)
     return set_error(LS_ERR_UNSUPPORTED_SHAPE, "linear: m=%lld k=%lld needs %zu B of shared memory", (long long)m,
@@ -440,6 +550,7 @@ static int launch_linear_impl(const void* x, int64_t m, int64_t k, const void* n
                                  : dispatch_m<EPI_ARGMAX, false>((int)m, p, grid, smem, stream);
     case EPI_STORE_F32: return norm ? dispatch_m<EPI_STORE_F32, true>((int)m, p, grid, smem, stream)
                                     : dispatch_m<EPI_STORE_F32, false>((int)m, p, grid, smem, stream);
+    case EPI_AR_RESIDUAL: return dispatch_m<EPI_AR_RESIDUAL, false>((int)m, p, grid, smem, stream);
     default: return set_error(LS_ERR_INVALID_ARGUMENT, "linear: unknown epilogue %d", epi);
   }
 }
@@ -457,6 +568,12 @@ int launch_lmhead_keys(const void* h, int64_t m, int64_t k, const void* norm_w, 
                        int* part_idx, unsigned int* counter, int grid) {
   return launch_linear_impl(h, m, k, norm_w, eps, w, rows, EPI_ARGMAX, nullptr, nullptr, stream, part_val, part_idx,
                             counter, out_keys, grid, vocab_offset, true);
+}
+
+int launch_linear_allreduce(const void* x, int64_t m, int64_t k, const void* w, int64_t n, const void* residual,
+                            void* out, const P2PExchange* ex, cudaStream_t stream) {
+  return launch_linear_impl(x, m, k, nullptr, 0.f, w, n, EPI_AR_RESIDUAL, residual, out, stream, nullptr, nullptr,
+                            nullptr, nullptr, 0, 0, false, ex);
 }
 
 int lmhead_grid(int64_t vocab, int64_t m) { return linear_grid((int)vocab, (int)m); }

@@ -51,7 +51,7 @@ def resolve_backend(backend: str, batch_size: int) -> str:
 class DecodeEngine:
     def __init__(self, runtime: QwenSemanticStackRuntime, batch_size: int, max_seq_len: int,
                  max_tokens_per_step: int | None = None, use_graph: bool = True, linear_backend: str = "auto",
-                 tp: TPComm | None = None, shard: TPShard | None = None):
+                 tp: TPComm | None = None, shard: TPShard | None = None, gemv_tiles: bool = False):
         if runtime.final_norm_weight is None or runtime.lm_head_weight is None:
             raise ValueError("the engine needs the output head (include_output_head=True)")
         self.tp = tp if (tp is not None and tp.world > 1) else None
@@ -95,15 +95,35 @@ class DecodeEngine:
                       (batch_size, g.hidden_size, self.vocab_rows, K.EPI_STORE)]
             self.tc_ws = torch.zeros(max(K.gemm_workspace_bytes(*s_) for s_ in shapes), device=dev, dtype=torch.uint8)
             self.xn = torch.zeros(T, g.hidden_size, device=dev, dtype=runtime.dtype)
-            self.logits = torch.zeros(batch_size, self.vocab_rows, device=dev, dtype=runtime.dtype)
-            self.lm_ws = torch.zeros(K.argmax_workspace_bytes(batch_size, self.vocab_rows), device=dev,
-                                     dtype=torch.uint8)
+            self.logits = torch.zeros(T, self.vocab_rows, device=dev, dtype=runtime.dtype)
+            self.lm_ws = torch.zeros(K.argmax_workspace_bytes(T, self.vocab_rows), device=dev, dtype=torch.uint8)
         else:
-            self.lm_ws = torch.zeros(K.lmhead_workspace_bytes(batch_size, self.vocab_rows), device=dev,
+            self.lm_ws = torch.zeros(K.lmhead_workspace_bytes(self.T, self.vocab_rows), device=dev,
                                      dtype=torch.uint8)
+        # Optional: tensor-core GEMV over pre-tiled weights for the CUDA-core
+        # backend's linears (an extra copy of the layer weights in the tile
+        # layout).  Off by default while it streams slower than the CUDA-core
+        # kernels.
+        self.tiles = None
+        if self.backend == "cuda_core" and gemv_tiles and self._gemv_shapes_ok(g):
+            self.tiles = []
+            for layer in runtime.layers:
+                att, mlp = layer.attention, layer.mlp
+                self.tiles.append({"qkv": K.gemv_tile_weight(att.qkv_proj_weight),
+                                   "gu": K.gemv_tile_weight(mlp.gate_up_proj_weight, silu=True),
+                                   "o": None if self.tp is not None else K.gemv_tile_weight(att.o_proj_weight),
+                                   "down": None if self.tp is not None else K.gemv_tile_weight(mlp.down_proj_weight)})
+            shapes = [(self.T, g.qkv_dim, K.EPI_STORE), (self.T, g.hidden_size, K.EPI_RESIDUAL),
+                      (self.T, 2 * g.intermediate_size, K.EPI_SILU_MUL)]
+            self.gv_ws = torch.zeros(max(K.gemv_workspace_bytes(*s_) for s_ in shapes), device=dev, dtype=torch.uint8)
         if self.tp is not None:
             self.part = torch.zeros(self.T, g.hidden_size, device=dev, dtype=torch.float32)
-            self.keys = torch.zeros(batch_size, device=dev, dtype=torch.int64)
+            self.keys = torch.zeros(self.T, device=dev, dtype=torch.int64)
+        # speculative verify: the target's token after every input position, and per-sequence results
+        self.verdict = torch.zeros(self.T, device=dev, dtype=torch.int64)
+        self.next_ids = torch.zeros(batch_size, device=dev, dtype=torch.int64)
+        self.accepted = torch.zeros(batch_size, device=dev, dtype=torch.int32)
+        self.verify_graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.use_graph = use_graph
         self.graph: torch.cuda.CUDAGraph | None = None
         if self.persistent:
@@ -119,9 +139,22 @@ class DecodeEngine:
             self.ds_ws = torch.zeros(K.decode_step_workspace_bytes(g.num_key_value_heads), device=dev,
                                      dtype=torch.uint8)
 
+    @staticmethod
+    def _gemv_shapes_ok(g) -> bool:
+        sms = K.sm_count()
+        dims = [(g.qkv_dim, g.hidden_size, 1), (g.hidden_size, g.q_dim, 1), (g.intermediate_size, g.hidden_size, 2),
+                (g.hidden_size, g.intermediate_size, 1)]
+        return all(k % 32 == 0 and n % 8 == 0 and (n // 8) * (k // 32) >= 2 * sms for n, k, _ in dims)
+
     # ------------------------------------------------------------------
-    def _forward(self, q_len: int, head: bool) -> None:
-        """Enqueue one step of ``q_len`` tokens per sequence on the current stream."""
+    def _forward(self, q_len: int, head, advance: bool = True) -> None:
+        """Enqueue one step of ``q_len`` tokens per sequence on the current stream.
+
+        ``head``: falsy (no head), ``True`` / ``"last"`` (greedy token of each
+        sequence's last position into ``ids[:B]``) or ``"all"`` (greedy token
+        after every position into ``verdict[:m]``, the verify pass).
+        ``advance``: move the device cursors by ``q_len`` at the end.
+        """
         B, g, a, rt = self.B, self.g, self.arenas, self.rt
         m = B * q_len
         eps = g.rms_norm_eps
@@ -130,9 +163,14 @@ class DecodeEngine:
         K.embed_gather(a.ids[:m], rt.embed_tokens_weight, out=a.x[:m])
         for li, layer in enumerate(rt.layers):
             att, mlp = layer.attention, layer.mlp
-            if tc:
-                K.rmsnorm(a.x[:m], layer.input_layernorm_weight, eps, out=self.xn[:m])
-                K.gemm_tc(self.xn[:m], att.qkv_proj_weight, out=a.qkv[:m], workspace=self.tc_ws)
+            tl = self.tiles[li] if self.tiles is not None else None
+            if tc or tl is not None:
+                if tl is not None:
+                    K.gemv(a.x[:m], tl["qkv"], norm_w=layer.input_layernorm_weight, eps=eps, out=a.qkv[:m],
+                           workspace=self.gv_ws)
+                else:
+                    K.rmsnorm(a.x[:m], layer.input_layernorm_weight, eps, out=self.xn[:m])
+                    K.gemm_tc(self.xn[:m], att.qkv_proj_weight, out=a.qkv[:m], workspace=self.tc_ws)
                 K.qk_norm_rope(a.qkv[:m], B, q_len, g.num_attention_heads, g.num_key_value_heads, g.head_dim,
                                att.q_norm_weight, att.k_norm_weight, self.cos, self.sin, eps=eps,
                                cache_pos=kv.cache_pos, k_cache=kv.key_cache[li], v_cache=kv.value_cache[li],
@@ -148,7 +186,10 @@ class DecodeEngine:
                                cache_pos=kv.cache_pos, out=a.attn[:m], workspace=self.attn_ws)
             if self.tp is not None:
                 self._row_split(a.attn[:m], att.o_proj_weight, a.x[:m], a.h[:m], tc)
-                if tc:
+                if tl is not None:
+                    K.gemv(a.h[:m], tl["gu"], norm_w=layer.post_attention_layernorm_weight, eps=eps,
+                           epilogue=K.EPI_SILU_MUL, out=a.act[:m], workspace=self.gv_ws)
+                elif tc:
                     K.rmsnorm(a.h[:m], layer.post_attention_layernorm_weight, eps, out=self.xn[:m])
                     K.gemm_tc(self.xn[:m], mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=a.act[:m],
                               workspace=self.tc_ws)
@@ -156,6 +197,13 @@ class DecodeEngine:
                     K.gateup_silu(a.h[:m], layer.post_attention_layernorm_weight, mlp.gate_up_proj_weight, eps,
                                   out=a.act[:m])
                 self._row_split(a.act[:m], mlp.down_proj_weight, a.h[:m], a.x[:m], tc)
+            elif tl is not None:
+                K.gemv(a.attn[:m], tl["o"], epilogue=K.EPI_RESIDUAL, residual=a.x[:m], out=a.h[:m],
+                       workspace=self.gv_ws)
+                K.gemv(a.h[:m], tl["gu"], norm_w=layer.post_attention_layernorm_weight, eps=eps,
+                       epilogue=K.EPI_SILU_MUL, out=a.act[:m], workspace=self.gv_ws)
+                K.gemv(a.act[:m], tl["down"], epilogue=K.EPI_RESIDUAL, residual=a.h[:m], out=a.x[:m],
+                       workspace=self.gv_ws)
             elif tc:
                 K.gemm_tc(a.attn[:m], att.o_proj_weight, epilogue=K.EPI_RESIDUAL, residual=a.x[:m], out=a.h[:m],
                           workspace=self.tc_ws)
@@ -170,34 +218,41 @@ class DecodeEngine:
                               out=a.act[:m])
                 K.down_residual(a.act[:m], mlp.down_proj_weight, a.h[:m], out=a.x[:m])
         if head:
-            if q_len == 1:
-                rows = a.x[:B]
+            if head == "all":
+                rows, n, dest = a.x[:m], m, self.verdict[:m]
+            elif q_len == 1:
+                rows, n, dest = a.x[:B], B, a.ids[:B]
             else:
                 a.head_rows.copy_(a.x[:m].view(B, q_len, -1)[:, -1])
-                rows = a.head_rows
+                rows, n, dest = a.head_rows, B, a.ids[:B]
             self._head_rows = rows
             if self.tp is not None:
+                keys = self.keys[:n]
                 if tc:
-                    K.rmsnorm(rows, rt.final_norm_weight, eps, out=self.xn[:B])
-                    K.gemm_tc(self.xn[:B], rt.lm_head_weight, out=self.logits, workspace=self.tc_ws)
-                    K.argmax_rows_keys(self.logits, self.vocab_offset, out_keys=self.keys, workspace=self.lm_ws)
+                    K.rmsnorm(rows, rt.final_norm_weight, eps, out=self.xn[:n])
+                    K.gemm_tc(self.xn[:n], rt.lm_head_weight, out=self.logits[:n], workspace=self.tc_ws)
+                    K.argmax_rows_keys(self.logits[:n], self.vocab_offset, out_keys=keys, workspace=self.lm_ws)
                 else:
                     K.lmhead_argmax_keys(rows, rt.final_norm_weight, rt.lm_head_weight, eps, self.vocab_offset,
-                                         out_keys=self.keys, workspace=self.lm_ws)
-                self.tp.all_reduce_max(self.keys)
-                K.argmax_keys_to_ids(self.keys, out_ids=a.ids[:B])
+                                         out_keys=keys, workspace=self.lm_ws)
+                self.tp.all_reduce_max(keys)
+                K.argmax_keys_to_ids(keys, out_ids=dest)
             elif tc:
-                K.rmsnorm(rows, rt.final_norm_weight, eps, out=self.xn[:B])
-                K.gemm_tc(self.xn[:B], rt.lm_head_weight, out=self.logits, workspace=self.tc_ws)
-                K.argmax_rows(self.logits, out_ids=a.ids[:B], workspace=self.lm_ws)
+                K.rmsnorm(rows, rt.final_norm_weight, eps, out=self.xn[:n])
+                K.gemm_tc(self.xn[:n], rt.lm_head_weight, out=self.logits[:n], workspace=self.tc_ws)
+                K.argmax_rows(self.logits[:n], out_ids=dest, workspace=self.lm_ws)
             else:
-                K.lmhead_argmax(rows, rt.final_norm_weight, rt.lm_head_weight, eps, out_ids=a.ids[:B],
+                K.lmhead_argmax(rows, rt.final_norm_weight, rt.lm_head_weight, eps, out_ids=dest,
                                 workspace=self.lm_ws)
-        K.advance_cursors(kv.cache_pos, q_len)
+        if advance:
+            K.advance_cursors(kv.cache_pos, q_len)
 
     def _row_split(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor, out: torch.Tensor,
                    tc: bool) -> None:
         """Row-split linear of tensor parallelism: fp32 partial, all-reduce, residual add."""
+        if not tc and self.tp.p2p is not None:  # fused one-shot all-reduce in the linear's epilogue
+            K.linear_allreduce_residual(x, w, residual, self.tp.p2p, out=out)
+            return
         part = self.part[:x.shape[0]]
         if tc:
             K.gemm_tc(x, w, epilogue=K.EPI_STORE_F32, out=part, workspace=self.tc_ws)
@@ -266,6 +321,65 @@ class DecodeEngine:
         torch.cuda.synchronize()
         self.graph = graph
 
+    # ------------------------------------------------------------------
+    # speculative verify (runtime_loop.py:651-916)
+    # ------------------------------------------------------------------
+    def _verify_once(self, k: int, draft_cache_pos: torch.Tensor | None = None,
+                     out_tokens: torch.Tensor | None = None, out_len: torch.Tensor | None = None) -> None:
+        self._forward(k + 1, head="all", advance=False)
+        K.spec_accept(self.arenas.ids, self.verdict, self.B, k, next_ids=self.next_ids, accepted=self.accepted,
+                      cache_pos=self.kv.cache_pos, draft_cache_pos=draft_cache_pos, out_tokens=out_tokens,
+                      out_len=out_len)
+
+    def verify_inputs(self, k: int) -> torch.Tensor:
+        """View ``[B, k + 1]`` of the verify input ids: column 0 holds each
+        sequence's current token (kept by the accept kernel), columns 1..k the
+        proposals the caller writes before :meth:`verify_step`."""
+        return self.arenas.ids[:self.B * (k + 1)].view(self.B, k + 1)
+
+    def verify_step(self, k: int) -> None:
+        """One target verify pass over ``[current, d1..dk]`` per sequence plus the
+        greedy-exact accept / reject, all on the device (graph replay once captured).
+
+        Results: ``next_ids [B]`` (the next current token), ``accepted [B]``
+        (proposals kept), the cursors moved by ``accepted + 1``, ``verdict``.
+        The host's cursor mirror is not updated (that would need a sync); call
+        :meth:`sync_cursors` to refresh it.
+        """
+        if self.B * (k + 1) > self.T:
+            raise ValueError(f"verify of {self.B} x {k + 1} tokens exceeds the {self.T}-token step")
+        if max(self.kv.sequence_lens) + k + 1 > self.S:
+            raise ValueError("KV cache is full")
+        if self.use_graph and k not in self.verify_graphs:
+            a = self.arenas
+            saved = (self.kv.cache_pos.clone(), a.ids.clone())
+            self._verify_once(k)  # eager warm-up
+            torch.cuda.synchronize()
+            self.kv.cache_pos.copy_(saved[0])
+            a.ids.copy_(saved[1])
+            graph = torch.cuda.CUDAGraph()
+            stream = torch.cuda.Stream()
+            stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.graph(graph, stream=stream):
+                self._verify_once(k)
+            torch.cuda.current_stream().wait_stream(stream)
+            torch.cuda.synchronize()
+            self.verify_graphs[k] = graph
+        if self.use_graph:
+            self.verify_graphs[k].replay()
+        else:
+            self._verify_once(k)
+        # conservative host bound until the next sync_cursors()
+        self.kv.sequence_lens = [n + k + 1 for n in self.kv.sequence_lens]
+        self._unsynced = True
+
+    def sync_cursors(self) -> list[int]:
+        """Read the device cursors back (a host sync) into the host mirror."""
+        lens = [int(v) for v in self.kv.cache_pos.tolist()]
+        self.kv.set_sequence_lens(lens)
+        self._unsynced = False
+        return lens
+
     def decode_step(self) -> None:
         """Enqueue one decode step (graph replay when captured)."""
         if self.kv.sequence_lens[0] + 1 > self.S:
@@ -302,10 +416,15 @@ class DecodeEngine:
         per_layer = 8 if self.backend == "tc" else 6
         head = 3 if self.backend == "tc" else 1
         if self.tp is not None:  # + residual-add after each row-split linear, + keys-to-ids
-            per_layer += 2
+            if self.backend == "tc" or self.tp.p2p is None:
+                per_layer += 2
             head += 1
         return 1 + per_layer * len(self.rt.layers) + head + 1
 
     def collectives_per_step(self) -> int:
-        """NCCL all-reduces one decode step issues (0 on one GPU)."""
-        return 0 if self.tp is None else 2 * len(self.rt.layers) + 1
+        """NCCL all-reduces one decode step issues (0 on one GPU; the fused
+        all-reduce of the CUDA-core linears is not counted)."""
+        if self.tp is None:
+            return 0
+        fused = self.backend != "tc" and self.tp.p2p is not None
+        return (0 if fused else 2 * len(self.rt.layers)) + 1

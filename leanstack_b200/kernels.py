@@ -361,6 +361,63 @@ def decode_step(layer_table: torch.Tensor, num_layers: int, hidden: int, interme
              qkv.data_ptr(), attn.data_ptr(), act.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
 
 
+def gemv_tile_weight(w: torch.Tensor, silu: bool = False) -> torch.Tensor:
+    """Rewrite a ``[N, K]`` bf16 weight into the tensor-core GEMV tile layout (same bytes)."""
+    _check(w, "w")
+    out = torch.empty_like(w)
+    nat.call("ls_gemv_tile_weight", w.data_ptr(), w.shape[0], w.shape[1], int(bool(silu)), out.data_ptr(), _stream())
+    return out
+
+
+def gemv_workspace_bytes(m: int, n_rows: int, epilogue: int) -> int:
+    v = ctypes.c_int64(0)
+    nat.call("ls_gemv_workspace_bytes", m, n_rows, int(epilogue), ctypes.byref(v))
+    return v.value
+
+
+def gemv(x: torch.Tensor, w_tiled: torch.Tensor, *, norm_w: torch.Tensor | None = None, eps: float = 1e-6,
+         epilogue: int = EPI_STORE, residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+         workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """``epilogue(norm?(x) @ W.T)`` for x ``[m, K]`` (m <= 8) with ``W`` pre-tiled by :func:`gemv_tile_weight`."""
+    _check(x, "x")
+    _check(w_tiled, "w_tiled")
+    k = x.shape[-1]
+    m = x.numel() // k
+    n = w_tiled.shape[0]
+    if w_tiled.shape[1] != k:
+        raise ValueError(f"weight in-features {w_tiled.shape[1]} != activation width {k}")
+    if norm_w is not None:
+        _check(norm_w, "norm_w")
+    if residual is not None:
+        _check(residual, "residual")
+    cols = n // 2 if epilogue == EPI_SILU_MUL else n
+    if out is None:
+        out = torch.empty((*x.shape[:-1], cols), device=x.device, dtype=BF16)
+    if workspace is None:
+        workspace = torch.zeros(gemv_workspace_bytes(m, n, epilogue), device=x.device, dtype=torch.uint8)
+    nat.call("ls_gemv_bf16", x.data_ptr(), m, k, _ptr(norm_w), float(eps), w_tiled.data_ptr(), n, int(epilogue),
+             _ptr(residual), out.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
+    return out
+
+
+def linear_allreduce_residual(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor, exchange,
+                              out: torch.Tensor | None = None) -> torch.Tensor:
+    """Row-split linear + fused one-shot all-reduce over the ranks + residual (``ls_linear_allreduce_residual``).
+
+    ``exchange``: a :class:`leanstack_b200.tp.P2PExchange` (every rank calls with the same m)."""
+    _check(x, "x")
+    _check(w, "w")
+    _check(residual, "residual")
+    k = x.shape[-1]
+    m = x.numel() // k
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty_like(residual)
+    nat.call("ls_linear_allreduce_residual", x.data_ptr(), m, k, w.data_ptr(), n, residual.data_ptr(),
+             out.data_ptr(), ctypes.byref(exchange.desc), _stream())
+    return out
+
+
 def residual_add_f32(residual: torch.Tensor, y: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """``out = bf16(residual + bf16(y))`` for an fp32 ``y`` (after a tensor-parallel all-reduce)."""
     _check(residual, "residual")
@@ -369,6 +426,32 @@ def residual_add_f32(residual: torch.Tensor, y: torch.Tensor, out: torch.Tensor 
         out = torch.empty_like(residual)
     nat.call("ls_residual_add_f32", residual.data_ptr(), y.data_ptr(), residual.numel(), out.data_ptr(), _stream())
     return out
+
+
+def spec_accept(ids: torch.Tensor, verdict: torch.Tensor, batch: int, k: int, *,
+                next_ids: torch.Tensor | None = None, accepted: torch.Tensor | None = None,
+                cache_pos: torch.Tensor | None = None, draft_cache_pos: torch.Tensor | None = None,
+                out_tokens: torch.Tensor | None = None, out_len: torch.Tensor | None = None) -> None:
+    """Greedy-exact accept / reject of a verify pass (see ``ls_spec_accept``); updates ``ids[:, 0]``."""
+    _check(ids, "ids", torch.int64)
+    _check(verdict, "verdict", torch.int64)
+    if ids.numel() < batch * (k + 1) or verdict.numel() < batch * (k + 1):
+        raise ValueError("ids / verdict must hold batch * (k + 1) tokens")
+    if next_ids is not None:
+        _check(next_ids, "next_ids", torch.int64)
+    if accepted is not None:
+        _check(accepted, "accepted", torch.int32)
+    for name, t in (("cache_pos", cache_pos), ("draft_cache_pos", draft_cache_pos), ("out_len", out_len)):
+        if t is not None:
+            _check(t, name, torch.int32)
+    cap = 0
+    if out_tokens is not None:
+        _check(out_tokens, "out_tokens", torch.int64)
+        if out_tokens.dim() != 2 or out_tokens.shape[0] != batch:
+            raise ValueError("out_tokens must be [batch, capacity]")
+        cap = out_tokens.shape[1]
+    nat.call("ls_spec_accept", ids.data_ptr(), verdict.data_ptr(), batch, k, _ptr(next_ids), _ptr(accepted),
+             _ptr(cache_pos), _ptr(draft_cache_pos), _ptr(out_tokens), _ptr(out_len), cap, _stream())
 
 
 def advance_cursors(cache_pos: torch.Tensor, q_len: int, delta: torch.Tensor | None = None) -> None:

@@ -130,6 +130,27 @@ def main(argv=None) -> int:
         xe = torch.empty(m, H, device=dev, dtype=torch.bfloat16)
         t = _time(lambda i: K.embed_gather(ids, emb, out=xe), args.reps)
         out["embed"] = (t, m * H * 2)
+    gv = {k for k in wanted if k.startswith("gv_")}
+    if gv:
+        def gv_case(name, n_rows, k_dim, epi, silu=False, norm=False):
+            wts = [K.gemv_tile_weight(t, silu=silu) for t in w((n_rows, k_dim), "mb/gv" + name)]
+            xa = synth.normal((m, k_dim), 1.0, 0, "mb/gx" + name, device=dev)
+            n_out = n_rows // 2 if silu else n_rows
+            res = synth.normal((m, n_out), 1.0, 0, "mb/gres" + name, device=dev)
+            nwk = synth.norm_weight((k_dim,), 0, "mb/gnw" + name, device=dev) if norm else None
+            o = torch.empty(m, n_out, device=dev, dtype=torch.bfloat16)
+            ws_ = torch.zeros(K.gemv_workspace_bytes(m, n_rows, epi), device=dev, dtype=torch.uint8)
+            t = _time(lambda i: K.gemv(xa, wts[i % C], norm_w=nwk, epilogue=epi, residual=res, out=o,
+                                       workspace=ws_), args.reps)
+            out[f"gv_{name}(m={m})"] = (t, n_rows * k_dim * 2)
+        if "gv_qkv" in gv:
+            gv_case("qkv", g.qkv_dim, H, K.EPI_STORE, norm=True)
+        if "gv_oproj" in gv:
+            gv_case("oproj", H, g.q_dim, K.EPI_RESIDUAL)
+        if "gv_gateup" in gv:
+            gv_case("gateup", 2 * I, H, K.EPI_SILU_MUL, silu=True, norm=True)
+        if "gv_down" in gv:
+            gv_case("down", H, I, K.EPI_RESIDUAL)
     tc = {k for k in wanted if k.startswith("tc_")}
     if tc:
         def tc_case(name, n_rows, k_dim, epi, n_out, extra=None):

@@ -165,16 +165,29 @@ def argmax_key_id(key: int) -> int:
 # ---------------------------------------------------------------------------
 
 class TPComm:
-    """The two collectives of the tensor-parallel step, over a torch.distributed group.
+    """The collectives of the tensor-parallel step, over a torch.distributed group.
 
     NCCL for CUDA tensors (captured into the decode graph like any other
-    launch); gloo works for the CPU tests of the partition math.
+    launch); gloo works for the CPU tests of the partition math.  ``p2p`` (set
+    by :meth:`enable_p2p`) is the exchange of the fused one-shot all-reduce
+    that the CUDA-core row-split linears use instead of NCCL.
     """
 
     def __init__(self, rank: int, world: int, group=None):
         self.rank = rank
         self.world = world
         self.group = group
+        self.p2p: P2PExchange | None = None
+
+    def enable_p2p(self, width: int, max_rows: int = 8, max_ctas: int = 512) -> "P2PExchange":
+        if self.world > 1 and self.p2p is None:
+            self.p2p = P2PExchange(self, width, max_rows, max_ctas)
+        return self.p2p
+
+    def close(self) -> None:
+        if self.p2p is not None:
+            self.p2p.close()
+            self.p2p = None
 
     def all_reduce_sum(self, t: torch.Tensor) -> None:
         if self.world > 1:
@@ -187,3 +200,71 @@ class TPComm:
             import torch.distributed as dist
 
             dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+
+
+class P2PExchange:
+    """Exchange regions of the fused one-shot all-reduce (``ls_linear_allreduce_residual``).
+
+    Every rank allocates one region (``cudaMalloc``, zeroed), exports a CUDA
+    IPC handle, gathers the others' handles over the process group and maps
+    them (plain peer mappings, no multicast).  Refuses to run when two ranks
+    share a GPU: the kernel's ranks wait on each other and must run
+    concurrently, one per device.
+    """
+
+    def __init__(self, comm: TPComm, width: int, max_rows: int = 8, max_ctas: int = 512):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _native as nat
+
+        if comm.world > nat.MAX_TP_RANKS:
+            raise ValueError(f"the fused all-reduce handles up to {nat.MAX_TP_RANKS} ranks")
+        dev = torch.cuda.current_device()
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        uuids: list = [None] * comm.world
+        dist.all_gather_object(uuids, uuid, group=comm.group)
+        if len(set(uuids)) != comm.world:
+            raise RuntimeError("the fused all-reduce needs one GPU per rank")
+        nbytes = ctypes.c_int64(0)
+        nat.call("ls_p2p_region_bytes", max_rows, width, max_ctas, ctypes.byref(nbytes))
+        region = ctypes.c_void_p(0)
+        nat.call("ls_p2p_alloc", nbytes.value, ctypes.byref(region))
+        handle = (ctypes.c_ubyte * 64)()
+        nat.call("ls_ipc_get_handle", region, handle)
+        handles: list = [None] * comm.world
+        dist.all_gather_object(handles, bytes(handle), group=comm.group)
+        self.region = region.value
+        self.opened: list[int] = []
+        desc = nat.P2PExchangeDesc()
+        for q in range(comm.world):
+            if q == comm.rank:
+                desc.peer[q] = self.region
+                continue
+            h = (ctypes.c_ubyte * 64).from_buffer_copy(handles[q])
+            ptr = ctypes.c_void_p(0)
+            nat.call("ls_ipc_open", h, ctypes.byref(ptr))
+            desc.peer[q] = ptr.value
+            self.opened.append(ptr.value)
+        desc.rank, desc.world, desc.max_ctas, desc.max_rows, desc.width = comm.rank, comm.world, max_ctas, \
+            max_rows, width
+        self.desc = desc
+        self._group = comm.group
+        dist.barrier(group=comm.group)  # every region is zeroed and mapped before any kernel signals
+
+    def close(self) -> None:
+        """Unmap the peers' regions and free this rank's (after every rank has stopped using them)."""
+        import torch.distributed as dist
+
+        from . import _native as nat
+
+        torch.cuda.synchronize()
+        if dist.is_initialized():
+            dist.barrier(group=self._group)
+        for ptr in self.opened:
+            nat.call("ls_ipc_close", ptr)
+        self.opened = []
+        if self.region:
+            nat.call("ls_p2p_free", self.region)
+            self.region = 0

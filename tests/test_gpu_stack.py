@@ -156,6 +156,18 @@ def test_tiny_stack_greedy_engine_and_dispatch(golden_dir):
     assert toks == want
 
 
+def test_tiny_stack_greedy_engine_tiled_gemv(golden_dir):
+    """The engine with the tensor-core GEMV over pre-tiled weights reproduces the reference's greedy stream."""
+    gold = _gold(golden_dir, "tiny_stack.pt")["greedy"]
+    rt = _tiny_runtime()
+    prompt = gold["prompt"]
+    want = gold["tokens"].tolist()
+    eng = DecodeEngine(rt, batch_size=1, max_seq_len=prompt.shape[1] + 40, gemv_tiles=True)
+    assert eng.tiles is not None
+    got = eng.generate(prompt, len(want))[0].tolist()
+    assert got == want
+
+
 def test_persistent_step_matches_layered_step():
     """The one-kernel decode step produces the same tokens as the kernel-per-op step on the tiny stack."""
     rt = _tiny_runtime()

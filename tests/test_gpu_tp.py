@@ -5,7 +5,9 @@ seeded checkpoint.  The TP engine's greedy tokens must equal the single-GPU
 engine's (fp32 partial sums differ only in summation order) and its last hidden
 rows must agree within the north-star bound.  Both the eager step and the
 CUDA-graph step (NCCL captured in the graph) are checked, for the CUDA-core
-(batch 1) and tensor-core (batch 4) linears.  Skipped with fewer than 2 GPUs.
+(batch 1) and tensor-core (batch 4) linears, and for the CUDA-core linears with
+the fused one-shot all-reduce over peer memory instead of NCCL.  Skipped with
+fewer than 2 GPUs.
 """
 
 from __future__ import annotations
@@ -20,6 +22,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 WORLD = 2
+CASES = ((1, "cuda_core", False), (1, "cuda_core", True), (4, "tc", False))
 
 
 def _free_port() -> int:
@@ -37,6 +40,7 @@ def _run(rank: int, port: int, q) -> None:
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.cuda.set_device(rank)
         dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120))
+        from leanstack_b200 import kernels as K
         from leanstack_b200 import synth, tp
         from leanstack_b200.config import TINY
         from leanstack_b200.engine import DecodeEngine
@@ -45,19 +49,23 @@ def _run(rank: int, port: int, q) -> None:
         dev = torch.device("cuda", rank)
         g = TINY
         out = {}
-        for batch, backend in ((1, "cuda_core"), (4, "tc")):
+        for batch, backend, p2p in CASES:
             prompt = synth.token_ids((batch, 24), g.vocab_size, 3, "tp/prompt")
             rt, shard = tp.materialize_tp_shard(g, synth.synth_checkpoint(g, 3, device=dev), rank, WORLD, device=dev)
             comm = tp.TPComm(rank, WORLD)
+            if p2p:
+                comm.enable_p2p(g.hidden_size)
             for use_graph in (False, True):
                 eng = DecodeEngine(rt, batch_size=batch, max_seq_len=128, linear_backend=backend, tp=comm,
                                    shard=shard, use_graph=use_graph)
                 toks = eng.generate(prompt, 12).cpu()
                 rows = eng.last_head_rows().float().cpu()
-                out[(batch, backend, use_graph)] = (toks, rows)
+                out[(batch, backend, p2p, use_graph)] = (toks, rows)
                 eng.graph = None
                 del eng
-            if rank == 0:
+            assert K.device_error() == 0
+            comm.close()
+            if rank == 0 and (batch, backend, "single") not in out:
                 full = materialize_from_tensors(g, synth.synth_checkpoint(g, 3, device=dev), device=dev,
                                                 free_source=True)
                 e1 = DecodeEngine(full, batch_size=batch, max_seq_len=128, linear_backend=backend)
@@ -90,15 +98,15 @@ def test_tp2_engine_matches_single_gpu_engine():
     for r, v in res.items():
         assert not isinstance(v, str), f"rank {r}: {v}"
     out0, out1 = res[0], res[1]
-    for batch, backend in ((1, "cuda_core"), (4, "tc")):
+    for batch, backend, p2p in CASES:
         ref_toks, ref_rows = out0[(batch, backend, "single")]
         for use_graph in (False, True):
-            toks0, rows0 = out0[(batch, backend, use_graph)]
-            toks1, rows1 = out1[(batch, backend, use_graph)]
+            toks0, rows0 = out0[(batch, backend, p2p, use_graph)]
+            toks1, rows1 = out1[(batch, backend, p2p, use_graph)]
             assert torch.equal(toks0, toks1), "ranks disagree"
             assert torch.equal(rows0, rows1), "ranks hold different residual streams"
             same = (toks0 == ref_toks).float().mean().item()
-            assert same >= 0.9, (batch, backend, use_graph, toks0.tolist(), ref_toks.tolist())
+            assert same >= 0.9, (batch, backend, p2p, use_graph, toks0.tolist(), ref_toks.tolist())
             assert torch.equal(toks0[:, :4], ref_toks[:, :4])
             err = (rows0 - ref_rows).abs().max().item()
             if torch.equal(toks0, ref_toks):
