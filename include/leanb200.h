@@ -125,6 +125,19 @@ int ls_rmsnorm_qkv_rope_kvappend(const void* x, int64_t batch, int64_t q_len, in
                                  void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* qkv_scratch,
                                  void* q_out, ls_stream_t stream);
 
+/* The same GEMM over weights pre-tiled once by ls_gemm_tc_tile_weight (the
+ * leanpack-v1 tile layout): [ceil(n/128)][ceil(k/64)] tiles of 128 rows x 64 k,
+ * each the 16 KB shared-memory image the MMA reads (128-byte swizzle), rows
+ * past n and columns past k zero; for SILU_MUL the gate half is tiled first,
+ * then the up half.  Every weight tile arrives as one contiguous bulk copy
+ * instead of a 128-row strided TMA box.  n_rows as in the untiled call (2n for
+ * SILU_MUL). */
+int ls_gemm_tc_tiled_bytes(int64_t n_rows, int64_t k, int silu, int64_t* bytes);
+int ls_gemm_tc_tile_weight(const void* w, int64_t n_rows, int64_t k, int silu, void* out, ls_stream_t stream);
+int ls_gemm_bf16_tcgen05_tiled(const void* x, int64_t m, int64_t k, const void* w_tiled, int64_t n, int epilogue,
+                               const void* residual, void* out, void* workspace, int64_t workspace_bytes,
+                               ls_stream_t stream);
+
 /*
  * The second half of ls_rmsnorm_qkv_rope_kvappend on a precomputed fused
  * projection qkv [m, (Hq + 2 Hkv) D]: per-head q/k RMSNorm, NeoX RoPE and the
@@ -316,6 +329,11 @@ int ls_argmax_keys_to_ids(const int64_t* keys, int64_t m, int64_t* out_ids, ls_s
 /* out = bf16(residual + bf16(y)) over n elements, y fp32: the residual epilogue
  * of o_proj / down applied after the tensor-parallel all-reduce of their
  * fp32 partials (src/leanstack/runtime/qwen_explicit.py:819-829, :1262). */
+/* Profiling hook of ls_decode_step: with a non-NULL device buffer of
+ * (barriers per step) x grid x 2 u64, each barrier records every CTA's arrival
+ * and release time (globaltimer ns).  NULL turns it off. */
+int ls_decode_step_set_trace(void* buffer);
+
 int ls_residual_add_f32(const void* residual, const float* y, int64_t n, void* out, ls_stream_t stream);
 
 /* Standalone RMSNorm over the last dim, bf16((x * rsqrt(mean(x^2) + eps)) * w),

@@ -232,7 +232,10 @@ int launch_decode_attention(const void* q, const void* k_cache, const void* v_ca
 
 int tc_workspace_bytes(int64_t m, int64_t k, int64_t n_out, int epi, int64_t* bytes);
 int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n_out, int epi, const void* residual,
-                   void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream);
+                   void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream,
+                   const void* w_tiled = nullptr);
+int64_t tc_tiled_bytes(int64_t n_out, int64_t k, int silu);
+int launch_tc_tile(const void* w, int64_t n_rows, int64_t k, int silu, void* out, cudaStream_t stream);
 
 int decode_step_workspace_bytes(int64_t hkv, int64_t* bytes);
 int decode_step(const void* layers, int64_t L, int64_t H, int64_t I, int64_t hq, int64_t hkv, int64_t head_dim,
@@ -428,6 +431,27 @@ int ls_gemm_bf16_tcgen05(const void* x, int64_t m, int64_t k, const void* w, int
   LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32,
              LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d", epilogue);
   return launch_gemm_tc(x, m, k, w, n, epilogue, residual, out, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int ls_gemm_tc_tiled_bytes(int64_t n_rows, int64_t k, int silu, int64_t* bytes) {
+  LS_REQUIRE(bytes && n_rows > 0 && k > 0 && (!silu || n_rows % 2 == 0), LS_ERR_INVALID_ARGUMENT,
+             "ls_gemm_tc_tiled_bytes: bad arguments");
+  *bytes = tc_tiled_bytes(silu ? n_rows / 2 : n_rows, k, silu);
+  return LS_OK;
+}
+
+int ls_gemm_tc_tile_weight(const void* w, int64_t n_rows, int64_t k, int silu, void* out, ls_stream_t stream) {
+  return launch_tc_tile(w, n_rows, k, silu, out, (cudaStream_t)stream);
+}
+
+int ls_gemm_bf16_tcgen05_tiled(const void* x, int64_t m, int64_t k, const void* w_tiled, int64_t n, int epilogue,
+                               const void* residual, void* out, void* workspace, int64_t workspace_bytes,
+                               ls_stream_t stream) {
+  LS_REQUIRE(w_tiled, LS_ERR_INVALID_ARGUMENT, "ls_gemm_bf16_tcgen05_tiled: null weights");
+  LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32,
+             LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d", epilogue);
+  return launch_gemm_tc(x, m, k, nullptr, n, epilogue, residual, out, workspace, workspace_bytes,
+                        (cudaStream_t)stream, w_tiled);
 }
 
 int ls_qk_norm_rope_kvappend(const void* qkv, int64_t batch, int64_t q_len, int64_t num_heads, int64_t num_kv_heads,

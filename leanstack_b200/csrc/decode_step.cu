@@ -70,6 +70,7 @@ struct DsParams {
   unsigned int* barrier;            // zeroed before every launch
   unsigned int* head_counter;       // [1] zero between steps
   int* err;
+  unsigned long long* trace;        // optional: per barrier and CTA, globaltimer at arrival and at release
   int L, H, I, Hq, Hkv, V, S, splits;
   float eps, scale_log2;
 };
@@ -87,6 +88,9 @@ __device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
 __device__ bool ds_grid_sync(const DsParams& p, unsigned int& gen, int* s_abort) {
   __syncthreads();
   if (threadIdx.x == 0) {
+    unsigned long long* tr =
+        p.trace ? p.trace + ((size_t)(gen / gridDim.x) * gridDim.x + blockIdx.x) * 2 : nullptr;
+    if (tr) tr[0] = global_timer_ns();
     gen += gridDim.x;
     __threadfence();
     atomicAdd(p.barrier, 1u);
@@ -104,6 +108,7 @@ __device__ bool ds_grid_sync(const DsParams& p, unsigned int& gen, int* s_abort)
       }
     }
     __threadfence();
+    if (tr) tr[1] = global_timer_ns();
   } else {
     gen += gridDim.x;
   }
@@ -542,6 +547,12 @@ __global__ void __launch_bounds__(kDsThreads, 1) decode_step_kernel(DsParams p) 
 }  // namespace lsb
 
 namespace lsb_host {
+// Profiling hook: when set, every barrier of the next decode_step launches
+// records (arrival, release) globaltimer stamps per CTA into this buffer.
+static unsigned long long* g_ds_trace = nullptr;
+}  // namespace lsb_host
+
+namespace lsb_host {
 using namespace lsb;
 
 size_t decode_step_smem() { return sizeof(DsSmem); }
@@ -653,6 +664,7 @@ int decode_step(const void* layers, int64_t L, int64_t H, int64_t I, int64_t hq,
   p.best_idx = reinterpret_cast<int*>(ws + w.best_idx);
   p.attn_part = reinterpret_cast<float*>(ws + w.attn_part);
   p.err = device_error_ptr();
+  p.trace = g_ds_trace;
   p.L = (int)L;
   p.H = (int)H;
   p.I = (int)I;
@@ -667,3 +679,8 @@ int decode_step(const void* layers, int64_t L, int64_t H, int64_t I, int64_t hq,
 }
 
 }  // namespace lsb_host
+
+extern "C" int ls_decode_step_set_trace(void* buffer) {
+  lsb_host::g_ds_trace = static_cast<unsigned long long*>(buffer);
+  return LS_OK;
+}

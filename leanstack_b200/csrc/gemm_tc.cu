@@ -37,7 +37,7 @@ constexpr int kTcTileN = 128;   // weight rows per tile (MMA M)
 constexpr int kTcBlockK = 64;   // K per stage: one 128-byte swizzle atom of bf16
 constexpr int kTcThreads = 192;
 constexpr int kTcEpiThreads = 128;
-constexpr int kTcMaxStages = 8;
+constexpr int kTcMaxStages = 16;
 // Tile counters sit in a fixed-size region at the start of the workspace, so
 // one workspace can serve GEMMs of different shapes: partials of one call never
 // land on another call's counters.
@@ -61,6 +61,10 @@ struct TcParams {
   int stage_bytes;
   int acc_buffers;  // 2: the MMA fills one TMEM accumulator while the epilogue drains the other
   uint32_t tmem_cols;
+  // Pre-tiled weights (ls_gemm_tc_tile_weight): tile (t, kb) is the 16 KB
+  // shared-memory image at w_tiled[(t * kblocks + kb) * 16 KB]; null: TMA maps.
+  const unsigned char* w_tiled;
+  const unsigned char* w2_tiled;
 };
 
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
@@ -198,13 +202,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const long long n_units = ue - ub;
       const long long pre = n_units < NS ? n_units : NS;
       // Weights first (independent of the previous kernel), then activations.
+      auto load_w = [&](unsigned char* st, int t, int kb, uint64_t* bar) {
+        if (p.w_tiled) {
+          const size_t off = ((size_t)t * KB + kb) * kWBytes;
+          bulk_g2s(st, p.w_tiled + off, kWBytes, bar);
+          if (SILU) bulk_g2s(st + kWBytes, p.w2_tiled + off, kWBytes, bar);
+        } else {
+          tma_load_2d(st, &tm_w, kb * kTcBlockK, t * kTcTileN, bar);
+          if (SILU) tma_load_2d(st + kWBytes, &tm_w2, kb * kTcBlockK, t * kTcTileN, bar);
+        }
+      };
       for (long long i = 0; i < pre; ++i) {
         const long long u = ub + i;
         const int t = (int)(u / KB), kb = (int)(u % KB);
         unsigned char* st = smem + (size_t)i * p.stage_bytes;
         mbar_arrive_expect_tx(&full[i], kWBytes * ACCS + x_bytes);
-        tma_load_2d(st, &tm_w, kb * kTcBlockK, t * kTcTileN, &full[i]);
-        if (SILU) tma_load_2d(st + kWBytes, &tm_w2, kb * kTcBlockK, t * kTcTileN, &full[i]);
+        load_w(st, t, kb, &full[i]);
       }
       grid_dep_wait();
       for (long long i = 0; i < pre; ++i) {
@@ -222,8 +235,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int t = (int)(u / KB), kb = (int)(u % KB);
         unsigned char* st = smem + (size_t)s * p.stage_bytes;
         mbar_arrive_expect_tx(&full[s], kWBytes * ACCS + x_bytes);
-        tma_load_2d(st, &tm_w, kb * kTcBlockK, t * kTcTileN, &full[s]);
-        if (SILU) tma_load_2d(st + kWBytes, &tm_w2, kb * kTcBlockK, t * kTcTileN, &full[s]);
+        load_w(st, t, kb, &full[s]);
         tma_load_2d(st + kWBytes * ACCS, &tm_x, kb * kTcBlockK, 0, &full[s]);
       }
     }
@@ -433,6 +445,20 @@ struct TcPlan {
   size_t smem, counter_bytes, partial_bytes;
 };
 
+// Shared memory given to the stage ring.  Under load the HBM round trip is a
+// few microseconds, so the bytes in flight per SM (stages x tile bytes) set the
+// stream rate.  LEANB200_TC_SMEM_KB overrides it (measurement).
+static int tc_stage_budget_kb() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("LEANB200_TC_SMEM_KB");
+    v = e ? atoi(e) : 112;
+    if (v < 64) v = 64;
+    if (v > 208) v = 208;
+  }
+  return v;
+}
+
 static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
   TcPlan pl = {};
   pl.accs = (epi == TEPI_SILU_MUL) ? 2 : 1;
@@ -444,9 +470,7 @@ static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
   pl.grid = (int)(units < sms ? units : sms);
   pl.stage_bytes = (int)(((size_t)kTcTileN * kTcBlockK * 2 * pl.accs + (size_t)pl.BN * kTcBlockK * 2 + 1023) / 1024 *
                          1024);
-  // ~112 KB of stages: deep enough to cover HBM latency, small enough that the
-  // next kernel's CTA fits beside this one on the SM (PDL overlap).
-  int stages = (int)((112 * 1024) / pl.stage_bytes);
+  int stages = (int)(((size_t)tc_stage_budget_kb() * 1024) / pl.stage_bytes);
   if (stages > kTcMaxStages) stages = kTcMaxStages;
   if (stages < 3) stages = 3;
   pl.stages = stages;
@@ -496,16 +520,20 @@ static int launch_tc_t(const CUtensorMap& w, const CUtensorMap& w2, const CUtens
 }
 
 // out[m, n_out] = epilogue(x[m, k] . w^T); for SILU_MUL w is [2 n_out, k] (gate rows, then up rows).
+int64_t tc_tiled_bytes(int64_t n_out, int64_t k, int silu);
+
 int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n_out, int epi, const void* residual,
-                   void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
-  if (!x || !w || !out) return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_tc: null pointer");
+                   void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream,
+                   const void* w_tiled) {
+  if (!x || !(w || w_tiled) || !out) return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_tc: null pointer");
   // m <= 128 keeps every CTA at <= 256 TMEM columns, so any two CTAs that
   // share an SM can both allocate (a blocked allocation would stall the
   // stream-K reduction of the CTA holding the columns).
   if (m < 1 || m > 128) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "gemm_tc: m=%lld outside 1..128", (long long)m);
   if (k < 8 || k % 8 || n_out < 1) return set_error(LS_ERR_MISALIGNED, "gemm_tc: k=%lld must be a positive multiple of 8",
                                                     (long long)k);
-  if (!aligned16(x) || !aligned16(w)) return set_error(LS_ERR_MISALIGNED, "gemm_tc: x and w must be 16-byte aligned");
+  if (!aligned16(x) || (!w_tiled && !aligned16(w)))
+    return set_error(LS_ERR_MISALIGNED, "gemm_tc: x and w must be 16-byte aligned");
   if (epi == TEPI_RESIDUAL && !residual) return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_tc: residual is null");
   TcPlan pl = tc_plan(m, k, n_out, epi);
   if (pl.tmem_cols > 256) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "gemm_tc: m=%lld too wide for TMEM", (long long)m);
@@ -514,16 +542,23 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
                      kTcMaxTiles);
   if (!workspace || workspace_bytes < (int64_t)(pl.counter_bytes + pl.partial_bytes))
     return set_error(LS_ERR_WORKSPACE, "gemm_tc: workspace needs %zu bytes", pl.counter_bytes + pl.partial_bytes);
-  if (epi == TEPI_SILU_MUL && ((n_out * k * 2) % 16))
+  if (!w_tiled && epi == TEPI_SILU_MUL && ((n_out * k * 2) % 16))
     return set_error(LS_ERR_MISALIGNED, "gemm_tc: up-projection view misaligned");
   CUtensorMap mw, mw2, mx;
-  int rc = make_map(&mw, w, n_out, k, kTcTileN);
-  if (rc) return rc;
-  if (epi == TEPI_SILU_MUL) {
-    rc = make_map(&mw2, static_cast<const __nv_bfloat16*>(w) + n_out * k, n_out, k, kTcTileN);
-    if (rc) return rc;
-  } else {
+  int rc = 0;
+  if (w_tiled) {
+    if (!aligned16(w_tiled)) return set_error(LS_ERR_MISALIGNED, "gemm_tc: tiled weights not 16-byte aligned");
+    memset(&mw, 0, sizeof(mw));
     mw2 = mw;
+  } else {
+    rc = make_map(&mw, w, n_out, k, kTcTileN);
+    if (rc) return rc;
+    if (epi == TEPI_SILU_MUL) {
+      rc = make_map(&mw2, static_cast<const __nv_bfloat16*>(w) + n_out * k, n_out, k, kTcTileN);
+      if (rc) return rc;
+    } else {
+      mw2 = mw;
+    }
   }
   rc = make_map(&mx, x, m, k, pl.BN);
   if (rc) return rc;
@@ -542,6 +577,8 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
   p.stage_bytes = pl.stage_bytes;
   p.acc_buffers = pl.acc_buffers;
   p.tmem_cols = pl.tmem_cols;
+  p.w_tiled = static_cast<const unsigned char*>(w_tiled);
+  p.w2_tiled = w_tiled ? p.w_tiled + tc_tiled_bytes(n_out, k, 0) : nullptr;
   switch (epi) {
     case TEPI_STORE: return launch_tc_t<TEPI_STORE>(mw, mw2, mx, p, pl, stream);
     case TEPI_RESIDUAL: return launch_tc_t<TEPI_RESIDUAL>(mw, mw2, mx, p, pl, stream);
@@ -549,6 +586,52 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
     case TEPI_STORE_F32: return launch_tc_t<TEPI_STORE_F32>(mw, mw2, mx, p, pl, stream);
     default: return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_tc: unknown epilogue %d", epi);
   }
+}
+
+// Pre-tiling for the tcgen05 GEMM: W [N, K] -> [ceil(N/128)][ceil(K/64)] tiles
+// of 128 rows x 64 k, each the 16 KB shared-memory image the MMA reads
+// (K-major, 128-byte swizzle: 16-byte chunk c of row r at r * 128 + ((c ^ (r % 8)) * 16));
+// rows >= N and k >= K are zero.  silu: the gate half [0, N/2) and the up half
+// [N/2, N) are tiled separately, gate tiles first.
+}  // namespace lsb_host
+
+namespace lsb {
+__global__ void tc_tile_kernel(const __nv_bfloat16* w, int N, int K, int tiles, int kblocks, uint4* out) {
+  const long long chunks = (long long)tiles * kblocks * 128 * 8;  // 16-byte chunks
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < chunks;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i & 7);
+    const int r = (int)((i >> 3) & 127);
+    const long long tk = i >> 10;  // tile index t * kblocks + kb
+    const int kb = (int)(tk % kblocks), t = (int)(tk / kblocks);
+    const int row = t * 128 + r, k0 = kb * 64 + c * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < N && k0 < K) v = *reinterpret_cast<const uint4*>(w + (size_t)row * K + k0);
+    out[(tk << 10) + r * 8 + (c ^ (r & 7))] = v;
+  }
+}
+}  // namespace lsb
+
+namespace lsb_host {
+int64_t tc_tiled_bytes(int64_t n_out, int64_t k, int silu) {
+  const int64_t tiles = (n_out + kTcTileN - 1) / kTcTileN, kb = (k + kTcBlockK - 1) / kTcBlockK;
+  return (silu ? 2 : 1) * tiles * kb * (int64_t)kTcTileN * kTcBlockK * 2;
+}
+
+int launch_tc_tile(const void* w, int64_t n_rows, int64_t k, int silu, void* out, cudaStream_t stream) {
+  if (!w || !out || n_rows < 1 || k < 8 || k % 8 || (silu && n_rows % 2))
+    return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_tc_tile: bad arguments");
+  if (!aligned16(w) || !aligned16(out)) return set_error(LS_ERR_MISALIGNED, "gemm_tc_tile: not 16-byte aligned");
+  const int64_t n_out = silu ? n_rows / 2 : n_rows;
+  const int tiles = (int)((n_out + kTcTileN - 1) / kTcTileN), kb = (int)((k + kTcBlockK - 1) / kTcBlockK);
+  const int parts = silu ? 2 : 1;
+  for (int h = 0; h < parts; ++h) {
+    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(w) + (size_t)h * n_out * k;
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<char*>(out) + (size_t)h * tc_tiled_bytes(n_out, k, 0));
+    tc_tile_kernel<<<4 * sm_count(), 256, 0, stream>>>(src, (int)n_out, (int)k, tiles, kb, dst);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "gemm_tc_tile launch: %s", cudaGetErrorString(e));
 }
 
 }  // namespace lsb_host

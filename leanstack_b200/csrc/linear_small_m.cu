@@ -53,7 +53,6 @@ struct LinearParams {
   // EPI_AR_RESIDUAL: tensor-parallel exchange regions
   P2PExchange ex;
   int* err;
-  int pf_rows;  // > 0: each warp keeps its weight rows this many rows ahead in L2 (bulk prefetch)
 };
 
 template <int M>
@@ -88,22 +87,7 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
   // Weights do not depend on the previous kernel: start pulling this CTA's
   // first weight bytes into L2, let the next kernel launch, and only then wait
   // (PDL) for the activations the previous kernel writes.
-  if (p.pf_rows > 0) {
-    // Each warp starts its first pf_rows rows toward L2; the main loop keeps that distance.
-    const int total_g = R * ((K + kGranule - 1) / kGranule);
-    const int gb = (int)(((int64_t)total_g * warp) / kLinWarps), ge = (int)(((int64_t)total_g * (warp + 1)) / kLinWarps);
-    const int gpr0 = (K + kGranule - 1) / kGranule;
-    if (lane == 0 && gb < ge) {
-      for (int ta = gb / gpr0; ta <= min((ge - 1) / gpr0, gb / gpr0 + p.pf_rows - 1); ++ta) {
-        const int ra = (RPU == 2) ? ((ta < P) ? (u0 + ta) : (u0 + (ta - P) + p.N / 2)) : (u0 + ta);
-        const int k0 = (ta == gb / gpr0) ? (gb - ta * gpr0) * kGranule : 0;
-        const int k1 = (ta == (ge - 1) / gpr0) ? min(K, (ge - ta * gpr0) * kGranule) : K;
-        const uint32_t bytes = (uint32_t)((k1 - k0) * 2) & ~15u;
-        const char* base = reinterpret_cast<const char*>(p.w + (size_t)ra * K + k0);
-        for (uint32_t off = 0; off < bytes; off += 16384) prefetch_l2(base + off, min(16384u, bytes - off));
-      }
-    }
-  } else if (tid == 0 && P > 0) {
+  if (tid == 0 && P > 0) {
     const size_t range = (size_t)P * K * 2;
     const uint32_t pf = (uint32_t)(range < kPrefetchBytes ? range : kPrefetchBytes);
     const char* base = reinterpret_cast<const char*>(p.w + (size_t)u0 * K);
@@ -191,18 +175,6 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
     if (RPU == 2) row = (t < P) ? (u0 + t) : (u0 + (t - P) + half_rows);
     else row = u0 + t;
     const __nv_bfloat16* wrow = p.w + (size_t)row * K;
-    if (p.pf_rows > 0 && lane == 0) {  // keep this warp's stream pf_rows rows ahead in L2
-      const int ta = t + p.pf_rows;
-      const int t_last = (g_end - 1) / gpr;
-      if (ta <= t_last) {
-        const int ra = (RPU == 2) ? ((ta < P) ? (u0 + ta) : (u0 + (ta - P) + half_rows)) : (u0 + ta);
-        const int k0 = (ta == t_first) ? (g_begin - ta * gpr) * kGranule : 0;
-        const int k1 = (ta == t_last) ? min(K, (g_end - ta * gpr) * kGranule) : K;
-        const uint32_t bytes = (uint32_t)((k1 - k0) * 2) & ~15u;
-        const char* base = reinterpret_cast<const char*>(p.w + (size_t)ra * K + k0);
-        for (uint32_t off = 0; off < bytes; off += 16384) prefetch_l2(base + off, min(16384u, bytes - off));
-      }
-    }
     float a[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) a[m] = 0.f;
@@ -398,21 +370,8 @@ using namespace lsb;
 // keep ~128 KB per SM in flight, what the measured 6 TB/s needs (one CTA per
 // SM reached only 4.5 TB/s on the lm_head).  m > 4 needs more registers and
 // runs one CTA per SM.
-// LEANB200_LIN_PF=<rows>: one CTA per SM that keeps its weight stream <rows>
-// rows ahead in L2 (leaving room on the SM for the next kernel's CTA, which
-// starts its own prefetch under PDL); unset: two CTAs per SM for m <= 4.
-static int lin_pf_rows() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("LEANB200_LIN_PF");
-    v = e ? atoi(e) : 0;
-    if (v < 0) v = 0;
-  }
-  return v;
-}
-
 static int linear_grid(int units, int m) {
-  const int g = (lin_pf_rows() == 0 && m <= 4 ? 2 : 1) * sm_count();
+  const int g = (m <= 4 ? 2 : 1) * sm_count();
   return units < g ? units : g;
 }
 
@@ -525,7 +484,6 @@ static int launch_linear_impl(const void* x, int64_t m, int64_t k, const void* n
   p.id_offset = id_offset;
   p.out_keys = out_keys ? 1 : 0;
   p.err = device_error_ptr();
-  p.pf_rows = lin_pf_rows() > 0 ? (lin_pf_rows() * 2560 + (int)k - 1) / (int)k : 0;  // scale with row length
   if (epi == EPI_AR_RESIDUAL) {
     p.ex = *ex;
     const int g_ar = grid_override > 0 ? grid_override : linear_grid(p.units, (int)m);

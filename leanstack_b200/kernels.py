@@ -314,7 +314,8 @@ def gemm_workspace_bytes(m: int, k: int, n: int, epilogue: int) -> int:
 
 
 def gemm_tc(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,
-            out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+            out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+            tiled: torch.Tensor | None = None) -> torch.Tensor:
     """tcgen05 weight-streaming GEMM: ``out = epilogue(x @ w.T)`` for x ``[m, k]``, 1 <= m <= 128."""
     _check(x, "x")
     _check(w, "w")
@@ -331,8 +332,12 @@ def gemm_tc(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = EPI_STORE, resi
     need = gemm_workspace_bytes(m, k, n, epilogue)
     if workspace is None:
         workspace = torch.zeros(need, device=x.device, dtype=torch.uint8)
-    nat.call("ls_gemm_bf16_tcgen05", x.data_ptr(), m, k, w.data_ptr(), n, int(epilogue), _ptr(residual),
-             out.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
+    if tiled is not None:  # the weight's pre-tiled copy (gemm_tc_tile_weight); ``w`` gives the shape only
+        nat.call("ls_gemm_bf16_tcgen05_tiled", x.data_ptr(), m, k, tiled.data_ptr(), n, int(epilogue),
+                 _ptr(residual), out.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
+    else:
+        nat.call("ls_gemm_bf16_tcgen05", x.data_ptr(), m, k, w.data_ptr(), n, int(epilogue), _ptr(residual),
+                 out.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
     return out
 
 
@@ -359,6 +364,17 @@ def decode_step(layer_table: torch.Tensor, num_layers: int, hidden: int, interme
              head_dim, vocab, max_seq, float(eps), embed.data_ptr(), final_norm_w.data_ptr(), lm_head_w.data_ptr(),
              cos.data_ptr(), sin.data_ptr(), ids.data_ptr(), cache_pos.data_ptr(), x.data_ptr(), h.data_ptr(),
              qkv.data_ptr(), attn.data_ptr(), act.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
+
+
+def gemm_tc_tile_weight(w: torch.Tensor, silu: bool = False) -> torch.Tensor:
+    """Tile a ``[N, K]`` weight for :func:`gemm_tc` (``tiled=``): 16 KB MMA-image tiles (uint8 buffer)."""
+    _check(w, "w")
+    nbytes = ctypes.c_int64(0)
+    nat.call("ls_gemm_tc_tiled_bytes", w.shape[0], w.shape[1], int(bool(silu)), ctypes.byref(nbytes))
+    out = torch.empty(nbytes.value, device=w.device, dtype=torch.uint8)
+    nat.call("ls_gemm_tc_tile_weight", w.data_ptr(), w.shape[0], w.shape[1], int(bool(silu)), out.data_ptr(),
+             _stream())
+    return out
 
 
 def gemv_tile_weight(w: torch.Tensor, silu: bool = False) -> torch.Tensor:

@@ -162,6 +162,11 @@ def main(argv=None) -> int:
             t = _time(lambda i: K.gemm_tc(xa, wts[i % C], epilogue=epi, residual=res, out=o, workspace=ws_),
                       args.reps)
             out[f"tc_{name}(m={m})"] = (t, n_rows * k_dim * 2)
+            tl = [K.gemm_tc_tile_weight(t_, silu=epi == K.EPI_SILU_MUL) for t_ in wts]
+            t = _time(lambda i: K.gemm_tc(xa, wts[i % C], epilogue=epi, residual=res, out=o, workspace=ws_,
+                                          tiled=tl[i % C]), args.reps)
+            out[f"tc_tiled_{name}(m={m})"] = (t, n_rows * k_dim * 2)
+            del tl
         if "tc_qkv" in tc:
             tc_case("qkv", g.qkv_dim, H, K.EPI_STORE, g.qkv_dim)
         if "tc_oproj" in tc:

@@ -145,3 +145,20 @@ def test_gemm_tc_f32_partials(m):
     ref = x.float() @ w.float().t()
     assert (out - ref).abs().max().item() <= 1e-3 * max(1.0, ref.abs().max().item())
     assert torch.equal(out.bfloat16(), K.gemm_tc(x, w))
+
+
+@pytest.mark.parametrize("m", [1, 32, 80])
+@pytest.mark.parametrize("n,k,epi", [(6144, 2560, K.EPI_STORE), (2560, 9728, K.EPI_RESIDUAL),
+                                     (19456, 2560, K.EPI_SILU_MUL), (2432, 2560, K.EPI_SILU_MUL),
+                                     (300, 264, K.EPI_STORE)])
+def test_gemm_tc_pretiled_weights_bit_identical(m, n, k, epi):
+    """Pre-tiled weights (one bulk copy per tile) give bit-identical results to the TMA-map path,
+    including ragged n and k (zero-padded tiles)."""
+    x = _rand((m, k), 1.0, f"tx{m}{k}")
+    w = _rand((n, k), 0.02, f"tw{n}{k}")
+    cols = n // 2 if epi == K.EPI_SILU_MUL else n
+    res = _rand((m, cols), 1.0, f"tr{m}{cols}")
+    tl = K.gemm_tc_tile_weight(w, silu=epi == K.EPI_SILU_MUL)
+    a = K.gemm_tc(x, w, epilogue=epi, residual=res)
+    b = K.gemm_tc(x, w, epilogue=epi, residual=res, tiled=tl)
+    assert torch.equal(a, b)
