@@ -71,6 +71,9 @@ def parse_args():
     ap.add_argument("--batched-cached", type=int, default=2048, help="cached positions per sequence (config 3)")
     ap.add_argument("--batched-steps", type=int, default=128)
     ap.add_argument("--no-verify", action="store_true", help="skip the config-4 speculative-verify section")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-5 prefill section")
+    ap.add_argument("--prefill-batch", type=int, default=16)
+    ap.add_argument("--prefill-len", type=int, default=4096)
     ap.add_argument("--allreduce", choices=("fused", "nccl"), default="fused",
                     help="tensor parallelism: fused one-shot P2P all-reduce in the CUDA-core linears, or NCCL")
     return ap.parse_args()
@@ -284,6 +287,42 @@ def run_batched(rt, comm, shard, batch: int, cached: int, steps: int, warmup: in
     return out
 
 
+def run_prefill(rt, comm, shard, batch: int, plen: int, decode_steps: int, world: int, peaks) -> dict:
+    """one-pass prefill of ``batch`` x ``plen`` uniform prompt ids (M = batch * plen
+    large-M tcgen05 GEMMs), then ``decode_steps`` greedy steps at that batch."""
+    from leanstack_b200.engine import DecodeEngine
+
+    g = QWEN3_4B
+    eng = DecodeEngine(rt, batch_size=batch, max_seq_len=plen + decode_steps + 16, linear_backend="tc", tp=comm,
+                       shard=shard)
+    eng.prefill_full(synth.token_ids((batch, 128), g.vocab_size, SEED, "cfg5/warm"))  # warm-up pass
+    torch.cuda.synchronize()
+    eng.reset()
+    prompt = synth.token_ids((batch, plen), g.vocab_size, SEED, "cfg5/prompt")
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    eng.prefill_full(prompt)
+    e1.record()
+    torch.cuda.synchronize()
+    t = max_over_ranks(e0.elapsed_time(e1) / 1000.0, world)
+    eng.capture()
+    td = _timed(eng.decode_step, decode_steps, 2, world)
+    gl = eng.g
+    lin_params = gl.qkv_dim * g.hidden_size + g.hidden_size * gl.q_dim + 2 * gl.intermediate_size * g.hidden_size + \
+        g.hidden_size * gl.intermediate_size
+    flops = 2.0 * batch * plen * lin_params * g.num_hidden_layers * world  # whole job (all ranks)
+    out = {"batch": batch, "prompt_len": plen, "m": batch * plen, "prefill_s": t,
+           "prefill_tok_per_s": batch * plen / t, "linear_tflops": flops / t / 1e12,
+           "linear_tensor_frac_per_gpu": flops / world / t / 1e12 / peaks.get("bf16_tflops", 1663.3),
+           "decode_steps": decode_steps, "decode_tok_per_s": batch * decode_steps / td,
+           "attention": "split-KV tensor-core decode kernel with q_len = prompt (no dedicated flash prefill yet)"}
+    eng.graph = None
+    del eng
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_verify(rt, comm, shard, steps: int, warmup: int, world: int, peaks) -> dict:
     """target verify at batch 16, k = 4 uniform proposals, 1024 cached (M = 80)."""
     from leanstack_b200 import kernels as K
@@ -467,6 +506,8 @@ def run_ours(args, world, rank, local):
                                        peaks)
     if not args.no_verify:
         extra["verify_cfg4"] = run_verify(rt, comm, shard, 64, 4, world, peaks)
+    if not args.no_prefill:
+        extra["prefill_cfg5"] = run_prefill(rt, comm, shard, args.prefill_batch, args.prefill_len, 64, world, peaks)
 
     # --- CPU baseline (rank 0, N == 1 only) ---
     cpu = None

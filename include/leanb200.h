@@ -125,6 +125,16 @@ int ls_rmsnorm_qkv_rope_kvappend(const void* x, int64_t batch, int64_t q_len, in
                                  void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* qkv_scratch,
                                  void* q_out, ls_stream_t stream);
 
+/* Large-M GEMM for prefill (m in the thousands; config 5: m = 65536):
+ * out[m, n] = epilogue(x[m, k] . W[n, k]^T) with the epilogues of
+ * ls_gemm_bf16_tcgen05, replacing the F.linear calls of the prefill layer
+ * (src/leanstack/runtime/qwen_explicit.py:809-829, :1093-1144).  Persistent
+ * tcgen05 kernel: 128 weight rows x 256 activation rows per tile (128 for
+ * SILU_MUL), the whole K per tile, tiles visited in L2-sized bands.  No
+ * workspace.  k a multiple of 8. */
+int ls_gemm_bf16_tcgen05_big(const void* x, int64_t m, int64_t k, const void* w, int64_t n, int epilogue,
+                             const void* residual, void* out, ls_stream_t stream);
+
 /* The same GEMM over weights pre-tiled once by ls_gemm_tc_tile_weight (the
  * leanpack-v1 tile layout): [ceil(n/128)][ceil(k/64)] tiles of 128 rows x 64 k,
  * each the 16 KB shared-memory image the MMA reads (128-byte swizzle), rows

@@ -381,6 +381,9 @@ int launch_decode_attention_tc(const void* q, const void* k_cache, const void* v
                                int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv,
                                int64_t max_seq, float scale, void* out, cudaStream_t stream) {
   const TaPlan pl = ta_plan(batch, q_len, hq, hkv, max_seq);
+  if ((int64_t)hkv * pl.RG > 65535)
+    return set_error(LS_ERR_UNSUPPORTED_SHAPE, "decode_attention: %lld kv heads x %d row groups exceed the grid",
+                     (long long)hkv, pl.RG);
   TaParams p = {};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k_cache = static_cast<const __nv_bfloat16*>(k_cache);

@@ -15,14 +15,14 @@ __device__ int g_device_error = 0;
 __global__ void embed_gather_kernel(const int64_t* ids, const __nv_bfloat16* embed, int64_t vocab, int hidden,
                                     __nv_bfloat16* out, int* err) {
   grid_dep_wait();
-  const int m = blockIdx.y;
+  const int m = blockIdx.x;  // one token per grid column (up to 2^31 - 1 tokens)
   const int64_t id = ids[m];
   const int vec = hidden >> 3;
   if (id < 0 || id >= vocab) {
-    if (threadIdx.x == 0 && blockIdx.x == 0) raise_device_error(err, LS_ERR_INVALID_ARGUMENT);
+    if (threadIdx.x == 0 && blockIdx.y == 0) raise_device_error(err, LS_ERR_INVALID_ARGUMENT);
     return;
   }
-  for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < vec; v += gridDim.x * blockDim.x)
+  for (int v = blockIdx.y * blockDim.x + threadIdx.x; v < vec; v += gridDim.y * blockDim.x)
     reinterpret_cast<uint4*>(out + (size_t)m * hidden)[v] =
         reinterpret_cast<const uint4*>(embed + (size_t)id * hidden)[v];
 }
@@ -235,6 +235,8 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
                    void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream,
                    const void* w_tiled = nullptr);
 int64_t tc_tiled_bytes(int64_t n_out, int64_t k, int silu);
+int launch_gemm_big(const void* x, int64_t m, int64_t k, const void* w, int64_t n_out, int epi, const void* residual,
+                    void* out, cudaStream_t stream);
 int launch_tc_tile(const void* w, int64_t n_rows, int64_t k, int silu, void* out, cudaStream_t stream);
 
 int decode_step_workspace_bytes(int64_t hkv, int64_t* bytes);
@@ -284,13 +286,14 @@ int ls_get_device_error(int* code, int clear) {
 int ls_embed_gather(const int64_t* ids, int64_t m, const void* embed, int64_t vocab, int64_t hidden, void* out,
                     ls_stream_t stream) {
   LS_REQUIRE(ids && embed && out, LS_ERR_INVALID_ARGUMENT, "ls_embed_gather: null pointer");
-  LS_REQUIRE(m > 0 && m <= 65535 && vocab > 0 && hidden > 0, LS_ERR_INVALID_ARGUMENT, "ls_embed_gather: bad sizes");
+  LS_REQUIRE(m > 0 && m < (1ll << 31) && vocab > 0 && hidden > 0 && hidden <= (1 << 20), LS_ERR_INVALID_ARGUMENT,
+             "ls_embed_gather: bad sizes");
   LS_REQUIRE(hidden % 8 == 0 && aligned16(embed) && aligned16(out), LS_ERR_MISALIGNED,
              "ls_embed_gather: hidden must be a multiple of 8 and pointers 16-byte aligned");
   const int vec = (int)(hidden / 8);
   const int threads = 128;
   const int blocks = (vec + threads - 1) / threads;
-  lsb::embed_gather_kernel<<<dim3(blocks, (unsigned)m), threads, 0, (cudaStream_t)stream>>>(
+  lsb::embed_gather_kernel<<<dim3((unsigned)m, blocks), threads, 0, (cudaStream_t)stream>>>(
       ids, static_cast<const __nv_bfloat16*>(embed), vocab, (int)hidden, static_cast<__nv_bfloat16*>(out),
       device_error_ptr());
   cudaError_t e = cudaGetLastError();
@@ -433,6 +436,13 @@ int ls_gemm_bf16_tcgen05(const void* x, int64_t m, int64_t k, const void* w, int
   return launch_gemm_tc(x, m, k, w, n, epilogue, residual, out, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
+int ls_gemm_bf16_tcgen05_big(const void* x, int64_t m, int64_t k, const void* w, int64_t n, int epilogue,
+                             const void* residual, void* out, ls_stream_t stream) {
+  LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32,
+             LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d", epilogue);
+  return launch_gemm_big(x, m, k, w, n, epilogue, residual, out, (cudaStream_t)stream);
+}
+
 int ls_gemm_tc_tiled_bytes(int64_t n_rows, int64_t k, int silu, int64_t* bytes) {
   LS_REQUIRE(bytes && n_rows > 0 && k > 0 && (!silu || n_rows % 2 == 0), LS_ERR_INVALID_ARGUMENT,
              "ls_gemm_tc_tiled_bytes: bad arguments");
@@ -464,7 +474,7 @@ int ls_qk_norm_rope_kvappend(const void* qkv, int64_t batch, int64_t q_len, int6
   LS_REQUIRE(head_dim == 128, LS_ERR_UNSUPPORTED_SHAPE, "head_dim=%lld (only 128 is implemented)",
              (long long)head_dim);
   LS_REQUIRE(batch > 0 && q_len > 0 && num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0 &&
-                 batch * q_len <= 65535,
+                 batch * q_len < (1ll << 31) && (num_heads + num_kv_heads + 3) / 4 <= 65535,
              LS_ERR_INVALID_ARGUMENT, "ls_qk_norm_rope_kvappend: bad sizes");
   LS_REQUIRE((k_cache == nullptr) == (v_cache == nullptr) && (k_out == nullptr) == (v_out == nullptr),
              LS_ERR_INVALID_ARGUMENT, "k/v cache and k/v out come in pairs");

@@ -400,6 +400,186 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Large-M GEMM (prefill, config 5): out[M, N] = epilogue(x[M, K] . w[N, K]^T)
+// for M in the thousands.  Persistent CTAs walk output tiles of 128 weight
+// rows (MMA M, operand A) x BN activation rows (MMA N, operand B: 256, or 128
+// for the SiLU pair whose gate and up tiles share one activation tile), each
+// over the whole K: no split-K, no partials.  Tiles are visited in bands of
+// kBgGroup activation tiles so that a band's activations and the weight tiles
+// in use stay in L2.  Warp roles as in gemm_tc_kernel; two TMEM accumulators
+// (512 columns) let the epilogue of one tile overlap the MMAs of the next.
+// ---------------------------------------------------------------------------
+constexpr int kBgGroup = 16;
+
+struct BgParams {
+  const __nv_bfloat16* residual;  // [M, N]
+  void* out;                      // [M, N] bf16 (fp32 for STORE_F32)
+  int* err;
+  int M, N, tiles_n, tiles_m, kblocks, BN, stages, stage_bytes;
+};
+
+__device__ __forceinline__ void bg_tile(int i, const BgParams& p, int& tn, int& tm) {
+  const int band_tiles = kBgGroup * p.tiles_n;
+  const int band = i / band_tiles, j = i - band * band_tiles;
+  const int gm = min(kBgGroup, p.tiles_m - band * kBgGroup);
+  tm = band * kBgGroup + j % gm;
+  tn = j / gm;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_big_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
+                    const __grid_constant__ CUtensorMap tm_x, BgParams p) {
+  constexpr bool SILU = (EPI == TEPI_SILU_MUL);
+  constexpr int ACCS = SILU ? 2 : 1;
+  constexpr uint32_t kWBytes = kTcTileN * kTcBlockK * 2;
+  extern __shared__ unsigned char bg_smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<size_t>(bg_smem_raw) + 1023) & ~size_t(1023));
+  const int NS = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)NS * p.stage_bytes);
+  uint64_t* empty = full + NS;
+  uint64_t* acc_full = empty + NS;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  __shared__ int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = p.tiles_n * p.tiles_m;
+  const int KB = p.kblocks;
+  const uint32_t x_bytes = (uint32_t)p.BN * kTcBlockK * 2;
+  const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.BN >> 3) << 17) |
+                         ((uint32_t)(kTcTileN >> 4) << 24);
+  const uint32_t acc_cols = (uint32_t)(p.BN * ACCS);
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < NS; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], kTcEpiThreads);
+    }
+    s_abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  grid_dep_launch();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {  // TMA producer
+      grid_dep_wait();
+      long long it = 0;
+      for (int i = blockIdx.x; i < total && !*(volatile int*)&s_abort; i += gridDim.x) {
+        int tn, tm;
+        bg_tile(i, p, tn, tm);
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int st = (int)(it % NS);
+          if (it >= NS && !mbar_wait(&empty[st], (uint32_t)((it / NS) - 1) & 1u, p.err, 17)) {
+            s_abort = 1;
+            break;
+          }
+          unsigned char* sp = smem + (size_t)st * p.stage_bytes;
+          mbar_arrive_expect_tx(&full[st], kWBytes * ACCS + x_bytes);
+          tma_load_2d(sp, &tm_w, kb * kTcBlockK, tn * kTcTileN, &full[st]);
+          if (SILU) tma_load_2d(sp + kWBytes, &tm_w2, kb * kTcBlockK, tn * kTcTileN, &full[st]);
+          tma_load_2d(sp + kWBytes * ACCS, &tm_x, kb * kTcBlockK, tm * p.BN, &full[st]);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {  // MMA issuer
+      long long it = 0;
+      int lt = 0;
+      for (int i = blockIdx.x; i < total && !*(volatile int*)&s_abort; i += gridDim.x, ++lt) {
+        const int a = lt & 1;
+        if (lt >= 2 && !mbar_wait(&acc_empty[a], (uint32_t)((lt >> 1) - 1) & 1u, p.err, 18)) {
+          s_abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc_tmem = tmem + (uint32_t)a * acc_cols;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int st = (int)(it % NS);
+          if (!mbar_wait(&full[st], (uint32_t)(it / NS) & 1u, p.err, 19)) {
+            s_abort = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sw = smem_u32(smem + (size_t)st * p.stage_bytes);
+          const uint32_t sx = sw + kWBytes * ACCS;
+#pragma unroll
+          for (int kk = 0; kk < kTcBlockK / 16; ++kk) {
+            const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+            const uint64_t bdesc = umma_desc_sw128(sx + kk * 32);
+            umma_f16(acc_tmem, umma_desc_sw128(sw + kk * 32), bdesc, idesc, acc);
+            if (SILU) umma_f16(acc_tmem + (uint32_t)p.BN, umma_desc_sw128(sw + kWBytes + kk * 32), bdesc, idesc, acc);
+          }
+          umma_commit(&empty[st]);
+        }
+        umma_commit(&acc_full[a]);
+      }
+    }
+  } else {  // epilogue: warps 0-3 own TMEM lanes 0-127 (= weight rows of the tile)
+    grid_dep_wait();
+    const int row = warp * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    int lt = 0;
+    for (int i = blockIdx.x; i < total; i += gridDim.x, ++lt) {
+      int tn, tm;
+      bg_tile(i, p, tn, tm);
+      const int a = lt & 1;
+      if (!mbar_wait(&acc_full[a], (uint32_t)(lt >> 1) & 1u, p.err, 20)) s_abort = 1;
+      named_bar_sync(1, kTcEpiThreads);
+      if (*(volatile int*)&s_abort) break;
+      tc_fence_after();
+      const uint32_t acc_addr = tmem + lane_off + (uint32_t)a * acc_cols;
+      const int n = tn * kTcTileN + row;
+      for (int cb = 0; cb < p.BN; cb += 16) {
+        float v[16], w2[16];
+        tmem_ld16(acc_addr + (uint32_t)cb, v);
+        if (SILU) tmem_ld16(acc_addr + (uint32_t)(p.BN + cb), w2);
+        if (n < p.N) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int b = tm * p.BN + cb + j;
+            if (b < p.M) {
+              const size_t o = (size_t)b * p.N + n;
+              float y = v[j];
+              if (EPI == TEPI_RESIDUAL) y = bf16_to_f(p.residual[o]) + round_bf16(y);
+              if (SILU) {
+                const float g = round_bf16(v[j]);
+                y = round_bf16(g / (1.0f + expf(-g))) * round_bf16(w2[j]);
+              }
+              if (EPI == TEPI_STORE_F32) reinterpret_cast<float*>(p.out)[o] = y;
+              else reinterpret_cast<__nv_bfloat16*>(p.out)[o] = f_to_bf16(y);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[a]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+  }
+}
+
 }  // namespace lsb
 
 // ---------------------------------------------------------------------------
@@ -585,6 +765,80 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
     case TEPI_SILU_MUL: return launch_tc_t<TEPI_SILU_MUL>(mw, mw2, mx, p, pl, stream);
     case TEPI_STORE_F32: return launch_tc_t<TEPI_STORE_F32>(mw, mw2, mx, p, pl, stream);
     default: return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_tc: unknown epilogue %d", epi);
+  }
+}
+
+
+template <int EPI>
+static int launch_big_t(const CUtensorMap& w, const CUtensorMap& w2, const CUtensorMap& x, const BgParams& p,
+                        int grid, size_t smem, cudaStream_t stream) {
+  auto kern = gemm_big_kernel<EPI>;
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && (int)smem > configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "cudaFuncSetAttribute(gemm_big): %s", cudaGetErrorString(e));
+    configured[dev] = (int)smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, w, w2, x, p);
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "gemm_big launch: %s", cudaGetErrorString(e));
+}
+
+// Large-M GEMM (see gemm_big_kernel); any m >= 1, k a multiple of 8.
+int launch_gemm_big(const void* x, int64_t m, int64_t k, const void* w, int64_t n_out, int epi, const void* residual,
+                    void* out, cudaStream_t stream) {
+  if (!x || !w || !out) return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_big: null pointer");
+  if (m < 1 || m > (1ll << 30) || n_out < 1 || k < 8 || k % 8)
+    return set_error(LS_ERR_UNSUPPORTED_SHAPE, "gemm_big: m=%lld k=%lld n=%lld", (long long)m, (long long)k,
+                     (long long)n_out);
+  if (!aligned16(x) || !aligned16(w)) return set_error(LS_ERR_MISALIGNED, "gemm_big: x and w must be 16-byte aligned");
+  if (epi == TEPI_RESIDUAL && !residual) return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_big: residual is null");
+  const bool silu = epi == TEPI_SILU_MUL;
+  if (silu && ((n_out * k * 2) % 16)) return set_error(LS_ERR_MISALIGNED, "gemm_big: up-projection view misaligned");
+  BgParams p = {};
+  p.BN = silu ? 128 : 256;
+  p.M = (int)m;
+  p.N = (int)n_out;
+  p.tiles_n = (int)((n_out + kTcTileN - 1) / kTcTileN);
+  p.tiles_m = (int)((m + p.BN - 1) / p.BN);
+  p.kblocks = (int)((k + kTcBlockK - 1) / kTcBlockK);
+  p.stage_bytes = (silu ? 2 : 1) * kTcTileN * kTcBlockK * 2 + p.BN * kTcBlockK * 2;  // 48 KB either way
+  p.stages = 4;
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.out = out;
+  p.err = device_error_ptr();
+  const long long total = (long long)p.tiles_n * p.tiles_m;
+  if (total > (1ll << 31) - 1) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "gemm_big: too many tiles");
+  const int grid = (int)(total < sm_count() ? total : sm_count());
+  const size_t smem = 1024 + (size_t)p.stages * p.stage_bytes + (size_t)(2 * p.stages + 4) * 8 + 16;
+  CUtensorMap mw, mw2, mx;
+  int rc = make_map(&mw, w, n_out, k, kTcTileN);
+  if (rc) return rc;
+  if (silu) {
+    rc = make_map(&mw2, static_cast<const __nv_bfloat16*>(w) + n_out * k, n_out, k, kTcTileN);
+    if (rc) return rc;
+  } else {
+    mw2 = mw;
+  }
+  rc = make_map(&mx, x, m, k, p.BN);
+  if (rc) return rc;
+  switch (epi) {
+    case TEPI_STORE: return launch_big_t<TEPI_STORE>(mw, mw2, mx, p, grid, smem, stream);
+    case TEPI_RESIDUAL: return launch_big_t<TEPI_RESIDUAL>(mw, mw2, mx, p, grid, smem, stream);
+    case TEPI_SILU_MUL: return launch_big_t<TEPI_SILU_MUL>(mw, mw2, mx, p, grid, smem, stream);
+    case TEPI_STORE_F32: return launch_big_t<TEPI_STORE_F32>(mw, mw2, mx, p, grid, smem, stream);
+    default: return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_big: unknown epilogue %d", epi);
   }
 }
 

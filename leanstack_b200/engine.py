@@ -225,27 +225,87 @@ class DecodeEngine:
             else:
                 a.head_rows.copy_(a.x[:m].view(B, q_len, -1)[:, -1])
                 rows, n, dest = a.head_rows, B, a.ids[:B]
-            self._head_rows = rows
-            if self.tp is not None:
-                keys = self.keys[:n]
-                if tc:
-                    K.rmsnorm(rows, rt.final_norm_weight, eps, out=self.xn[:n])
-                    K.gemm_tc(self.xn[:n], rt.lm_head_weight, out=self.logits[:n], workspace=self.tc_ws)
-                    K.argmax_rows_keys(self.logits[:n], self.vocab_offset, out_keys=keys, workspace=self.lm_ws)
-                else:
-                    K.lmhead_argmax_keys(rows, rt.final_norm_weight, rt.lm_head_weight, eps, self.vocab_offset,
-                                         out_keys=keys, workspace=self.lm_ws)
-                self.tp.all_reduce_max(keys)
-                K.argmax_keys_to_ids(keys, out_ids=dest)
-            elif tc:
-                K.rmsnorm(rows, rt.final_norm_weight, eps, out=self.xn[:n])
-                K.gemm_tc(self.xn[:n], rt.lm_head_weight, out=self.logits[:n], workspace=self.tc_ws)
-                K.argmax_rows(self.logits[:n], out_ids=dest, workspace=self.lm_ws)
-            else:
-                K.lmhead_argmax(rows, rt.final_norm_weight, rt.lm_head_weight, eps, out_ids=dest,
-                                workspace=self.lm_ws)
+            self._head(rows, n, dest, tc)
         if advance:
             K.advance_cursors(kv.cache_pos, q_len)
+
+    def _head(self, rows: torch.Tensor, n: int, dest: torch.Tensor, tc: bool) -> None:
+        """Greedy head over ``rows [n, H]``: final norm, lm_head (this rank's vocab shard), argmax into ``dest``."""
+        rt, eps = self.rt, self.g.rms_norm_eps
+        self._head_rows = rows
+        if self.tp is not None:
+            keys = self.keys[:n]
+            if tc:
+                K.rmsnorm(rows, rt.final_norm_weight, eps, out=self.xn[:n])
+                K.gemm_tc(self.xn[:n], rt.lm_head_weight, out=self.logits[:n], workspace=self.tc_ws)
+                K.argmax_rows_keys(self.logits[:n], self.vocab_offset, out_keys=keys, workspace=self.lm_ws)
+            else:
+                K.lmhead_argmax_keys(rows, rt.final_norm_weight, rt.lm_head_weight, eps, self.vocab_offset,
+                                     out_keys=keys, workspace=self.lm_ws)
+            self.tp.all_reduce_max(keys)
+            K.argmax_keys_to_ids(keys, out_ids=dest)
+        elif tc:
+            K.rmsnorm(rows, rt.final_norm_weight, eps, out=self.xn[:n])
+            K.gemm_tc(self.xn[:n], rt.lm_head_weight, out=self.logits[:n], workspace=self.tc_ws)
+            K.argmax_rows(self.logits[:n], out_ids=dest, workspace=self.lm_ws)
+        else:
+            K.lmhead_argmax(rows, rt.final_norm_weight, rt.lm_head_weight, eps, out_ids=dest, workspace=self.lm_ws)
+
+    def prefill_full(self, prompt_ids: torch.Tensor) -> torch.Tensor:
+        """Prefill ``[B, P]`` prompts in one pass per layer.
+
+        All B·P tokens go through each layer together: the linears run as
+        large-M tcgen05 GEMMs (``ls_gemm_bf16_tcgen05_big``), attention runs
+        causally over each sequence (the decode kernel with q_len = P), and the
+        K/V of every position land in the cache.  Activations for the pass are
+        allocated for its duration.  Returns the first greedy token per
+        sequence ``[B]``; the cursors advance by P.
+        """
+        if prompt_ids.dim() != 2 or prompt_ids.shape[0] != self.B:
+            raise ValueError(f"prompt_ids must be [{self.B}, P]")
+        B, P = prompt_ids.shape
+        if len(set(self.kv.sequence_lens)) != 1 or self.kv.sequence_lens[0] + P > self.S:
+            raise ValueError("prefill_full needs equal cursors and room for the prompt")
+        g, rt, a, kv = self.g, self.rt, self.arenas, self.kv
+        dev, dt, eps, m = rt.device, rt.dtype, g.rms_norm_eps, B * P
+        ids = prompt_ids.to(dev, torch.int64).reshape(-1)
+        x = torch.empty(m, g.hidden_size, device=dev, dtype=dt)
+        h = torch.empty_like(x)
+        xn = torch.empty_like(x)
+        qkv = torch.empty(m, g.qkv_dim, device=dev, dtype=dt)
+        q = torch.empty(m, g.num_attention_heads, g.head_dim, device=dev, dtype=dt)
+        attn = torch.empty(m, g.q_dim, device=dev, dtype=dt)
+        act = torch.empty(m, g.intermediate_size, device=dev, dtype=dt)
+        part = torch.empty(m, g.hidden_size, device=dev, dtype=torch.float32) if self.tp is not None else None
+
+        def row_split(inp, w, res, out):
+            if self.tp is None:
+                K.gemm_big(inp, w, epilogue=K.EPI_RESIDUAL, residual=res, out=out)
+            else:
+                K.gemm_big(inp, w, epilogue=K.EPI_STORE_F32, out=part)
+                self.tp.all_reduce_sum(part)
+                K.residual_add_f32(res, part, out=out)
+
+        K.embed_gather(ids, rt.embed_tokens_weight, out=x)
+        for li, layer in enumerate(rt.layers):
+            att, mlp = layer.attention, layer.mlp
+            K.rmsnorm(x, layer.input_layernorm_weight, eps, out=xn)
+            K.gemm_big(xn, att.qkv_proj_weight, out=qkv)
+            K.qk_norm_rope(qkv, B, P, g.num_attention_heads, g.num_key_value_heads, g.head_dim, att.q_norm_weight,
+                           att.k_norm_weight, self.cos, self.sin, eps=eps, cache_pos=kv.cache_pos,
+                           k_cache=kv.key_cache[li], v_cache=kv.value_cache[li], max_seq=self.S, q_out=q)
+            K.decode_attention(q, kv.key_cache[li], kv.value_cache[li], B, P, g.num_attention_heads,
+                               g.num_key_value_heads, g.head_dim, self.S, att.attention_scale,
+                               cache_pos=kv.cache_pos, out=attn, workspace=self.attn_ws)
+            row_split(attn, att.o_proj_weight, x, h)
+            K.rmsnorm(h, layer.post_attention_layernorm_weight, eps, out=xn)
+            K.gemm_big(xn, mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=act)
+            row_split(act, mlp.down_proj_weight, h, x)
+        a.head_rows.copy_(x.view(B, P, -1)[:, -1])
+        self._head(a.head_rows, B, a.ids[:B], self.backend == "tc")
+        K.advance_cursors(kv.cache_pos, P)
+        kv.note_advanced(P)
+        return a.ids[:B].clone()
 
     def _row_split(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor, out: torch.Tensor,
                    tc: bool) -> None:

@@ -366,6 +366,26 @@ def decode_step(layer_table: torch.Tensor, num_layers: int, hidden: int, interme
              qkv.data_ptr(), attn.data_ptr(), act.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
 
 
+def gemm_big(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """Large-M tcgen05 GEMM (prefill): ``out = epilogue(x @ w.T)`` for x ``[m, k]`` with m in the thousands."""
+    _check(x, "x")
+    _check(w, "w")
+    k = x.shape[-1]
+    m = x.numel() // k
+    n = w.shape[0] // 2 if epilogue == EPI_SILU_MUL else w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"weight in-features {w.shape[1]} != activation width {k}")
+    if residual is not None:
+        _check(residual, "residual")
+    if out is None:
+        out = torch.empty((*x.shape[:-1], n), device=x.device,
+                          dtype=torch.float32 if epilogue == EPI_STORE_F32 else BF16)
+    nat.call("ls_gemm_bf16_tcgen05_big", x.data_ptr(), m, k, w.data_ptr(), n, int(epilogue), _ptr(residual),
+             out.data_ptr(), _stream())
+    return out
+
+
 def gemm_tc_tile_weight(w: torch.Tensor, silu: bool = False) -> torch.Tensor:
     """Tile a ``[N, K]`` weight for :func:`gemm_tc` (``tiled=``): 16 KB MMA-image tiles (uint8 buffer)."""
     _check(w, "w")

@@ -162,3 +162,29 @@ def test_gemm_tc_pretiled_weights_bit_identical(m, n, k, epi):
     a = K.gemm_tc(x, w, epilogue=epi, residual=res)
     b = K.gemm_tc(x, w, epilogue=epi, residual=res, tiled=tl)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 2560, 4096), (1000, 6144, 2560), (4096, 2560, 9728), (777, 300, 264),
+                                   (1, 2560, 2560)])
+def test_gemm_big_store_residual(m, n, k):
+    """Large-M prefill GEMM against fp32 torch, ragged m / n / k (partial tiles)."""
+    x = _rand((m, k), 1.0, f"bx{m}{k}")
+    w = _rand((n, k), 0.02, f"bw{n}{k}")
+    ref = x.float() @ w.float().t()
+    _check(K.gemm_big(x, w), ref)
+    res = _rand((m, n), 1.0, f"br{m}{n}")
+    _check(K.gemm_big(x, w, epilogue=K.EPI_RESIDUAL, residual=res), res.float() + ref.bfloat16().float())
+    f32 = K.gemm_big(x, w, epilogue=K.EPI_STORE_F32)
+    assert (f32 - ref).abs().max().item() <= 1e-3 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("m", [384, 2048])
+def test_gemm_big_silu(m):
+    x = _rand((m, 2560), 1.0, f"bsx{m}")
+    w = _rand((2 * 9728, 2560), 0.02, "bsw")
+    out = K.gemm_big(x, w, epilogue=K.EPI_SILU_MUL)
+    gu = (x.float() @ w.float().t()).bfloat16()
+    ref = F.silu(gu[:, :9728]).bfloat16().float() * gu[:, 9728:].float()
+    _check(out, ref)
+    dec = K.gemm_tc(x[:128].contiguous(), w, epilogue=K.EPI_SILU_MUL)  # the decode GEMM on a 128-row slice
+    assert (out[:128].float() - dec.float()).abs().max().item() <= tol(dec.float())

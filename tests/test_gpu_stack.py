@@ -223,3 +223,32 @@ def test_cfg2_4b_greedy_stream_teacher_forced(golden_dir, backend):
     for i in mism:
         assert margins[i] <= NEAR_TIE, f"step {i}: mismatch with reference margin {margins[i]}"
     assert len(mism) <= 8
+
+
+def test_prefill_full_matches_chunked_prefill():
+    """One-pass prefill (large-M GEMMs, causal attention over the whole prompt)
+    gives the chunked prefill's first tokens and greedy continuation (tiny
+    stack), and the same last hidden rows within the bound (Qwen3-4B, 2 x 384)."""
+    rt = _tiny_runtime()
+    prompt = synth.token_ids((3, 40), TINY.vocab_size, 5, "pf/prompt")
+    a = DecodeEngine(rt, batch_size=3, max_seq_len=64, linear_backend="tc")
+    b = DecodeEngine(rt, batch_size=3, max_seq_len=64, linear_backend="tc")
+    first_a = a.prefill(prompt)
+    first_b = b.prefill_full(prompt)
+    assert torch.equal(first_a, first_b)
+    for _ in range(6):
+        a.decode_step()
+        b.decode_step()
+        assert torch.equal(a.current_ids, b.current_ids)
+    g = QWEN3_4B
+    from dataclasses import replace
+    g4 = replace(g, num_hidden_layers=4)
+    rt4 = materialize_from_tensors(g4, synth.synth_checkpoint(g4, 1, device=DEV), device=DEV, free_source=True)
+    prompt4 = synth.token_ids((2, 384), g.vocab_size, 1, "pf4/prompt")
+    c = DecodeEngine(rt4, batch_size=2, max_seq_len=512, linear_backend="tc")
+    d = DecodeEngine(rt4, batch_size=2, max_seq_len=512, linear_backend="tc")
+    c.prefill(prompt4)
+    d.prefill_full(prompt4)
+    hc, hd = c.last_head_rows().float(), d.last_head_rows().float()
+    assert (hc - hd).abs().max().item() <= tol(hc)
+    assert c.kv.sequence_lens == d.kv.sequence_lens == [384, 384]
