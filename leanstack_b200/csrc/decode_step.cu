@@ -234,14 +234,21 @@ __device__ void ds_gemv(const __nv_bfloat16* W, int N, int K, const __nv_bfloat1
     if (lane == 0 && t - t_first < seg_cap) segbuf[warp * seg_cap + (t - t_first)] = a;
     g += seg;
   }
+  // Rows [s_wr0[w], s_wr1[w]] of warp w (empty: r0 > r1), once per call instead of per output.
+  __shared__ int s_wr0[kDsWarps], s_wr1[kDsWarps];
+  if (tid < kDsWarps) {
+    const int wb = (int)(((int64_t)total * tid) / kDsWarps);
+    const int we = (int)(((int64_t)total * (tid + 1)) / kDsWarps);
+    s_wr0[tid] = wb < we ? wb / gpr : 1;
+    s_wr1[tid] = wb < we ? (we - 1) / gpr : 0;
+  }
   __syncthreads();
   auto row_sum = [&](int t) -> float {
     float s = 0.f;
-    const int lo = t * gpr, hi = lo + gpr;
+#pragma unroll 4
     for (int w = 0; w < kDsWarps; ++w) {
-      const int wb = (int)(((int64_t)total * w) / kDsWarps);
-      const int we = (int)(((int64_t)total * (w + 1)) / kDsWarps);
-      if (wb < we && wb < hi && we > lo) s += segbuf[w * seg_cap + (t - wb / gpr)];
+      const int f = s_wr0[w];
+      if (t >= f && t <= s_wr1[w]) s += segbuf[w * seg_cap + (t - f)];
     }
     return s;
   };

@@ -208,14 +208,23 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
   }
   __syncthreads();
 
-  // Sum of local row t for activation row m over the warps that cover it.
+  // Sum of local row t for activation row m over the warps that cover it, in
+  // warp order.  Warp w covers local rows [s_wr0[w], s_wr1[w]] (empty: r0 > r1),
+  // computed once per CTA instead of per output.
+  __shared__ int s_wr0[kLinWarps], s_wr1[kLinWarps];
+  if (tid < kLinWarps) {
+    const int wb = (int)(((int64_t)total * tid) / kLinWarps);
+    const int we = (int)(((int64_t)total * (tid + 1)) / kLinWarps);
+    s_wr0[tid] = wb < we ? wb / gpr : 1;
+    s_wr1[tid] = wb < we ? (we - 1) / gpr : 0;
+  }
+  __syncthreads();
   auto row_sum = [&](int m, int t) -> float {
     float s = 0.f;
-    const int lo = t * gpr, hi = lo + gpr;
+#pragma unroll 4
     for (int w = 0; w < kLinWarps; ++w) {
-      const int wb = (int)(((int64_t)total * w) / kLinWarps);
-      const int we = (int)(((int64_t)total * (w + 1)) / kLinWarps);
-      if (wb < we && wb < hi && we > lo) s += segbuf[((size_t)w * ms + (t - wb / gpr)) * M + m];
+      const int f = s_wr0[w];
+      if (t >= f && t <= s_wr1[w]) s += segbuf[((size_t)w * ms + (t - f)) * M + m];
     }
     return s;
   };

@@ -230,3 +230,36 @@ def test_linear_f32_partials_and_residual_add(m):
     # Same rounding points as the fused residual epilogue.
     y1 = K.residual_add_f32(res, full)
     assert (y1 == K.oproj_residual(x, w, res)).float().mean().item() > 0.99
+
+
+@pytest.mark.parametrize("batch,q_len,past", [(1, 64, 0), (2, 200, 37), (1, 512, 0), (2, 96, 300)])
+def test_prefill_attention_matches_fp64(batch, q_len, past):
+    """Long query blocks (>= 256 rows per kv head) take the 128-row prefill kernel;
+    causal rule key j <= cache_pos + i, against an fp64 softmax of the same bf16 inputs."""
+    hq, hkv, d, S = 32, 8, 128, 1024
+    gen = torch.Generator(device="cpu").manual_seed(7 + q_len)
+    q = torch.randn(batch * q_len, hq, d, generator=gen).bfloat16().to(DEV)
+    kc = torch.randn(batch, hkv, S, d, generator=gen).bfloat16().to(DEV)
+    vc = torch.randn(batch, hkv, S, d, generator=gen).bfloat16().to(DEV)
+    pos = torch.tensor([past + 5 * b for b in range(batch)], dtype=torch.int32, device=DEV)
+    scale = d ** -0.5
+    out = K.decode_attention(q, kc, vc, batch, q_len, hq, hkv, d, S, scale, cache_pos=pos)
+    torch.cuda.synchronize()
+    qc, kcc, vcc = q.cpu().double(), kc.cpu().double(), vc.cpu().double()
+    G = hq // hkv
+    ref = torch.empty(batch * q_len, hq, d, dtype=torch.float64)
+    for b in range(batch):
+        cp = int(pos[b])
+        L = cp + q_len
+        for h in range(hq):
+            k = kcc[b, h // G, :L]
+            v = vcc[b, h // G, :L]
+            s = (qc[b * q_len:(b + 1) * q_len, h] @ k.t()) * scale
+            mask = torch.arange(L)[None, :] > (cp + torch.arange(q_len))[:, None]
+            s = s.masked_fill(mask, float("-inf"))
+            ref[b * q_len:(b + 1) * q_len, h] = torch.softmax(s, -1) @ v
+    ref = ref.view(batch * q_len, hq * d)
+    err = (out.double().cpu() - ref).abs().max().item()
+    assert err <= 1e-2, err
+    assert (out.cpu() == ref.bfloat16()).float().mean().item() > 0.99
+    assert K.device_error() == 0
