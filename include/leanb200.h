@@ -185,6 +185,18 @@ int ls_decode_attention(const void* q, const void* k_cache, const void* v_cache,
                         int64_t uniform_past, int64_t batch, int64_t q_len, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
                         int64_t max_seq, float scale, void* out, void* workspace, int64_t workspace_bytes,
                         ls_stream_t stream);
+/* Decode / verify attention with the q/k RMSNorm, RoPE and K/V append of
+ * ls_qk_norm_rope_kvappend folded in (one launch instead of two): reads the
+ * raw fused-QKV rows qkv [batch * q_len, (Hq + 2 Hkv) * 128], normalises and
+ * rotates q in registers, and the CTAs that stream a new position write its
+ * K/V into the cache first.  Same rounding as the two-kernel form
+ * (qwen_explicit.py:733-806, :886-903, :1000-1039).  Up to 16 * 65535 query
+ * rows per kv head. */
+int ls_decode_attention_fused(const void* qkv, int64_t batch, int64_t q_len, int64_t num_heads,
+                              int64_t num_kv_heads, int64_t head_dim, const void* q_norm_w, const void* k_norm_w,
+                              float eps, const void* rope_cos, const void* rope_sin, int64_t rope_len,
+                              int64_t rope_offset, const int32_t* cache_pos, int64_t uniform_past, void* k_cache,
+                              void* v_cache, int64_t max_seq, float scale, void* out, ls_stream_t stream);
 int ls_decode_attention_workspace_bytes(int64_t batch, int64_t q_len, int64_t num_heads, int64_t num_kv_heads,
                                         int64_t head_dim, int64_t max_seq, int64_t* bytes);
 

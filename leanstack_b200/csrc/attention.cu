@@ -159,9 +159,11 @@ int attention_workspace_bytes(int64_t batch, int64_t q_len, int64_t hq, int64_t 
   return LS_OK;
 }
 
+struct TaFused;
 int launch_decode_attention_tc(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
                                int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv,
-                               int64_t max_seq, float scale, void* out, cudaStream_t stream);
+                               int64_t max_seq, float scale, void* out, cudaStream_t stream,
+                               const TaFused* fused = nullptr);
 
 int launch_prefill_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
                              int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv,

@@ -235,6 +235,11 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
                    void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream,
                    const void* w_tiled = nullptr);
 int64_t tc_tiled_bytes(int64_t n_out, int64_t k, int silu);
+int launch_decode_attention_fused(const void* qkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                                  const void* cos, const void* sin, int64_t rope_len, int64_t rope_offset,
+                                  void* k_cache, void* v_cache, const int32_t* cache_pos, int64_t uniform_past,
+                                  int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int64_t max_seq,
+                                  float scale, void* out, cudaStream_t stream);
 int launch_gemm_big(const void* x, int64_t m, int64_t k, const void* w, int64_t n_out, int epi, const void* residual,
                     void* out, cudaStream_t stream);
 int launch_tc_tile(const void* w, int64_t n_rows, int64_t k, int silu, void* out, cudaStream_t stream);
@@ -434,6 +439,27 @@ int ls_gemm_bf16_tcgen05(const void* x, int64_t m, int64_t k, const void* w, int
   LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32,
              LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d", epilogue);
   return launch_gemm_tc(x, m, k, w, n, epilogue, residual, out, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int ls_decode_attention_fused(const void* qkv, int64_t batch, int64_t q_len, int64_t num_heads,
+                              int64_t num_kv_heads, int64_t head_dim, const void* q_norm_w, const void* k_norm_w,
+                              float eps, const void* rope_cos, const void* rope_sin, int64_t rope_len,
+                              int64_t rope_offset, const int32_t* cache_pos, int64_t uniform_past, void* k_cache,
+                              void* v_cache, int64_t max_seq, float scale, void* out, ls_stream_t stream) {
+  LS_REQUIRE(qkv && q_norm_w && k_norm_w && rope_cos && rope_sin && k_cache && v_cache && out,
+             LS_ERR_INVALID_ARGUMENT, "ls_decode_attention_fused: null pointer");
+  LS_REQUIRE(head_dim == 128, LS_ERR_UNSUPPORTED_SHAPE, "head_dim=%lld (only 128 is implemented)",
+             (long long)head_dim);
+  LS_REQUIRE(batch > 0 && batch <= 65535 && q_len > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0 &&
+                 max_seq > 0 && rope_len > 0 && rope_offset >= 0,
+             LS_ERR_INVALID_ARGUMENT, "ls_decode_attention_fused: bad sizes");
+  LS_REQUIRE(cache_pos || (uniform_past >= 0 && uniform_past + q_len <= max_seq), LS_ERR_KV_OVERFLOW,
+             "ls_decode_attention_fused: uniform_past + q_len beyond max_seq");
+  LS_REQUIRE(aligned16(qkv) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out), LS_ERR_MISALIGNED,
+             "ls_decode_attention_fused: pointers must be 16-byte aligned");
+  return launch_decode_attention_fused(qkv, q_norm_w, k_norm_w, eps, rope_cos, rope_sin, rope_len, rope_offset,
+                                       k_cache, v_cache, cache_pos, uniform_past, batch, q_len, num_heads,
+                                       num_kv_heads, max_seq, scale, out, (cudaStream_t)stream);
 }
 
 int ls_gemm_bf16_tcgen05_big(const void* x, int64_t m, int64_t k, const void* w, int64_t n, int epilogue,

@@ -366,6 +366,23 @@ def decode_step(layer_table: torch.Tensor, num_layers: int, hidden: int, interme
              qkv.data_ptr(), attn.data_ptr(), act.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
 
 
+def decode_attention_fused(qkv: torch.Tensor, batch: int, q_len: int, num_heads: int, num_kv_heads: int,
+                           head_dim: int, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor, cos: torch.Tensor,
+                           sin: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, max_seq: int, scale: float,
+                           *, eps: float = 1e-6, cache_pos: torch.Tensor | None = None, uniform_past: int = 0,
+                           rope_offset: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention from the raw QKV rows with q/k norm, RoPE and the K/V append folded in."""
+    _check(qkv, "qkv")
+    m = batch * q_len
+    if out is None:
+        out = torch.empty((m, num_heads * head_dim), device=qkv.device, dtype=BF16)
+    nat.call("ls_decode_attention_fused", qkv.data_ptr(), batch, q_len, num_heads, num_kv_heads, head_dim,
+             q_norm_w.data_ptr(), k_norm_w.data_ptr(), float(eps), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
+             int(rope_offset), _ptr(cache_pos), int(uniform_past), k_cache.data_ptr(), v_cache.data_ptr(), max_seq,
+             float(scale), out.data_ptr(), _stream())
+    return out
+
+
 def gemm_big(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,
              out: torch.Tensor | None = None) -> torch.Tensor:
     """Large-M tcgen05 GEMM (prefill): ``out = epilogue(x @ w.T)`` for x ``[m, k]`` with m in the thousands."""
