@@ -130,6 +130,22 @@ def main(argv=None) -> int:
         xe = torch.empty(m, H, device=dev, dtype=torch.bfloat16)
         t = _time(lambda i: K.embed_gather(ids, emb, out=xe), args.reps)
         out["embed"] = (t, m * H * 2)
+    big = {k for k in wanted if k.startswith("big_")}
+    if big:  # large-M prefill GEMM; --m is the token count (e.g. 4096)
+        def big_case(name, n_rows, k_dim, epi):
+            wts = w((n_rows, k_dim), "mb/big" + name)
+            xa = synth.normal((m, k_dim), 1.0, 0, "mb/bx" + name, device=dev)
+            n_out = n_rows // 2 if epi == K.EPI_SILU_MUL else n_rows
+            res = synth.normal((m, n_out), 1.0, 0, "mb/bres" + name, device=dev)
+            o = torch.empty(m, n_out, device=dev, dtype=torch.bfloat16)
+            t = _time(lambda i: K.gemm_big(xa, wts[i % C], epilogue=epi, residual=res, out=o), args.reps)
+            out[f"big_{name}(m={m})"] = (t, 2.0 * m * n_rows * k_dim)  # FLOPs, not bytes
+        if "big_qkv" in big:
+            big_case("qkv", g.qkv_dim, H, K.EPI_STORE)
+        if "big_gateup" in big:
+            big_case("gateup", 2 * I, H, K.EPI_SILU_MUL)
+        if "big_down" in big:
+            big_case("down", H, I, K.EPI_RESIDUAL)
     gv = {k for k in wanted if k.startswith("gv_")}
     if gv:
         def gv_case(name, n_rows, k_dim, epi, silu=False, norm=False):
@@ -205,6 +221,10 @@ def main(argv=None) -> int:
         torch.cuda.synchronize()
         out[f"persistent_step(layers={args.layers})"] = (a0.elapsed_time(a1) / 1000.0 / args.reps, step_bytes)
     for name, (t, nbytes) in out.items():
+        if name.startswith("big_"):
+            print(json.dumps({"kernel": name, "m": m, "us": round(t * 1e6, 2), "flops": nbytes,
+                              "tflops": round(nbytes / t / 1e12, 1)}))
+            continue
         print(json.dumps({"kernel": name, "m": m, "us": round(t * 1e6, 2), "bytes": nbytes,
                           "gbs": round(nbytes / t / 1e9, 1)}))
     return 0
