@@ -355,6 +355,18 @@ int ls_argmax_keys_to_ids(const int64_t* keys, int64_t m, int64_t* out_ids, ls_s
  * (barriers per step) x grid x 2 u64, each barrier records every CTA's arrival
  * and release time (globaltimer ns).  NULL turns it off. */
 int ls_decode_step_set_trace(void* buffer);
+/* Profiling hook of ls_linear_bf16 and the fused head / all-reduce forms: with a
+ * non-NULL device buffer of grid x 5 u64, every launch records per CTA the
+ * globaltimer at start, after the PDL wait, after the activation prologue,
+ * after the weight stream, and at the end.  NULL turns it off. */
+int ls_linear_set_trace(void* buffer);
+/* Profiling hook of ls_gemm_bf16_tcgen05(_tiled): with a non-NULL device buffer
+ * of grid x 8 u64, each launch records per CTA the globaltimer at start, when
+ * the first stage landed, after the last MMA issue, after the epilogue, and
+ * for the first and the last split tile when its contributors were complete
+ * and when this CTA's share was reduced (0 where there is none).  NULL turns
+ * it off. */
+int ls_gemm_tc_set_trace(void* buffer);
 
 int ls_residual_add_f32(const void* residual, const float* y, int64_t n, void* out, ls_stream_t stream);
 

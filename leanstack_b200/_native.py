@@ -74,6 +74,8 @@ SIGNATURES: dict[str, list] = {
     "ls_rmsnorm": [_p, _i64, _i64, _p, _f32, _p, _p],
     "ls_residual_add_f32": [_p, _p, _i64, _p, _p],
     "ls_decode_step_set_trace": [_p],
+    "ls_linear_set_trace": [_p],
+    "ls_gemm_tc_set_trace": [_p],
     "ls_spec_accept": [_p, _p, _i64, _i64, _p, _p, _p, _p, _p, _p, _i64, _p],
     "ls_gemm_bf16_tcgen05_big": [_p, _i64, _i64, _p, _i64, ctypes.c_int, _p, _p, _p],
     "ls_decode_attention_fused": [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _f32, _p, _p, _i64, _i64, _p, _i64, _p,

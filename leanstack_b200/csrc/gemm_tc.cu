@@ -65,6 +65,8 @@ struct TcParams {
   // shared-memory image at w_tiled[(t * kblocks + kb) * 16 KB]; null: TMA maps.
   const unsigned char* w_tiled;
   const unsigned char* w2_tiled;
+  unsigned long long* trace;  // optional profiling: per CTA 8 globaltimer stamps
+  int aligned;  // N % 8 == 0 and out / residual 16-byte aligned: vector stores, bulk residual rows
 };
 
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
@@ -144,6 +146,288 @@ __device__ __forceinline__ void tc_store(const TcParams& p, size_t o, float v) {
   else p.out[o] = f_to_bf16(v);
 }
 
+// One contributor's share of a split tile's reduction: output columns
+// [b0, b1) x the tile's 128 weight rows, summed over the partials of CTAs
+// c_lo..c_hi in CTA order.  Work items are (column, 4-row quad) pairs read as
+// float4; the partials of up to kRedC contributors x kRedI items are loaded
+// before any is added, so one L2 round trip serves 16 float4 loads per thread.
+template <int EPI>
+__device__ __forceinline__ void tc_reduce_tile(const TcParams& p, int t, int c_lo, int c_hi, int b0, int b1,
+                                               long long U, int G, int KB) {
+  constexpr int ACCS = (EPI == TEPI_SILU_MUL) ? 2 : 1;
+  constexpr int kRedI = 4 / ACCS;  // items per batch
+  constexpr int kRedC = 4;         // contributors per load round
+  const int items = (b1 - b0) * (kTcTileN / 4);
+  const size_t part_stride = (size_t)ACCS * p.BN * kTcTileN;  // floats per partial slot
+  for (int it0 = threadIdx.x; it0 < items; it0 += kTcEpiThreads * kRedI) {
+    float4 y[kRedI][ACCS];
+#pragma unroll
+    for (int i = 0; i < kRedI; ++i)
+#pragma unroll
+      for (int a = 0; a < ACCS; ++a) y[i][a] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c0 = c_lo; c0 <= c_hi; c0 += kRedC) {
+      float4 v[kRedC][kRedI][ACCS];
+#pragma unroll
+      for (int cu = 0; cu < kRedC; ++cu) {
+        const int c = c0 + cu;
+        if (c > c_hi) break;
+        const int sl = (t == (int)(tc_unit_begin(U, G, c) / KB)) ? 0 : 1;
+        const float* part = p.partial + ((size_t)c * 2 + sl) * part_stride;
+#pragma unroll
+        for (int i = 0; i < kRedI; ++i) {
+          const int it = it0 + i * kTcEpiThreads;
+          if (it < items) {
+            const int b = b0 + it / (kTcTileN / 4), row0 = (it % (kTcTileN / 4)) * 4;
+#pragma unroll
+            for (int a = 0; a < ACCS; ++a)
+              v[cu][i][a] = __ldcg(reinterpret_cast<const float4*>(part + ((size_t)a * p.BN + b) * kTcTileN + row0));
+          }
+        }
+      }
+#pragma unroll
+      for (int cu = 0; cu < kRedC; ++cu) {
+        if (c0 + cu > c_hi) break;
+#pragma unroll
+        for (int i = 0; i < kRedI; ++i)
+#pragma unroll
+          for (int a = 0; a < ACCS; ++a) {
+            y[i][a].x += v[cu][i][a].x;
+            y[i][a].y += v[cu][i][a].y;
+            y[i][a].z += v[cu][i][a].z;
+            y[i][a].w += v[cu][i][a].w;
+          }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kRedI; ++i) {
+      const int it = it0 + i * kTcEpiThreads;
+      if (it >= items) continue;
+      const int b = b0 + it / (kTcTileN / 4);
+      const int n0 = t * kTcTileN + (it % (kTcTileN / 4)) * 4;
+      const float ya[4] = {y[i][0].x, y[i][0].y, y[i][0].z, y[i][0].w};
+      const float yb[4] = {y[i][ACCS - 1].x, y[i][ACCS - 1].y, y[i][ACCS - 1].z, y[i][ACCS - 1].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (n0 + q < p.N) {
+          const size_t o = (size_t)b * p.N + n0 + q;
+          tc_store<EPI>(p, o, tc_apply<EPI>(p, o, ya[q], yb[q]));
+        }
+      }
+    }
+  }
+}
+
+// Output of one reduced element with the residual value already loaded.
+template <int EPI>
+__device__ __forceinline__ float tc_apply_r(float y, float y2, float r) {
+  if (EPI == TEPI_STORE || EPI == TEPI_STORE_F32) return y;
+  if (EPI == TEPI_RESIDUAL) return r + round_bf16(y);
+  const float g = round_bf16(y);
+  return round_bf16(g / (1.0f + expf(-g))) * round_bf16(y2);
+}
+
+__device__ __forceinline__ void red_release_gpu(unsigned int* ctr, unsigned int v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(ctr), "r"(v) : "memory");
+}
+
+// Deferred stream-K reduction of the (at most two) split tiles this CTA
+// contributed to.  Each contributor of a tile owns a slice [b0, b1) of its
+// activation columns and sums the fp32 partials of all contributors for that
+// slice in CTA order (deterministic).  Shares are taken last tile first: its
+// other contributor (the next CTA) wrote its part at the start of its
+// mainloop, so it is complete as soon as this CTA's own part is.
+//
+// The idle stage ring serves as two staging regions.  One thread waits for a
+// tile's contributors and pulls their partial columns (and, for RESIDUAL, the
+// residual rows) in with bulk async copies; the next job's copies are in
+// flight while the 128 epilogue threads sum the current one.  Shapes whose
+// jobs do not fit fall back to tc_reduce_tile (direct float4 loads).
+constexpr int kTcMaxRedJobs = 16;
+
+template <int EPI>
+__device__ __forceinline__ void tc_stream_k_fixup(const TcParams& p, long long U, int G, int KB, long long ub,
+                                                  long long ue, int cta, unsigned char* area, size_t area_bytes,
+                                                  uint64_t* bars, volatile int* abort,
+                                                  unsigned long long* tr) {
+  constexpr int ACCS = (EPI == TEPI_SILU_MUL) ? 2 : 1;
+  constexpr uint32_t kColBytes = kTcTileN * 4;  // one activation column of one partial
+  constexpr uint32_t kResBytes = kTcTileN * 2;  // one residual row segment
+  const bool res_bulk = (EPI == TEPI_RESIDUAL) && p.aligned;
+  const int tid = threadIdx.x;
+  int sh_t[2], sh_lo[2], sh_hi[2], sh_b0[2], sh_b1[2];
+  int ns = 0;
+  const int t_first = (int)(ub / KB), t_last = (int)((ue - 1) / KB);
+  for (int w = 0; w < 2; ++w) {
+    const int t = w == 0 ? t_last : t_first;
+    if (w == 1 && t_first == t_last) break;
+    const long long tile_begin = (long long)t * KB, tile_end = tile_begin + KB;
+    const int c_lo = tc_unit_owner(U, G, tile_begin), c_hi = tc_unit_owner(U, G, tile_end - 1);
+    const int nc = c_hi - c_lo + 1;
+    if (nc == 1) continue;  // a whole tile: written by the epilogue
+    const int j = cta - c_lo;
+    sh_t[ns] = t;
+    sh_lo[ns] = c_lo;
+    sh_hi[ns] = c_hi;
+    sh_b0[ns] = (int)(((long long)p.B * j) / nc);
+    sh_b1[ns] = (int)(((long long)p.B * (j + 1)) / nc);
+    ++ns;
+  }
+  const size_t part_stride = (size_t)ACCS * p.BN * kTcTileN;  // floats per partial slot
+  const size_t half = (area_bytes / 2) & ~(size_t)1023;
+  // Jobs: (share, first column, columns), in order.
+  int jb_s[kTcMaxRedJobs], jb_c0[kTcMaxRedJobs], jb_cn[kTcMaxRedJobs];
+  int nj = 0;
+  bool staged = true;
+  for (int s = 0; s < ns && staged; ++s) {
+    const int nc = sh_hi[s] - sh_lo[s] + 1;
+    const size_t per_col = (size_t)nc * ACCS * kColBytes + (res_bulk ? kResBytes : 0);
+    int chunk = (int)(half / per_col);
+    if (chunk < 1) {
+      staged = false;
+      break;
+    }
+    for (int c0 = sh_b0[s]; c0 < sh_b1[s]; c0 += chunk) {
+      if (nj == kTcMaxRedJobs) {
+        staged = false;
+        break;
+      }
+      jb_s[nj] = s;
+      jb_c0[nj] = c0;
+      jb_cn[nj] = min(chunk, sh_b1[s] - c0);
+      ++nj;
+    }
+  }
+
+  if (!staged) {
+    for (int s = 0; s < ns; ++s) {
+      const int nc = sh_hi[s] - sh_lo[s] + 1;
+      if (sh_b1[s] <= sh_b0[s]) continue;
+      if (tid == 0 && !wait_counter(p.counters + sh_t[s], (unsigned int)nc, p.err, 5 + s)) *abort = 1;
+      named_bar_sync(1, kTcEpiThreads);
+      if (*abort) return;
+      tc_reduce_tile<EPI>(p, sh_t[s], sh_lo[s], sh_hi[s], sh_b0[s], sh_b1[s], U, G, KB);
+    }
+  } else {
+    // Thread 0: wait for the job's tile (first job of a share only), then
+    // start its copies into region (job & 1).  On a timeout it arrives without
+    // copies so that nobody waits on the region's barrier for nothing.
+    auto issue = [&](int jj) {
+      const int s = jb_s[jj], t = sh_t[s], c_lo = sh_lo[s], c_hi = sh_hi[s], nc = c_hi - c_lo + 1;
+      uint64_t* bar = bars + (jj & 1);
+      unsigned char* region = area + (size_t)(jj & 1) * half;
+      if ((jj == 0 || jb_s[jj - 1] != s) && !*abort) {
+        if (!wait_counter(p.counters + t, (unsigned int)nc, p.err, 5 + s)) *abort = 1;
+        if (tr) tr[4 + 2 * s] = global_timer_ns();
+      }
+      if (*abort) {
+        mbar_arrive(bar);
+        return;
+      }
+      const int c0 = jb_c0[jj], cn = jb_cn[jj];
+      const uint32_t seg_bytes = (uint32_t)cn * kColBytes;
+      const int n_first = t * kTcTileN;
+      const uint32_t res_row = (uint32_t)min(kTcTileN, p.N - n_first) * 2;
+      // Partials were published with generic stores and a release; the
+      // acquire above orders them before these bulk (async-proxy) reads, as
+      // does the proxy fence for this CTA's generic reads of the region.
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive_expect_tx(bar, (uint32_t)(nc * ACCS) * seg_bytes + (res_bulk ? (uint32_t)cn * res_row : 0u));
+      for (int c = c_lo; c <= c_hi; ++c) {
+        const int sl = (t == (int)(tc_unit_begin(U, G, c) / KB)) ? 0 : 1;
+        const float* part = p.partial + ((size_t)c * 2 + sl) * part_stride;
+        for (int a = 0; a < ACCS; ++a)
+          bulk_g2s(region + (size_t)((c - c_lo) * ACCS + a) * seg_bytes, part + ((size_t)a * p.BN + c0) * kTcTileN,
+                   seg_bytes, bar);
+      }
+      if (res_bulk) {
+        unsigned char* rdst = region + (size_t)nc * ACCS * seg_bytes;
+        for (int bl = 0; bl < cn; ++bl)
+          bulk_g2s(rdst + (size_t)bl * kResBytes, p.residual + (size_t)(c0 + bl) * p.N + n_first, res_row, bar);
+      }
+    };
+    if (tid == 0) {
+      if (nj > 0) issue(0);
+      if (nj > 1) issue(1);
+    }
+    uint32_t phase[2] = {0u, 0u};
+    for (int jj = 0; jj < nj; ++jj) {
+      const int r = jj & 1;
+      if (!mbar_wait(bars + r, phase[r], p.err, 7)) *abort = 1;
+      phase[r] ^= 1u;
+      named_bar_sync(1, kTcEpiThreads);
+      if (*abort) return;
+      const int s = jb_s[jj], t = sh_t[s], nc = sh_hi[s] - sh_lo[s] + 1;
+      const int c0 = jb_c0[jj], cn = jb_cn[jj];
+      const float* sm = reinterpret_cast<const float*>(area + (size_t)r * half);
+      const __nv_bfloat16* smr = reinterpret_cast<const __nv_bfloat16*>(area + (size_t)r * half +
+                                                                         (size_t)nc * ACCS * cn * kColBytes);
+      const int items = cn * (kTcTileN / 4);
+      for (int it = tid; it < items; it += kTcEpiThreads) {
+        const int bl = it / (kTcTileN / 4), row0 = (it % (kTcTileN / 4)) * 4;
+        float4 y[ACCS];
+#pragma unroll
+        for (int a = 0; a < ACCS; ++a) y[a] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c = 0; c < nc; ++c) {
+#pragma unroll
+          for (int a = 0; a < ACCS; ++a) {
+            const float4 v = *reinterpret_cast<const float4*>(sm + ((size_t)(c * ACCS + a) * cn + bl) * kTcTileN + row0);
+            y[a].x += v.x;
+            y[a].y += v.y;
+            y[a].z += v.z;
+            y[a].w += v.w;
+          }
+        }
+        const int b = c0 + bl;
+        const int n0 = t * kTcTileN + row0;
+        const size_t o = (size_t)b * p.N + n0;
+        const float ya[4] = {y[0].x, y[0].y, y[0].z, y[0].w};
+        const float yb[4] = {y[ACCS - 1].x, y[ACCS - 1].y, y[ACCS - 1].z, y[ACCS - 1].w};
+        float rv[4] = {0.f, 0.f, 0.f, 0.f};
+        if (EPI == TEPI_RESIDUAL) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (n0 + q < p.N) rv[q] = bf16_to_f(res_bulk ? smr[bl * kTcTileN + row0 + q] : p.residual[o + q]);
+        }
+        float ov[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) ov[q] = tc_apply_r<EPI>(ya[q], yb[q], rv[q]);
+        if (p.aligned && n0 + 3 < p.N) {
+          if (EPI == TEPI_STORE_F32) {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + o) = make_float4(ov[0], ov[1], ov[2], ov[3]);
+          } else {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(ov[0], ov[1]), hi = __floats2bfloat162_rn(ov[2], ov[3]);
+            uint2 pk;
+            pk.x = *reinterpret_cast<uint32_t*>(&lo);
+            pk.y = *reinterpret_cast<uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(p.out + o) = pk;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (n0 + q < p.N) tc_store<EPI>(p, o + q, ov[q]);
+        }
+      }
+      named_bar_sync(1, kTcEpiThreads);  // region r is free again
+      if (tr && tid == 0 && (jj + 1 == nj || jb_s[jj + 1] != s)) tr[5 + 2 * s] = global_timer_ns();
+      if (tid == 0 && jj + 2 < nj) issue(jj + 2);
+    }
+  }
+  // Departures: the last contributor of a tile to leave resets its counters
+  // for the next call.  Contributors without columns leave without waiting:
+  // some contributor with columns saw every arrival before it left.
+  if (tid == 0 && !*abort) {
+    unsigned int prev[2] = {0u, 0u};
+    for (int s = 0; s < ns; ++s) prev[s] = atomicAdd(p.counters + p.tiles + sh_t[s], 1u);
+    for (int s = 0; s < ns; ++s) {
+      if (prev[s] == (unsigned int)(sh_hi[s] - sh_lo[s])) {
+        p.counters[sh_t[s]] = 0u;
+        p.counters[p.tiles + sh_t[s]] = 0u;
+      }
+    }
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
@@ -158,7 +442,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* empty = full + NS;
   uint64_t* acc_full = empty + NS;   // [2]
   uint64_t* acc_empty = acc_full + 2;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* red_bar = acc_empty + 2;    // [2] stream-K reduction copies
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 2);
   __shared__ int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -181,6 +466,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], kTcEpiThreads);
     }
+    mbar_init(&red_bar[0], 1);
+    mbar_init(&red_bar[1], 1);
     s_abort = 0;
     mbar_fence_init();
   }
@@ -195,6 +482,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   grid_dep_launch();
   const uint32_t tmem = *tmem_slot;
+  unsigned long long* tr = p.trace ? p.trace + (size_t)cta * 8 : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = global_timer_ns();
 
   if (warp == 4) {
     // ---------------- TMA producer ----------------
@@ -261,6 +550,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             s_abort = 1;
             break;
           }
+          if (tr && i == 0) tr[1] = global_timer_ns();
           tc_fence_after();
           const uint32_t sw = smem_u32(smem + (size_t)s * p.stage_bytes);
           const uint32_t sx = sw + kWBytes * ACCS;
@@ -278,6 +568,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         ++seg;
         u = seg_end;
       }
+      if (tr) tr[2] = global_timer_ns();
     }
   } else {
     // ---------------- epilogue (warps 0-3: TMEM lanes 0-127) ----------------
@@ -328,69 +619,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (!whole) {
         // Publish this contributor's partial; the reduction waits until the
         // whole mainloop is done (below), so no CTA ever waits mid-stream.
-        __threadfence();
         named_bar_sync(1, kTcEpiThreads);
-        if (threadIdx.x == 0) atomicAdd(p.counters + t, 1u);
+        if (threadIdx.x == 0) red_release_gpu(p.counters + t, 1u);
       }
       ++seg;
       u = seg_end;
     }
 
+    if (tr && threadIdx.x == 0) tr[3] = global_timer_ns();
     // ---- deferred stream-K reduction of this CTA's partial tiles ----
-    if (!*(volatile int*)&s_abort) {
-      const int t_first = (int)(ub / KB), t_last = (int)((ue - 1) / KB);
-      for (int which = 0; which < 2; ++which) {
-        const int t = which == 0 ? t_first : t_last;
-        if (which == 1 && t_last == t_first) break;
-        const long long tile_begin = (long long)t * KB, tile_end = tile_begin + KB;
-        const int c_lo = tc_unit_owner(U, G, tile_begin), c_hi = tc_unit_owner(U, G, tile_end - 1);
-        const int nc = c_hi - c_lo + 1;
-        if (nc == 1) continue;  // a whole tile: already written
-        if (threadIdx.x == 0 && !wait_counter(p.counters + t, (unsigned int)nc, p.err, 5 + which)) s_abort = 1;
-        named_bar_sync(1, kTcEpiThreads);
-        if (*(volatile int*)&s_abort) break;
-        __threadfence();
-        const int j = cta - c_lo;
-        const int b0 = (int)(((long long)p.B * j) / nc), b1 = (int)(((long long)p.B * (j + 1)) / nc);
-        const int n = t * kTcTileN + row;
-        if (n < p.N) {
-          // Columns in batches of 8 with all their partial loads issued before
-          // any is consumed (the loop is otherwise one L2 round trip per column).
-          for (int bb = b0; bb < b1; bb += 8) {
-            float y[8], y2[8];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) y[q] = y2[q] = 0.f;
-            for (int c = c_lo; c <= c_hi; ++c) {
-              const int sl = (t == (int)(tc_unit_begin(U, G, c) / KB)) ? 0 : 1;
-              const float* part = p.partial + (((size_t)c * 2 + sl) * ACCS * p.BN) * kTcTileN + row;
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                if (bb + q < b1) {
-                  y[q] += __ldcg(part + (size_t)(bb + q) * kTcTileN);
-                  if (SILU) y2[q] += __ldcg(part + ((size_t)p.BN + bb + q) * kTcTileN);
-                }
-              }
-            }
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              if (bb + q < b1) {
-                const size_t o = (size_t)(bb + q) * p.N + n;
-                tc_store<EPI>(p, o, tc_apply<EPI>(p, o, y[q], y2[q]));
-              }
-            }
-          }
-        }
-        // The last contributor to finish reducing resets the tile's counters.
-        named_bar_sync(1, kTcEpiThreads);
-        if (threadIdx.x == 0) {
-          const unsigned int prev = atomicAdd(p.counters + p.tiles + t, 1u);
-          if (prev == (unsigned int)nc - 1) {
-            p.counters[t] = 0u;
-            p.counters[p.tiles + t] = 0u;
-          }
-        }
-      }
-    }
+    if (!*(volatile int*)&s_abort)
+      tc_stream_k_fixup<EPI>(p, U, G, KB, ub, ue, cta, smem, (size_t)NS * p.stage_bytes, red_bar, &s_abort, tr);
   }
 
   __syncthreads();
@@ -639,6 +878,11 @@ static int tc_stage_budget_kb() {
   return v;
 }
 
+// Profiling hook (ls_gemm_tc_set_trace): per CTA 8 stamps: start, first stage
+// landed, last MMA issued, epilogue done, then for the first and the last
+// split tile: counter complete, share reduced (0 where there is none).
+static unsigned long long* g_tc_trace = nullptr;
+
 static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
   TcPlan pl = {};
   pl.accs = (epi == TEPI_SILU_MUL) ? 2 : 1;
@@ -660,7 +904,7 @@ static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
   uint32_t cols = 32;
   while (cols < (uint32_t)(pl.acc_buffers * pl.BN * pl.accs)) cols <<= 1;
   pl.tmem_cols = cols;
-  pl.smem = 1024 + (size_t)pl.stages * pl.stage_bytes + (size_t)(2 * pl.stages + 4) * 8 + 16;
+  pl.smem = 1024 + (size_t)pl.stages * pl.stage_bytes + (size_t)(2 * pl.stages + 6) * 8 + 16;
   pl.counter_bytes = kTcCounterBytes;
   pl.partial_bytes = (size_t)pl.grid * 2 * pl.accs * pl.BN * kTcTileN * 4;
   return pl;
@@ -712,8 +956,8 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
   if (m < 1 || m > 128) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "gemm_tc: m=%lld outside 1..128", (long long)m);
   if (k < 8 || k % 8 || n_out < 1) return set_error(LS_ERR_MISALIGNED, "gemm_tc: k=%lld must be a positive multiple of 8",
                                                     (long long)k);
-  if (!aligned16(x) || (!w_tiled && !aligned16(w)))
-    return set_error(LS_ERR_MISALIGNED, "gemm_tc: x and w must be 16-byte aligned");
+  if (!aligned16(x) || (!w_tiled && !aligned16(w)) || !aligned16(workspace))
+    return set_error(LS_ERR_MISALIGNED, "gemm_tc: x, w and the workspace must be 16-byte aligned");
   if (epi == TEPI_RESIDUAL && !residual) return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_tc: residual is null");
   TcPlan pl = tc_plan(m, k, n_out, epi);
   if (pl.tmem_cols > 256) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "gemm_tc: m=%lld too wide for TMEM", (long long)m);
@@ -758,6 +1002,8 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
   p.acc_buffers = pl.acc_buffers;
   p.tmem_cols = pl.tmem_cols;
   p.w_tiled = static_cast<const unsigned char*>(w_tiled);
+  p.trace = g_tc_trace;
+  p.aligned = (n_out % 8 == 0) && aligned16(out) && (!residual || aligned16(residual)) ? 1 : 0;
   p.w2_tiled = w_tiled ? p.w_tiled + tc_tiled_bytes(n_out, k, 0) : nullptr;
   switch (epi) {
     case TEPI_STORE: return launch_tc_t<TEPI_STORE>(mw, mw2, mx, p, pl, stream);
@@ -889,3 +1135,8 @@ int launch_tc_tile(const void* w, int64_t n_rows, int64_t k, int silu, void* out
 }
 
 }  // namespace lsb_host
+
+extern "C" int ls_gemm_tc_set_trace(void* buffer) {
+  lsb_host::g_tc_trace = static_cast<unsigned long long*>(buffer);
+  return LS_OK;
+}

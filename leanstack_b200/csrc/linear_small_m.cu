@@ -53,6 +53,7 @@ struct LinearParams {
   // EPI_AR_RESIDUAL: tensor-parallel exchange regions
   P2PExchange ex;
   int* err;
+  unsigned long long* trace;  // optional profiling: per CTA 5 globaltimer stamps
 };
 
 template <int M>
@@ -84,6 +85,8 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
   const int R = P * RPU;            // weight rows owned by this CTA
   const int ms = p.max_segs;
 
+  unsigned long long* tr = p.trace ? p.trace + (size_t)blockIdx.x * 5 : nullptr;
+  if (tr && tid == 0) tr[0] = global_timer_ns();
   // Weights do not depend on the previous kernel: start pulling this CTA's
   // first weight bytes into L2, let the next kernel launch, and only then wait
   // (PDL) for the activations the previous kernel writes.
@@ -99,6 +102,7 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
   }
   grid_dep_launch();
   grid_dep_wait();
+  if (tr && tid == 0) tr[1] = global_timer_ns();
   __shared__ uint32_t s_epoch;
   if (EPI == EPI_AR_RESIDUAL && tid == 0) {  // per-CTA call counter of the fused all-reduce
     uint32_t* ctr = reinterpret_cast<uint32_t*>(p.ex.peer[p.ex.rank] + p2p_ctr_offset(p.ex.max_ctas)) + blockIdx.x;
@@ -159,6 +163,7 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
   }
   __syncthreads();
 
+  if (tr && tid == 0) tr[2] = global_timer_ns();
   // ---- main loop: stream this CTA's weight rows ----
   const int gpr = (K + kGranule - 1) / kGranule;  // granules per row
   const int total = R * gpr;
@@ -208,6 +213,7 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
   }
   __syncthreads();
 
+  if (tr && tid == 0) tr[3] = global_timer_ns();
   // Sum of local row t for activation row m over the warps that cover it, in
   // warp order.  Warp w covers local rows [s_wr0[w], s_wr1[w]] (empty: r0 > r1),
   // computed once per CTA instead of per output.
@@ -228,10 +234,6 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
     }
     return s;
   };
-  // The next kernel may start its prologue now (it still waits for our exit
-  // before reading our outputs).
-  grid_dep_launch();
-
   // ---- epilogue ----
   if (EPI == EPI_STORE_F32) {  // unrounded fp32 partial (tensor-parallel row-split linears)
     for (int i = tid; i < M * P; i += kLinThreads) {
@@ -364,6 +366,10 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
       if (tid == 0) *p.counter = 0u;
     }
   }
+  if (tr) {
+    __syncthreads();
+    if (tid == 0) tr[4] = global_timer_ns();
+  }
 }
 
 }  // namespace lsb
@@ -379,6 +385,10 @@ using namespace lsb;
 // keep ~128 KB per SM in flight, what the measured 6 TB/s needs (one CTA per
 // SM reached only 4.5 TB/s on the lm_head).  m > 4 needs more registers and
 // runs one CTA per SM.
+// Profiling hook (ls_linear_set_trace): when set, every launch records per CTA
+// (start, after the PDL wait, after the prologue, after the main loop, end).
+static unsigned long long* g_lin_trace = nullptr;
+
 static int linear_grid(int units, int m) {
   const int g = (m <= 4 ? 2 : 1) * sm_count();
   return units < g ? units : g;
@@ -493,6 +503,7 @@ static int launch_linear_impl(const void* x, int64_t m, int64_t k, const void* n
   p.id_offset = id_offset;
   p.out_keys = out_keys ? 1 : 0;
   p.err = device_error_ptr();
+  p.trace = g_lin_trace;
   if (epi == EPI_AR_RESIDUAL) {
     p.ex = *ex;
     const int g_ar = grid_override > 0 ? grid_override : linear_grid(p.units, (int)m);
@@ -546,3 +557,8 @@ int launch_linear_allreduce(const void* x, int64_t m, int64_t k, const void* w, 
 int lmhead_grid(int64_t vocab, int64_t m) { return linear_grid((int)vocab, (int)m); }
 
 }  // namespace lsb_host
+
+extern "C" int ls_linear_set_trace(void* buffer) {
+  lsb_host::g_lin_trace = static_cast<unsigned long long*>(buffer);
+  return LS_OK;
+}
