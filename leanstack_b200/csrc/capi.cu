@@ -27,25 +27,57 @@ __global__ void embed_gather_kernel(const int64_t* ids, const __nv_bfloat16* emb
         reinterpret_cast<const uint4*>(embed + (size_t)id * hidden)[v];
 }
 
-// One CTA per row: y = bf16((x * rsqrt(mean(x^2) + eps)) * w).
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, int n, const __nv_bfloat16* w,
-                                                      float eps, __nv_bfloat16* out) {
+// One CTA per row: y = bf16((x * rsqrt(mean(x^2) + eps)) * w).  Rows whose
+// length is a multiple of 8 (16-byte aligned) go through 16-byte vectors; the
+// second pass re-reads x from L1.  Launched with programmatic dependent launch:
+// the next kernel may start its own prologue (weight prefetch) at once.
+constexpr int kNormThreads = 256;
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const __nv_bfloat16* x, int n, const __nv_bfloat16* w,
+                                                               float eps, __nv_bfloat16* out, int vec) {
+  grid_dep_launch();
   grid_dep_wait();
-  __shared__ float red[8];
+  __shared__ float red[kNormThreads / 32];
   const __nv_bfloat16* xr = x + (size_t)blockIdx.x * n;
+  __nv_bfloat16* orow = out + (size_t)blockIdx.x * n;
   float ss = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = bf16_to_f(xr[i]);
-    ss = fmaf(v, v, ss);
+  if (vec) {
+    for (int v = threadIdx.x; v < n / 8; v += kNormThreads) {
+      float f[8];
+      unpack8(ldg16(xr + v * 8), f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += kNormThreads) {
+      const float v = bf16_to_f(xr[i]);
+      ss = fmaf(v, v, ss);
+    }
   }
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   float tot = 0.f;
-  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
   const float r = rsqrtf(tot / (float)n + eps);
-  for (int i = threadIdx.x; i < n; i += blockDim.x)
-    out[(size_t)blockIdx.x * n + i] = f_to_bf16((bf16_to_f(xr[i]) * r) * bf16_to_f(w[i]));
+  if (vec) {
+    for (int v = threadIdx.x; v < n / 8; v += kNormThreads) {
+      float f[8], g[8];
+      unpack8(ldg16(xr + v * 8), f);
+      unpack8(ldg16(w + v * 8), g);
+      uint4 o;
+      uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 pr = __floats2bfloat162_rn((f[2 * j] * r) * g[2 * j], (f[2 * j + 1] * r) * g[2 * j + 1]);
+        op[j] = *reinterpret_cast<uint32_t*>(&pr);
+      }
+      *reinterpret_cast<uint4*>(orow + v * 8) = o;
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += kNormThreads)
+      orow[i] = f_to_bf16((bf16_to_f(xr[i]) * r) * bf16_to_f(w[i]));
+  }
 }
 
 // Row argmax over bf16 logits: grid (chunks, m); each CTA reduces one chunk of
@@ -633,10 +665,18 @@ int ls_residual_add_f32(const void* residual, const float* y, int64_t n, void* o
 int ls_rmsnorm(const void* x, int64_t m, int64_t n, const void* w, float eps, void* out, ls_stream_t stream) {
   LS_REQUIRE(x && w && out, LS_ERR_INVALID_ARGUMENT, "ls_rmsnorm: null pointer");
   LS_REQUIRE(m > 0 && m < (1ll << 31) && n > 0 && n <= (1 << 20), LS_ERR_INVALID_ARGUMENT, "ls_rmsnorm: bad sizes");
-  lsb::rmsnorm_kernel<<<(unsigned)m, 256, 0, (cudaStream_t)stream>>>(static_cast<const __nv_bfloat16*>(x), (int)n,
-                                                                     static_cast<const __nv_bfloat16*>(w), eps,
-                                                                     static_cast<__nv_bfloat16*>(out));
-  cudaError_t e = cudaGetLastError();
+  const int vec = (n % 8 == 0) && aligned16(x) && aligned16(w) && aligned16(out) ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)m);
+  cfg.blockDim = dim3(lsb::kNormThreads);
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, lsb::rmsnorm_kernel, static_cast<const __nv_bfloat16*>(x), (int)n,
+                                     static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(out), vec);
   return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "rmsnorm launch: %s", cudaGetErrorString(e));
 }
 

@@ -91,6 +91,12 @@ def test_rmsnorm_and_embed():
     ref = qo.rmsnorm(x.cpu(), w.cpu(), 1e-6)
     assert (y.cpu() == ref).float().mean().item() > 0.999
     assert (y.float().cpu() - ref.float()).abs().max().item() <= 2 ** -6
+    # a row length that is not a multiple of 8 takes the scalar path
+    x2 = _rand((2, 1001), 1.0, "xr2")
+    w2 = synth.norm_weight((1001,), 1, "nr2", device=DEV)
+    y2 = K.rmsnorm(x2, w2, 1e-6)
+    ref2 = qo.rmsnorm(x2.cpu(), w2.cpu(), 1e-6)
+    assert (y2.float().cpu() - ref2.float()).abs().max().item() <= 2 ** -6
     emb = _rand((1000, 256), 0.02, "emb")
     ids = torch.tensor([5, 999, 0, 5], device=DEV)
     assert torch.equal(K.embed_gather(ids, emb), emb[ids])
