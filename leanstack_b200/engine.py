@@ -51,7 +51,8 @@ def resolve_backend(backend: str, batch_size: int) -> str:
 class DecodeEngine:
     def __init__(self, runtime: QwenSemanticStackRuntime, batch_size: int, max_seq_len: int,
                  max_tokens_per_step: int | None = None, use_graph: bool = True, linear_backend: str = "auto",
-                 tp: TPComm | None = None, shard: TPShard | None = None, gemv_tiles: bool = False):
+                 tp: TPComm | None = None, shard: TPShard | None = None, gemv_tiles: bool = False,
+                 tc_tiles: list[dict] | None = None):
         if runtime.final_norm_weight is None or runtime.lm_head_weight is None:
             raise ValueError("the engine needs the output head (include_output_head=True)")
         self.tp = tp if (tp is not None and tp.world > 1) else None
@@ -125,6 +126,12 @@ class DecodeEngine:
         self.accepted = torch.zeros(batch_size, device=dev, dtype=torch.int32)
         self.verify_graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.fuse_attention = False
+        # Pre-tiled tcgen05 weight images per layer ({"qkv", "o", "gu", "down"},
+        # e.g. from a leanpack/v1 artifact): the tensor-core linears stream them
+        # with plain bulk copies instead of TMA tensor maps.
+        if tc_tiles is not None and len(tc_tiles) != len(rt.layers):
+            raise ValueError(f"tc_tiles has {len(tc_tiles)} layers, the runtime {len(rt.layers)}")
+        self.tc_tiles = tc_tiles
         self.use_graph = use_graph
         self.graph: torch.cuda.CUDAGraph | None = None
         if self.persistent:
@@ -165,13 +172,14 @@ class DecodeEngine:
         for li, layer in enumerate(rt.layers):
             att, mlp = layer.attention, layer.mlp
             tl = self.tiles[li] if self.tiles is not None else None
+            tt = self.tc_tiles[li] if (tc and self.tc_tiles is not None) else {}
             # QKV projection (with the input RMSNorm) into a.qkv
             if tl is not None:
                 K.gemv(a.x[:m], tl["qkv"], norm_w=layer.input_layernorm_weight, eps=eps, out=a.qkv[:m],
                        workspace=self.gv_ws)
             elif tc:
                 K.rmsnorm(a.x[:m], layer.input_layernorm_weight, eps, out=self.xn[:m])
-                K.gemm_tc(self.xn[:m], att.qkv_proj_weight, out=a.qkv[:m], workspace=self.tc_ws)
+                K.gemm_tc(self.xn[:m], att.qkv_proj_weight, out=a.qkv[:m], workspace=self.tc_ws, tiled=tt.get("qkv"))
             else:
                 K.linear(a.x[:m], att.qkv_proj_weight, norm_w=layer.input_layernorm_weight, eps=eps, out=a.qkv[:m])
             if self._fused_attention(q_len):
@@ -189,18 +197,18 @@ class DecodeEngine:
                                    g.num_key_value_heads, g.head_dim, self.S, att.attention_scale,
                                    cache_pos=kv.cache_pos, out=a.attn[:m], workspace=self.attn_ws)
             if self.tp is not None:
-                self._row_split(a.attn[:m], att.o_proj_weight, a.x[:m], a.h[:m], tc)
+                self._row_split(a.attn[:m], att.o_proj_weight, a.x[:m], a.h[:m], tc, tt.get("o"))
                 if tl is not None:
                     K.gemv(a.h[:m], tl["gu"], norm_w=layer.post_attention_layernorm_weight, eps=eps,
                            epilogue=K.EPI_SILU_MUL, out=a.act[:m], workspace=self.gv_ws)
                 elif tc:
                     K.rmsnorm(a.h[:m], layer.post_attention_layernorm_weight, eps, out=self.xn[:m])
                     K.gemm_tc(self.xn[:m], mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=a.act[:m],
-                              workspace=self.tc_ws)
+                              workspace=self.tc_ws, tiled=tt.get("gu"))
                 else:
                     K.gateup_silu(a.h[:m], layer.post_attention_layernorm_weight, mlp.gate_up_proj_weight, eps,
                                   out=a.act[:m])
-                self._row_split(a.act[:m], mlp.down_proj_weight, a.h[:m], a.x[:m], tc)
+                self._row_split(a.act[:m], mlp.down_proj_weight, a.h[:m], a.x[:m], tc, tt.get("down"))
             elif tl is not None:
                 K.gemv(a.attn[:m], tl["o"], epilogue=K.EPI_RESIDUAL, residual=a.x[:m], out=a.h[:m],
                        workspace=self.gv_ws)
@@ -210,12 +218,12 @@ class DecodeEngine:
                        workspace=self.gv_ws)
             elif tc:
                 K.gemm_tc(a.attn[:m], att.o_proj_weight, epilogue=K.EPI_RESIDUAL, residual=a.x[:m], out=a.h[:m],
-                          workspace=self.tc_ws)
+                          workspace=self.tc_ws, tiled=tt.get("o"))
                 K.rmsnorm(a.h[:m], layer.post_attention_layernorm_weight, eps, out=self.xn[:m])
                 K.gemm_tc(self.xn[:m], mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=a.act[:m],
-                          workspace=self.tc_ws)
+                          workspace=self.tc_ws, tiled=tt.get("gu"))
                 K.gemm_tc(a.act[:m], mlp.down_proj_weight, epilogue=K.EPI_RESIDUAL, residual=a.h[:m],
-                          out=a.x[:m], workspace=self.tc_ws)
+                          out=a.x[:m], workspace=self.tc_ws, tiled=tt.get("down"))
             else:
                 K.oproj_residual(a.attn[:m], att.o_proj_weight, a.x[:m], out=a.h[:m])
                 K.gateup_silu(a.h[:m], layer.post_attention_layernorm_weight, mlp.gate_up_proj_weight, eps,
@@ -319,14 +327,14 @@ class DecodeEngine:
         return a.ids[:B].clone()
 
     def _row_split(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor, out: torch.Tensor,
-                   tc: bool) -> None:
+                   tc: bool, tiled: torch.Tensor | None = None) -> None:
         """Row-split linear of tensor parallelism: fp32 partial, all-reduce, residual add."""
         if not tc and self.tp.p2p is not None:  # fused one-shot all-reduce in the linear's epilogue
             K.linear_allreduce_residual(x, w, residual, self.tp.p2p, out=out)
             return
         part = self.part[:x.shape[0]]
         if tc:
-            K.gemm_tc(x, w, epilogue=K.EPI_STORE_F32, out=part, workspace=self.tc_ws)
+            K.gemm_tc(x, w, epilogue=K.EPI_STORE_F32, out=part, workspace=self.tc_ws, tiled=tiled)
         else:
             K.linear(x, w, epilogue=K.EPI_STORE_F32, out=part)
         self.tp.all_reduce_sum(part)

@@ -193,6 +193,94 @@ def materialize_qwen_full_semantic_runtime_from_leanpack(pack_dir, *, model=None
 
 
 # ---------------------------------------------------------------------------
+# leanpack/v1 reader (format written by pack.write_qwen_leanpack_v1)
+# ---------------------------------------------------------------------------
+
+_DTYPES = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32, "uint8": torch.uint8}
+
+
+def map_leanpack_v1_rank(pack_dir, rank: int = 0) -> tuple[dict, dict[str, torch.Tensor]]:
+    """Map rank ``rank``'s shard file and return ``(manifest, {name: CPU view})``.
+
+    The file is memory-mapped (copy-on-write, nothing is read until touched) and
+    every stored tensor is a zero-copy view at its recorded offset.  The tied
+    head's entry is left out: it is a row range of the embedding, see
+    :func:`materialize_from_leanpack_v1`.
+    """
+    root = Path(pack_dir)
+    if root.name == "manifest.json":
+        root = root.parent
+    manifest = json.loads((root / "manifest.json").read_text(encoding="utf-8"))
+    if manifest.get("format_version") != "leanpack/v1":
+        raise ValueError(f"not a leanpack/v1 artifact: {manifest.get('format_version')!r}")
+    world = int(manifest["tensor_parallel"]["world"])
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside the pack's tensor-parallel world of {world}")
+    finfo = next(f for f in manifest["files"] if f["rank"] == rank)
+    path = root / finfo["file"]
+    size = path.stat().st_size
+    if size != finfo["size_bytes"]:
+        raise ValueError(f"{path.name}: {size} bytes on disk, manifest says {finfo['size_bytes']}")
+    align = int(manifest.get("alignment_bytes", 1))
+    blob = torch.from_file(str(path), shared=False, size=size, dtype=torch.uint8)
+    views: dict[str, torch.Tensor] = {}
+    for e in manifest["tensors"]:
+        if e["rank"] != rank or e.get("view_of"):
+            continue
+        off, n = int(e["offset_bytes"]), int(e["size_bytes"])
+        if off % align or off + n > size:
+            raise ValueError(f"{e['name']}: bad extent [{off}, {off + n}) in a {size}-byte file")
+        dt = _DTYPES[e["dtype"]]
+        views[e["name"]] = blob[off:off + n].view(dt).view(e["shape"])
+    return manifest, views
+
+
+def materialize_from_leanpack_v1(pack_dir, *, rank: int = 0, device="cuda:0", dtype="bfloat16"):
+    """Build rank ``rank``'s runtime from a leanpack/v1 artifact.
+
+    Returns ``(runtime, shard, tc_tiles)``: the runtime in the rank's local
+    geometry (whole model when the pack has one rank), its
+    :class:`~leanstack_b200.tp.TPShard` (vocab range of its head), and, when the
+    pack holds tile images, one ``{"qkv", "o", "gu", "down"}`` dict per layer of
+    device tensors for ``DecodeEngine(tc_tiles=...)`` (else None).
+    """
+    from .tp import local_geometry, shard_info
+
+    manifest, views = map_leanpack_v1_rank(pack_dir, rank)
+    art = LeanPackArtifact(root=Path(pack_dir), manifest=manifest)
+    g = art.geometry()
+    world = int(manifest["tensor_parallel"]["world"])
+    lg = local_geometry(g, world)
+    shard = shard_info(g, rank, world)
+    dev, dt = torch.device(device), resolve_torch_dtype(dtype)
+    put = lambda name: views[name].to(dev, dt).contiguous()  # noqa: E731
+    names = {"input_layernorm": "input_layernorm.weight", "qkv": "attention.qkv_proj.weight",
+             "o_proj": "attention.o_proj.weight", "q_norm": "attention.q_norm.weight",
+             "k_norm": "attention.k_norm.weight", "post_attention_layernorm": "post_attention_layernorm.weight",
+             "gate_up": "mlp.gate_up_proj.weight", "down_proj": "mlp.down_proj.weight"}
+    layers = []
+    for i in range(g.num_hidden_layers):
+        layers.append(_layer_runtime(lg, i, {k: put(f"layers.{i}.{v}") for k, v in names.items()}))
+    embed = put("model.embed_tokens.weight")
+    head = next(e for e in manifest["tensors"] if e["rank"] == rank and e["name"] == "lm_head.weight")
+    if head.get("view_of"):
+        lm = embed[int(head["row_offset"]):int(head["row_offset"]) + int(head["rows"])]
+    else:
+        lm = put("lm_head.weight")
+    rt = QwenSemanticStackRuntime(
+        model_path=art.root, config=lg, layer_indices=tuple(range(g.num_hidden_layers)), embed_tokens_weight=embed,
+        layers=tuple(layers), rope_inv_freq=rope_inv_freq(g, dev), attention_scaling=1.0,
+        final_norm_weight=put("model.norm.weight"), lm_head_weight=lm, device=dev, dtype=dt)
+    tiles = None
+    if manifest.get("tc_tiles"):
+        keys = {"attention.qkv_proj": "qkv", "attention.o_proj": "o", "mlp.gate_up_proj": "gu",
+                "mlp.down_proj": "down"}
+        tiles = [{k: views[f"layers.{i}.{base}.tc_tiled"].to(dev) for base, k in keys.items()}
+                 for i in range(g.num_hidden_layers)]
+    return rt, shard, tiles
+
+
+# ---------------------------------------------------------------------------
 # Resident buffer planner
 # ---------------------------------------------------------------------------
 

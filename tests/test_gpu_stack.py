@@ -252,3 +252,23 @@ def test_prefill_full_matches_chunked_prefill():
     hc, hd = c.last_head_rows().float(), d.last_head_rows().float()
     assert (hc - hd).abs().max().item() <= tol(hc)
     assert c.kv.sequence_lens == d.kv.sequence_lens == [384, 384]
+
+
+def test_leanpack_v1_tiles_feed_the_tensor_core_step(tmp_path):
+    """A leanpack/v1 artifact with tcgen05 tile images: the engine that streams
+    the stored images computes exactly what the engine on row-major weights
+    does (same kernel, same summation order; only the loads differ)."""
+    from leanstack_b200.leanserve import materialize_from_leanpack_v1
+    from leanstack_b200.pack import write_qwen_leanpack_v1
+
+    tensors = synth.synth_checkpoint(TINY, 11)
+    write_qwen_leanpack_v1(TINY, tensors, tmp_path / "pack", tc_tiles=True)
+    rt, _, tiles = materialize_from_leanpack_v1(tmp_path / "pack", device=DEV)
+    assert tiles is not None and len(tiles) == TINY.num_hidden_layers
+    ref_rt = materialize_from_tensors(TINY, dict(tensors), device=DEV)
+    prompt = synth.token_ids((4, 9), TINY.vocab_size, 11, "v1/prompt").to(DEV)
+    a = DecodeEngine(rt, batch_size=4, max_seq_len=64, linear_backend="tc", tc_tiles=tiles)
+    b = DecodeEngine(ref_rt, batch_size=4, max_seq_len=64, linear_backend="tc")
+    ta, tb = a.generate(prompt, 10), b.generate(prompt, 10)
+    assert torch.equal(ta, tb)
+    assert torch.equal(a.last_head_rows(), b.last_head_rows())
