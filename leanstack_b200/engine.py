@@ -129,8 +129,8 @@ class DecodeEngine:
         # Pre-tiled tcgen05 weight images per layer ({"qkv", "o", "gu", "down"},
         # e.g. from a leanpack/v1 artifact): the tensor-core linears stream them
         # with plain bulk copies instead of TMA tensor maps.
-        if tc_tiles is not None and len(tc_tiles) != len(rt.layers):
-            raise ValueError(f"tc_tiles has {len(tc_tiles)} layers, the runtime {len(rt.layers)}")
+        if tc_tiles is not None and len(tc_tiles) != len(runtime.layers):
+            raise ValueError(f"tc_tiles has {len(tc_tiles)} layers, the runtime {len(runtime.layers)}")
         self.tc_tiles = tc_tiles
         self.use_graph = use_graph
         self.graph: torch.cuda.CUDAGraph | None = None
