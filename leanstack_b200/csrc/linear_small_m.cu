@@ -161,6 +161,13 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
       *reinterpret_cast<uint4*>(xs + (size_t)m * K + c * 8) = ldg16(p.x + (size_t)m * K + c * 8);
     }
   }
+  // The residual of this thread's first output, loaded now so that the
+  // epilogue does not wait for it (written by an earlier kernel: after the wait).
+  float res0 = 0.f;
+  if (EPI == EPI_RESIDUAL && tid < M * P) {
+    const int m = tid / P, t = tid - m * P;
+    res0 = bf16_to_f(p.residual[(size_t)m * p.N + u0 + t]);
+  }
   __syncthreads();
 
   if (tr && tid == 0) tr[2] = global_timer_ns();
@@ -215,22 +222,22 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
 
   if (tr && tid == 0) tr[3] = global_timer_ns();
   // Sum of local row t for activation row m over the warps that cover it, in
-  // warp order.  Warp w covers local rows [s_wr0[w], s_wr1[w]] (empty: r0 > r1),
-  // computed once per CTA instead of per output.
-  __shared__ int s_wr0[kLinWarps], s_wr1[kLinWarps];
-  if (tid < kLinWarps) {
-    const int wb = (int)(((int64_t)total * tid) / kLinWarps);
-    const int we = (int)(((int64_t)total * (tid + 1)) / kLinWarps);
-    s_wr0[tid] = wb < we ? wb / gpr : 1;
-    s_wr1[tid] = wb < we ? (we - 1) / gpr : 0;
-  }
-  __syncthreads();
+  // warp order.  Warp w streams granules [gb(w), gb(w + 1)) of the CTA's flat
+  // granule list, so the covering warps follow from arithmetic: the first is
+  // the last warp starting at or before the row's first granule, and usually
+  // one or two warps contribute.  Reading shared memory only for those keeps
+  // the epilogue's memory instructions few: each one queues behind the
+  // sibling CTA's weight loads in the SM's memory-instruction queue (measured
+  // at gate_up: ~2.4 us for a single store while the sibling streams).
+  auto gb = [&](int w) -> int { return (int)(((int64_t)total * w) / kLinWarps); };
   auto row_sum = [&](int m, int t) -> float {
     float s = 0.f;
-#pragma unroll 4
-    for (int w = 0; w < kLinWarps; ++w) {
-      const int f = s_wr0[w];
-      if (t >= f && t <= s_wr1[w]) s += segbuf[((size_t)w * ms + (t - f)) * M + m];
+    const int g0 = t * gpr, g1 = g0 + gpr;
+    int w = (int)(((int64_t)kLinWarps * (g0 + 1) + total - 1) / total) - 1;
+    for (w = w < 0 ? 0 : w; w < kLinWarps; ++w) {
+      const int wb = gb(w), we = gb(w + 1);
+      if (wb >= g1) break;
+      if (wb < we && we > g0) s += segbuf[((size_t)w * ms + (t - wb / gpr)) * M + m];
     }
     return s;
   };
@@ -292,7 +299,7 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
       const int m = i / P, t = i - m * P;
       const size_t o = (size_t)m * p.N + u0 + t;
       float y = row_sum(m, t);
-      if (EPI == EPI_RESIDUAL) y = bf16_to_f(p.residual[o]) + round_bf16(y);
+      if (EPI == EPI_RESIDUAL) y = (i == tid ? res0 : bf16_to_f(p.residual[o])) + round_bf16(y);
       p.out[o] = f_to_bf16(y);
     }
   } else if (EPI == EPI_SILU_MUL) {
