@@ -100,6 +100,10 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
       for (uint32_t off = 0; off < pf; off += 16384) prefetch_l2(up + off, min(16384u, pf - off));
     }
   }
+  // The norm weight does not depend on the previous kernel either: this
+  // thread's first 16-byte vector of it is loaded before the wait.
+  const int kvec = K >> 3;  // 16-byte vectors per activation row
+  const uint4 nw0 = (NORM && tid < kvec) ? ldg16(p.norm_w + tid * 8) : make_uint4(0, 0, 0, 0);
   grid_dep_launch();
   grid_dep_wait();
   if (tr && tid == 0) tr[1] = global_timer_ns();
@@ -111,8 +115,11 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
   }
 
   // ---- prologue: (optional) RMSNorm of the M activation rows into smem ----
-  const int kvec = K >> 3;  // 16-byte vectors per activation row
   if (NORM) {
+    // x is read from L2 once: the vectors of the first pass stay in registers
+    // for the second (one vector per thread and row covers K <= 4096).
+    constexpr int XC = (M <= 2) ? M : 1;
+    uint4 xc[XC];
     float ss[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) ss[m] = 0.f;
@@ -120,7 +127,9 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
 #pragma unroll
       for (int m = 0; m < M; ++m) {
         float f[8];
-        unpack8(ldg16(p.x + (size_t)m * K + v * 8), f);
+        const uint4 xv = ldg16(p.x + (size_t)m * K + v * 8);
+        if (M <= 2 && v == tid) xc[m < XC ? m : 0] = xv;
+        unpack8(xv, f);
 #pragma unroll
         for (int j = 0; j < 8; ++j) ss[m] = fmaf(f[j], f[j], ss[m]);
       }
@@ -139,11 +148,11 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
     __syncthreads();
     for (int v = tid; v < kvec; v += kLinThreads) {
       float wf[8];
-      unpack8(ldg16(p.norm_w + v * 8), wf);
+      unpack8(v == tid ? nw0 : ldg16(p.norm_w + v * 8), wf);
 #pragma unroll
       for (int m = 0; m < M; ++m) {
         float f[8];
-        unpack8(ldg16(p.x + (size_t)m * K + v * 8), f);
+        unpack8((M <= 2 && v == tid) ? xc[m < XC ? m : 0] : ldg16(p.x + (size_t)m * K + v * 8), f);
         const float r = rscale[m];
         uint4 o;
         uint32_t* op = reinterpret_cast<uint32_t*>(&o);
