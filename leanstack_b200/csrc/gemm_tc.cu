@@ -878,6 +878,16 @@ static int tc_stage_budget_kb() {
   return v;
 }
 
+// LEANB200_TC_ALIGNED=0 keeps full stream-K for every shape (measurement).
+static bool tc_tile_aligned_split() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("LEANB200_TC_ALIGNED");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 // Profiling hook (ls_gemm_tc_set_trace): per CTA 8 stamps: start, first stage
 // landed, last MMA issued, epilogue done, then for the first and the last
 // split tile: counter complete, share reduced (0 where there is none).
@@ -892,6 +902,18 @@ static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
   const int64_t units = (int64_t)pl.tiles * pl.kblocks;
   const int sms = sm_count();
   pl.grid = (int)(units < sms ? units : sms);
+  // Fewer tiles than SMs: with the grid a multiple of the tile count, the even
+  // split of the unit list falls on tile boundaries, so every CTA holds a
+  // k-range of exactly one tile and reduces one share (split-K).  Taken when
+  // it keeps at least 90% of the SMs streaming (Qwen3-4B: QKV 48 tiles -> 144
+  // CTAs, o_proj / down 20 tiles -> 140).  Under full stream-K the CTAs that
+  // hold pieces of two split tiles reduce both, one after the other, and set
+  // the end of the kernel (measured tail after the last MMA: 8-11 us at M 8-80).
+  if (tc_tile_aligned_split() && pl.tiles < sms) {
+    const int per_tile = sms / pl.tiles < pl.kblocks ? sms / pl.tiles : pl.kblocks;
+    const int g = pl.tiles * per_tile;
+    if ((int64_t)g * 10 >= (int64_t)sms * 9) pl.grid = g;
+  }
   pl.stage_bytes = (int)(((size_t)kTcTileN * kTcBlockK * 2 * pl.accs + (size_t)pl.BN * kTcBlockK * 2 + 1023) / 1024 *
                          1024);
   int stages = (int)(((size_t)tc_stage_budget_kb() * 1024) / pl.stage_bytes);
