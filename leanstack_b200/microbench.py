@@ -54,6 +54,7 @@ def main(argv=None) -> int:
     ap.add_argument("--seq", type=int, default=600, help="cached positions for attention")
     ap.add_argument("--copies", type=int, default=4)
     ap.add_argument("--layers", type=int, default=2, help="layers of the persistent-step case")
+    ap.add_argument("--batch", type=int, default=1, help="sequences of the prefill_attn case")
     args = ap.parse_args(argv)
     g = QWEN3_4B
     dev = torch.device("cuda")
@@ -101,6 +102,18 @@ def main(argv=None) -> int:
         t = _time(lambda i: K.decode_attention(q, kcs[i % 2], vcs[i % 2], m, 1, 32, 8, 128, S, 128 ** -0.5,
                                                cache_pos=pos, out=o, workspace=ws), args.reps)
         out[f"attention(seq={args.seq})"] = (t, m * args.seq * g.kv_dim * 2 * 2)
+    if "prefill_attn" in wanted:  # causal attention of --m prompt tokens per sequence, batch --batch
+        B, P = args.batch, m
+        kc = synth.normal((B, g.num_key_value_heads, P, g.head_dim), 1.0, 0, "mb/pk", device=dev)
+        vc = synth.normal((B, g.num_key_value_heads, P, g.head_dim), 1.0, 0, "mb/pv", device=dev)
+        q = synth.normal((B * P, g.num_attention_heads, g.head_dim), 1.0, 0, "mb/pq", device=dev)
+        o = torch.empty(B * P, g.q_dim, device=dev, dtype=torch.bfloat16)
+        ws = torch.zeros(max(256, K.attention_workspace_bytes(B, P, 32, 8, 128, P)), device=dev, dtype=torch.uint8)
+        t = _time(lambda i: K.decode_attention(q, kc, vc, B, P, 32, 8, 128, P, 128 ** -0.5, uniform_past=0, out=o,
+                                               workspace=ws), args.reps)
+        flops = 4.0 * B * g.num_attention_heads * (P * (P + 1) / 2) * g.head_dim
+        print(json.dumps({"kernel": f"prefill_attention(batch={B}, len={P})", "us": round(t * 1e6, 2),
+                          "tflops": round(flops / t / 1e12, 1)}), flush=True)
     if "oproj" in wanted:
         ow = w((H, g.q_dim), "mb/o")
         a = synth.normal((m, g.q_dim), 1.0, 0, "mb/a", device=dev)
