@@ -1162,3 +1162,401 @@ extern "C" int ls_gemm_tc_set_trace(void* buffer) {
   lsb_host::g_tc_trace = static_cast<unsigned long long*>(buffer);
   return LS_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Causal GQA prefill attention on tcgen05 (config 5).
+//
+// Same contract as prefill_attention_kernel (attention_prefill.cu): query row
+// r = (token i, group member g) of kv head h in sequence b sees keys
+// 0 .. cache_pos[b] + i (src/leanstack/runtime/qwen_explicit.py:551-563,
+// :1000-1039).  A CTA owns 128 consecutive rows of one (sequence, kv head)
+// (the MMA's M) and walks 128-key tiles of the cache:
+//   * warp 4 streams K and V tiles with TMA (128-byte swizzle) into a 2-stage
+//     ring; the rows of one (b, h) are contiguous [S, 128] strips;
+//   * warp 5 issues S = Q K^T into TMEM columns [0, 128) (Q and K K-major),
+//     then O += P V into columns [128, 256) with V as an MN-major B operand
+//     (the cache's [key][dim] layout read as dims x keys: 64-dim halves 16 KB
+//     apart, 8-key groups 1 KB apart), and S of the next tile while the
+//     softmax of the current one runs;
+//   * warps 0-3 own one row each (TMEM lane = row): mask, online softmax in
+//     fp32 (exp2 of the log2-scaled scores), P split into bf16 hi + lo (about
+//     16 bits of the probability, as the mma.sync kernels do) written to
+//     shared memory in the K-major layout, O rescaled in TMEM when the row
+//     maximum grows, and finally O / l stored as bf16.
+// V rows past the last visible key are zeroed in shared memory before the PV
+// product: the cache beyond a sequence's length is the caller's memory and may
+// hold anything, and 0 x NaN is NaN.  Every wait is bounded (LS_ERR_TIMEOUT).
+// ---------------------------------------------------------------------------
+namespace lsb {
+
+constexpr int kPtRows = 128;   // query rows per CTA (MMA M)
+constexpr int kPtKeys = 128;   // keys per tile (S's N, PV's K)
+constexpr int kPtHalf = 16384; // one 64-wide half of a [128 x 128] bf16 tile
+constexpr int kPtTile = 2 * kPtHalf;
+constexpr int kPtQ = 0, kPtPhi = kPtTile, kPtPlo = 2 * kPtTile, kPtRing = 3 * kPtTile;  // byte offsets
+constexpr int kPtStage = 2 * kPtTile;  // K + V
+constexpr int kPtStages = 2;
+constexpr int kPtBars = kPtRing + kPtStages * kPtStage;  // 229376
+constexpr int kPtSmem = 1024 + kPtBars + 128;
+constexpr int kPtThreads = 192;
+
+struct PtParams {
+  const __nv_bfloat16* q;  // [M, Hq, D]
+  const int* cache_pos;    // [B] or null (then uniform_past)
+  int uniform_past;
+  __nv_bfloat16* out;      // [M, Hq * D]
+  int* err;
+  int q_len, Hq, Hkv, G, R, max_seq;
+  float scale_log2;
+};
+
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t saddr) {
+  // MN-major, 128-byte swizzle: 64-element MN chunks 16 KB apart (LBO), 8-row
+  // K groups 1024 B apart (SBO), descriptor version 1, layout SWIZZLE_128B.
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(kPtHalf >> 4) << 16) | (64ull << 32) | (1ull << 46) |
+         (2ull << 61);
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float v[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+      "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+      "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Byte offset of 16-byte chunk c (0..15) of row r in a K-major [128 x 128] tile
+// stored as two 64-wide halves with the 128-byte swizzle.
+__device__ __forceinline__ uint32_t pt_off(int r, int c) {
+  return (uint32_t)((c >> 3) * kPtHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(kPtThreads, 1)
+    prefill_attention_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                                PtParams p) {
+  extern __shared__ unsigned char pt_smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<size_t>(pt_smem_raw) + 1023) & ~size_t(1023));
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + kPtBars);
+  uint64_t* kv_empty = kv_full + kPtStages;
+  uint64_t* q_full = kv_empty + kPtStages;
+  uint64_t* s_full = q_full + 1;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* p_full = s_free + 1;
+  uint64_t* o_done = p_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
+  __shared__ int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, hkv = blockIdx.y;
+  const int r0 = (gridDim.x - 1 - blockIdx.x) * kPtRows;  // longest row blocks first
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPtStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(q_full, kPtRows);
+    mbar_init(s_full, 1);
+    mbar_init(s_free, kPtRows);
+    mbar_init(p_full, kPtRows);
+    mbar_init(o_done, 1);
+    s_abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(256)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + kPtKeys;
+
+  // The cache and the queries are written by the previous kernel.
+  grid_dep_wait();
+  grid_dep_launch();
+  const int cp = p.cache_pos ? p.cache_pos[b] : p.uniform_past;
+  int L = cp + p.q_len;
+  if (L > p.max_seq || cp < 0) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) raise_device_error(p.err, LS_ERR_KV_OVERFLOW);
+    L = min(max(L, 0), p.max_seq);
+  }
+  const int r_last = min(r0 + kPtRows, p.R) - 1;
+  const int L_blk = min(L, cp + r_last / p.G + 1);
+  const int ntiles = L_blk > 0 ? (L_blk + kPtKeys - 1) / kPtKeys : 0;
+  const int kv_row0 = (b * p.Hkv + hkv) * p.max_seq;
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      for (int kt = 0; kt < ntiles && !*(volatile int*)&s_abort; ++kt) {
+        const int s = kt % kPtStages;
+        if (kt >= kPtStages && !mbar_wait(&kv_empty[s], (uint32_t)((kt / kPtStages) - 1) & 1u, p.err, 0x21)) {
+          s_abort = 1;
+          break;
+        }
+        unsigned char* st = smem + kPtRing + s * kPtStage;
+        mbar_arrive_expect_tx(&kv_full[s], kPtStage);
+        const int y = kv_row0 + kt * kPtKeys;
+        tma_load_2d(st, &tm_k, 0, y, &kv_full[s]);
+        tma_load_2d(st + kPtHalf, &tm_k, 64, y, &kv_full[s]);
+        tma_load_2d(st + kPtTile, &tm_v, 0, y, &kv_full[s]);
+        tma_load_2d(st + kPtTile + kPtHalf, &tm_v, 64, y, &kv_full[s]);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && ntiles > 0) {
+      constexpr uint32_t idesc_s = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPtKeys >> 3) << 17) |
+                                   ((uint32_t)(kPtRows >> 4) << 24);
+      constexpr uint32_t idesc_pv = idesc_s | (1u << 16);  // B (V) MN-major; N = 128 dims
+      const uint32_t sQ = smem_u32(smem + kPtQ), sPh = smem_u32(smem + kPtPhi), sPl = smem_u32(smem + kPtPlo);
+      auto issue_s = [&](int kt) -> bool {
+        const int s = kt % kPtStages;
+        if (!mbar_wait(&kv_full[s], (uint32_t)(kt / kPtStages) & 1u, p.err, 0x22)) return false;
+        if (kt > 0 && !mbar_wait(s_free, (uint32_t)(kt - 1) & 1u, p.err, 0x23)) return false;
+        tc_fence_after();
+        const uint32_t sK = smem_u32(smem + kPtRing + s * kPtStage);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * kPtHalf + (kk & 3) * 32);
+          umma_f16(tS, umma_desc_sw128(sQ + off), umma_desc_sw128(sK + off), idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0u, p.err, 0x24) && issue_s(0);
+      for (int kt = 0; ok && kt < ntiles; ++kt) {
+        if (kt + 1 < ntiles && !issue_s(kt + 1)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(p_full, (uint32_t)kt & 1u, p.err, 0x25)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sV = smem_u32(smem + kPtRing + (kt % kPtStages) * kPtStage + kPtTile);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t bdesc = umma_desc_sw128_mn(sV + kk * 2048);
+          const uint32_t off = (uint32_t)((kk >> 2) * kPtHalf + (kk & 3) * 32);
+          umma_f16(tO, umma_desc_sw128(sPh + off), bdesc, idesc_pv, (kt > 0 || kk > 0) ? 1u : 0u);
+          umma_f16(tO, umma_desc_sw128(sPl + off), bdesc, idesc_pv, 1u);
+        }
+        umma_commit(o_done);
+        umma_commit(&kv_empty[kt % kPtStages]);
+      }
+      if (!ok) s_abort = 1;
+    }
+  } else {
+    // ---------------- softmax / epilogue: warps 0-3, one query row per thread ----------------
+    const int r = warp * 32 + lane;
+    const int row = r0 + r;
+    const bool valid = row < p.R;
+    const int i = valid ? row / p.G : 0;
+    const int gq = valid ? row - i * p.G : 0;
+    const int lim = valid ? cp + i : -1;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    {  // Q row into shared memory (zeros for rows past the end)
+      const uint4* qp = reinterpret_cast<const uint4*>(p.q + ((size_t)(b * p.q_len + i) * p.Hq + hkv * p.G + gq) * 128);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint4 v = valid ? qp[c] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(smem + kPtQ + pt_off(r, c)) = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(q_full);
+    }
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int kt = 0; kt < ntiles; ++kt) {
+      if (!mbar_wait(s_full, (uint32_t)kt & 1u, p.err, 0x26)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[kPtKeys];
+#pragma unroll
+      for (int c = 0; c < kPtKeys / 16; ++c) tmem_ld16(tS + lane_off + (uint32_t)(c * 16), sv + c * 16);
+      tc_fence_before();
+      mbar_arrive(s_free);  // S is in registers: the next tile's QK^T may overwrite it
+      const int j0 = kt * kPtKeys;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < kPtKeys; ++e) {
+        const float v = (j0 + e > lim) ? -INFINITY : sv[e] * p.scale_log2;
+        sv[e] = v;
+        mx = fmaxf(mx, v);
+      }
+      const float mn = fmaxf(m_run, mx);
+      const float corr = (mn == -INFINITY) ? 1.f : exp2f(m_run - mn);
+      m_run = mn;
+      float ps = 0.f;
+#pragma unroll
+      for (int e = 0; e < kPtKeys; ++e) {
+        const float pv = (m_run == -INFINITY) ? 0.f : exp2f(sv[e] - m_run);
+        sv[e] = pv;
+        ps += pv;
+      }
+      l_run = l_run * corr + ps;
+      // The previous PV product must be done before P is overwritten and O rescaled.
+      if (kt > 0) {
+        if (!mbar_wait(o_done, (uint32_t)(kt - 1) & 1u, p.err, 0x27)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // tcgen05.ld / st are warp-collective: the whole warp rescales when any
+        // of its rows needs it (corr is 1 for the others).
+        if (__any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < 8; ++c) {
+            float ov[16];
+            tmem_ld16(tO + lane_off + (uint32_t)(c * 16), ov);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) ov[e] *= corr;
+            tmem_st16(tO + lane_off + (uint32_t)(c * 16), ov);
+          }
+          tmem_st_wait();
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x0 = sv[c * 8 + 2 * e], x1 = sv[c * 8 + 2 * e + 1];
+          const float h0 = round_bf16(x0), h1 = round_bf16(x1);
+          __nv_bfloat162 hv = __floats2bfloat162_rn(h0, h1), lv = __floats2bfloat162_rn(x0 - h0, x1 - h1);
+          hi[e] = *reinterpret_cast<uint32_t*>(&hv);
+          lo[e] = *reinterpret_cast<uint32_t*>(&lv);
+        }
+        *reinterpret_cast<uint4*>(smem + kPtPhi + pt_off(r, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(smem + kPtPlo + pt_off(r, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
+      if (j0 + kPtKeys > L_blk) {
+        // Last tile: zero the V rows past the last visible key (row r = key j0 + r).
+        const int s = kt % kPtStages;
+        if (!mbar_wait(&kv_full[s], (uint32_t)(kt / kPtStages) & 1u, p.err, 0x28)) {
+          ok = false;
+          break;
+        }
+        if (j0 + r >= L_blk) {
+          unsigned char* vt = smem + kPtRing + s * kPtStage + kPtTile;
+#pragma unroll
+          for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4*>(vt + pt_off(r, c)) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // Epilogue: O / l as bf16.
+    if (ok && ntiles > 0 && mbar_wait(o_done, (uint32_t)(ntiles - 1) & 1u, p.err, 0x29)) {
+      tc_fence_after();
+      // Every lane loads (warp-collective tcgen05.ld); only valid rows store.
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      uint4* op = reinterpret_cast<uint4*>(p.out + ((size_t)(b * p.q_len + i) * p.Hq + hkv * p.G + gq) * 128);
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        float ov[16];
+        tmem_ld16(tO + lane_off + (uint32_t)(c * 16), ov);
+        uint32_t pk[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          __nv_bfloat162 v2 = __floats2bfloat162_rn(ov[2 * e] * inv, ov[2 * e + 1] * inv);
+          pk[e] = *reinterpret_cast<uint32_t*>(&v2);
+        }
+        if (valid) {
+          op[2 * c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          op[2 * c + 1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+      }
+    } else if (!ok) {
+      s_abort = 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
+  }
+}
+
+}  // namespace lsb
+
+namespace lsb_host {
+
+// Causal prefill attention on tcgen05 (see prefill_attention_tc_kernel).
+// LEANB200_PREFILL_ATTN=mma selects the mma.sync kernel instead (measurement).
+bool prefill_attention_tc_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("LEANB200_PREFILL_ATTN");
+    v = (e && e[0] == 'm') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+int launch_prefill_attention_tc(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
+                                int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv,
+                                int64_t max_seq, float scale, void* out, cudaStream_t stream) {
+  const int64_t kv_rows = batch * hkv * max_seq;
+  if (hkv > 65535 || batch > 65535 || kv_rows + kPtKeys > (1ll << 31) || q_len * hq > (1ll << 31))
+    return set_error(LS_ERR_UNSUPPORTED_SHAPE, "prefill_attention_tc: %lld sequences x %lld kv heads x %lld positions",
+                     (long long)batch, (long long)hkv, (long long)max_seq);
+  PtParams p = {};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.cache_pos = cache_pos;
+  p.uniform_past = (int)uniform_past;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.q_len = (int)q_len;
+  p.Hq = (int)hq;
+  p.Hkv = (int)hkv;
+  p.G = (int)(hq / hkv);
+  p.R = (int)(q_len * p.G);
+  p.max_seq = (int)max_seq;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.err = device_error_ptr();
+  CUtensorMap mk, mv;
+  int rc = make_map(&mk, k_cache, kv_rows, 128, kPtKeys);
+  if (rc) return rc;
+  rc = make_map(&mv, v_cache, kv_rows, 128, kPtKeys);
+  if (rc) return rc;
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kPtSmem);
+    if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "prefill_attention_tc attribute: %s", cudaGetErrorString(e));
+    configured[dev] = 1;
+  }
+  const int row_blocks = (int)((p.R + kPtRows - 1) / kPtRows);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)row_blocks, (unsigned)hkv, (unsigned)batch);
+  cfg.blockDim = dim3(kPtThreads);
+  cfg.dynamicSmemBytes = kPtSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_attention_tc_kernel, mk, mv, p);
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "prefill_attention_tc launch: %s", cudaGetErrorString(e));
+}
+
+}  // namespace lsb_host
