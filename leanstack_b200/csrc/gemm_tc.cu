@@ -1178,11 +1178,15 @@ extern "C" int ls_gemm_tc_set_trace(void* buffer) {
 //     (the cache's [key][dim] layout read as dims x keys: 64-dim halves 16 KB
 //     apart, 8-key groups 1 KB apart), and S of the next tile while the
 //     softmax of the current one runs;
-//   * warps 0-3 own one row each (TMEM lane = row): mask, online softmax in
-//     fp32 (exp2 of the log2-scaled scores), P split into bf16 hi + lo (about
-//     16 bits of the probability, as the mma.sync kernels do) written to
-//     shared memory in the K-major layout, O rescaled in TMEM when the row
-//     maximum grows, and finally O / l stored as bf16.
+//   * warps 0-7 run the softmax, two threads per row: warps w and w + 4 read
+//     TMEM lanes 32 (w % 4) .. + 31 (row = lane) and own keys / output dims
+//     [0, 64) and [64, 128) respectively.  Both take the maximum over the
+//     whole 128-score row (exact and order-free, so they agree) and
+//     exponentiate their own half: online softmax in fp32 (exp2 of the
+//     log2-scaled scores), P split into bf16 hi + lo (about 16 bits of the
+//     probability, as the mma.sync kernels do) written to shared memory in the
+//     K-major layout, O rescaled in TMEM when the row maximum grows, and
+//     finally O / l stored as bf16 (the two halves' row sums added once).
 // V rows past the last visible key are zeroed in shared memory before the PV
 // product: the cache beyond a sequence's length is the caller's memory and may
 // hold anything, and 0 x NaN is NaN.  Every wait is bounded (LS_ERR_TIMEOUT).
@@ -1198,7 +1202,8 @@ constexpr int kPtStage = 2 * kPtTile;  // K + V
 constexpr int kPtStages = 2;
 constexpr int kPtBars = kPtRing + kPtStages * kPtStage;  // 229376
 constexpr int kPtSmem = 1024 + kPtBars + 128;
-constexpr int kPtThreads = 192;
+constexpr int kPtThreads = 320;  // 8 softmax warps, TMA warp 8, MMA warp 9
+constexpr int kPtSoft = 256;
 
 struct PtParams {
   const __nv_bfloat16* q;  // [M, Hq, D]
@@ -1261,10 +1266,10 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    mbar_init(q_full, kPtRows);
+    mbar_init(q_full, kPtSoft);
     mbar_init(s_full, 1);
-    mbar_init(s_free, kPtRows);
-    mbar_init(p_full, kPtRows);
+    mbar_init(s_free, kPtSoft);
+    mbar_init(p_full, kPtSoft);
     mbar_init(o_done, 1);
     s_abort = 0;
     mbar_fence_init();
@@ -1295,7 +1300,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
   const int ntiles = L_blk > 0 ? (L_blk + kPtKeys - 1) / kPtKeys : 0;
   const int kv_row0 = (b * p.Hkv + hkv) * p.max_seq;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       for (int kt = 0; kt < ntiles && !*(volatile int*)&s_abort; ++kt) {
@@ -1313,7 +1318,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         tma_load_2d(st + kPtTile + kPtHalf, &tm_v, 64, y, &kv_full[s]);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && ntiles > 0) {
       constexpr uint32_t idesc_s = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPtKeys >> 3) << 17) |
@@ -1359,42 +1364,54 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       if (!ok) s_abort = 1;
     }
   } else {
-    // ---------------- softmax / epilogue: warps 0-3, one query row per thread ----------------
-    const int r = warp * 32 + lane;
+    // ---------------- softmax / epilogue: warps 0-7, two threads per query row ----------------
+    const int quad = warp & 3, ch = warp >> 2;  // TMEM lane quadrant; key / dim half
+    const int r = quad * 32 + lane;
     const int row = r0 + r;
     const bool valid = row < p.R;
     const int i = valid ? row / p.G : 0;
     const int gq = valid ? row - i * p.G : 0;
     const int lim = valid ? cp + i : -1;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    {  // Q row into shared memory (zeros for rows past the end)
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t own = (uint32_t)(ch * 64), other = (uint32_t)((1 - ch) * 64);
+    {  // this thread's half of the Q row into shared memory (zeros for rows past the end)
       const uint4* qp = reinterpret_cast<const uint4*>(p.q + ((size_t)(b * p.q_len + i) * p.Hq + hkv * p.G + gq) * 128);
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const uint4 v = valid ? qp[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(smem + kPtQ + pt_off(r, c)) = v;
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = valid ? qp[ch * 8 + c] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(smem + kPtQ + pt_off(r, ch * 8 + c)) = v;
       }
       fence_proxy_async_smem();
       mbar_arrive(q_full);
     }
-    float m_run = -INFINITY, l_run = 0.f;
+    float m_run = -INFINITY, l_half = 0.f;
     bool ok = true;
     for (int kt = 0; kt < ntiles; ++kt) {
-      if (!mbar_wait(s_full, (uint32_t)kt & 1u, p.err, 0x26)) {
+      // Wait results are made warp-uniform: the tcgen05.ld / st below are
+      // warp-collective and must not be reached by part of a warp.
+      if (!__all_sync(0xffffffffu, mbar_wait(s_full, (uint32_t)kt & 1u, p.err, 0x26))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float sv[kPtKeys];
-#pragma unroll
-      for (int c = 0; c < kPtKeys / 16; ++c) tmem_ld16(tS + lane_off + (uint32_t)(c * 16), sv + c * 16);
-      tc_fence_before();
-      mbar_arrive(s_free);  // S is in registers: the next tile's QK^T may overwrite it
       const int j0 = kt * kPtKeys;
+      float sv[64];
       float mx = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < kPtKeys; ++e) {
-        const float v = (j0 + e > lim) ? -INFINITY : sv[e] * p.scale_log2;
+      for (int c = 0; c < 4; ++c) {  // the partner's half: only its maximum is needed here
+        float t[16];
+        tmem_ld16(tS + lane_off + other + (uint32_t)(c * 16), t);
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          mx = fmaxf(mx, (j0 + (int)other + c * 16 + e > lim) ? -INFINITY : t[e] * p.scale_log2);
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld16(tS + lane_off + own + (uint32_t)(c * 16), sv + c * 16);
+      tc_fence_before();
+      mbar_arrive(s_free);  // S is in registers: the next tile's QK^T may overwrite it
+#pragma unroll
+      for (int e = 0; e < 64; ++e) {
+        const float v = (j0 + (int)own + e > lim) ? -INFINITY : sv[e] * p.scale_log2;
         sv[e] = v;
         mx = fmaxf(mx, v);
       }
@@ -1403,35 +1420,34 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       m_run = mn;
       float ps = 0.f;
 #pragma unroll
-      for (int e = 0; e < kPtKeys; ++e) {
+      for (int e = 0; e < 64; ++e) {
         const float pv = (m_run == -INFINITY) ? 0.f : exp2f(sv[e] - m_run);
         sv[e] = pv;
         ps += pv;
       }
-      l_run = l_run * corr + ps;
+      l_half = l_half * corr + ps;
       // The previous PV product must be done before P is overwritten and O rescaled.
       if (kt > 0) {
-        if (!mbar_wait(o_done, (uint32_t)(kt - 1) & 1u, p.err, 0x27)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(o_done, (uint32_t)(kt - 1) & 1u, p.err, 0x27))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // tcgen05.ld / st are warp-collective: the whole warp rescales when any
-        // of its rows needs it (corr is 1 for the others).
+        // The whole warp rescales when any of its rows needs it (corr is 1 for the others).
         if (__any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < 8; ++c) {
+          for (int c = 0; c < 4; ++c) {
             float ov[16];
-            tmem_ld16(tO + lane_off + (uint32_t)(c * 16), ov);
+            tmem_ld16(tO + lane_off + own + (uint32_t)(c * 16), ov);
 #pragma unroll
             for (int e = 0; e < 16; ++e) ov[e] *= corr;
-            tmem_st16(tO + lane_off + (uint32_t)(c * 16), ov);
+            tmem_st16(tO + lane_off + own + (uint32_t)(c * 16), ov);
           }
           tmem_st_wait();
         }
       }
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c = 0; c < 8; ++c) {
         uint32_t hi[4], lo[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -1441,36 +1457,45 @@ __global__ void __launch_bounds__(kPtThreads, 1)
           hi[e] = *reinterpret_cast<uint32_t*>(&hv);
           lo[e] = *reinterpret_cast<uint32_t*>(&lv);
         }
-        *reinterpret_cast<uint4*>(smem + kPtPhi + pt_off(r, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(smem + kPtPlo + pt_off(r, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(smem + kPtPhi + pt_off(r, ch * 8 + c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(smem + kPtPlo + pt_off(r, ch * 8 + c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
       if (j0 + kPtKeys > L_blk) {
-        // Last tile: zero the V rows past the last visible key (row r = key j0 + r).
+        // Last tile: zero this thread's half of the V rows past the last visible key (row r = key j0 + r).
         const int s = kt % kPtStages;
-        if (!mbar_wait(&kv_full[s], (uint32_t)(kt / kPtStages) & 1u, p.err, 0x28)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&kv_full[s], (uint32_t)(kt / kPtStages) & 1u, p.err, 0x28))) {
           ok = false;
           break;
         }
         if (j0 + r >= L_blk) {
           unsigned char* vt = smem + kPtRing + s * kPtStage + kPtTile;
 #pragma unroll
-          for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4*>(vt + pt_off(r, c)) = make_uint4(0, 0, 0, 0);
+          for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vt + pt_off(r, ch * 8 + c)) = make_uint4(0, 0, 0, 0);
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    // Epilogue: O / l as bf16.
-    if (ok && ntiles > 0 && mbar_wait(o_done, (uint32_t)(ntiles - 1) & 1u, p.err, 0x29)) {
+    // Epilogue: O / l as bf16, l = the two halves' sums (added in a fixed order).
+    // Every softmax thread reaches the named barrier, on error paths too.
+    const bool fin = __all_sync(0xffffffffu, ok && ntiles > 0 &&
+                                                 mbar_wait(o_done, (uint32_t)(ntiles - 1) & 1u, p.err, 0x29));
+    float* lsum = reinterpret_cast<float*>(smem + kPtPhi);  // P is no longer read once the last PV is done
+    if (fin) {
       tc_fence_after();
+      lsum[ch * kPtRows + r] = l_half;
+    }
+    named_bar_sync(1, kPtSoft);
+    if (fin) {
+      const float l = lsum[r] + lsum[kPtRows + r];
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint4* op = reinterpret_cast<uint4*>(p.out + ((size_t)(b * p.q_len + i) * p.Hq + hkv * p.G + gq) * 128 + ch * 64);
       // Every lane loads (warp-collective tcgen05.ld); only valid rows store.
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      uint4* op = reinterpret_cast<uint4*>(p.out + ((size_t)(b * p.q_len + i) * p.Hq + hkv * p.G + gq) * 128);
 #pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         float ov[16];
-        tmem_ld16(tO + lane_off + (uint32_t)(c * 16), ov);
+        tmem_ld16(tO + lane_off + own + (uint32_t)(c * 16), ov);
         uint32_t pk[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
