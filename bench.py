@@ -316,7 +316,7 @@ def run_prefill(rt, comm, shard, batch: int, plen: int, decode_steps: int, world
            "prefill_tok_per_s": batch * plen / t, "linear_tflops": flops / t / 1e12,
            "linear_tensor_frac_per_gpu": flops / world / t / 1e12 / peaks.get("bf16_tflops", 1663.3),
            "decode_steps": decode_steps, "decode_tok_per_s": batch * decode_steps / td,
-           "attention": "128-row causal prefill kernel (prefill_attention_kernel, mma.sync)"}
+           "attention": "causal prefill attention on tcgen05 (prefill_attention_tc_kernel: S and O in TMEM)"}
     eng.graph = None
     del eng
     torch.cuda.empty_cache()
