@@ -1194,16 +1194,23 @@ extern "C" int ls_gemm_tc_set_trace(void* buffer) {
 namespace lsb {
 
 constexpr int kPtRows = 128;   // query rows per CTA (MMA M)
-constexpr int kPtKeys = 128;   // keys per tile (S's N, PV's K)
-constexpr int kPtHalf = 16384; // one 64-wide half of a [128 x 128] bf16 tile
-constexpr int kPtTile = 2 * kPtHalf;
-constexpr int kPtQ = 0, kPtPhi = kPtTile, kPtPlo = 2 * kPtTile, kPtRing = 3 * kPtTile;  // byte offsets
-constexpr int kPtStage = 2 * kPtTile;  // K + V
-constexpr int kPtStages = 2;
-constexpr int kPtBars = kPtRing + kPtStages * kPtStage;  // 229376
+constexpr int kPtKeys = 64;    // keys per tile (S's N, PV's K)
+constexpr int kPtQHalf = 16384;              // Q: two 64-dim halves of [128 rows x 64] bf16
+constexpr int kPtKvHalf = 8192;              // K or V tile: two 64-dim halves of [64 keys x 64] bf16
+constexpr int kPtP = 8192 * 2;               // one P tile [128 rows x 64 keys] bf16 = 16 KB (hi or lo)
+constexpr int kPtQ = 0;
+constexpr int kPtPbuf = 2 * kPtQHalf;        // P buffers: 2 x (hi, lo)
+constexpr int kPtRing = kPtPbuf + 2 * 2 * kPtP;
+constexpr int kPtStage = 4 * kPtKvHalf;      // K + V of one tile: 32 KB
+constexpr int kPtStages = 3;
+constexpr int kPtBars = kPtRing + kPtStages * kPtStage;  // 196608
 constexpr int kPtSmem = 1024 + kPtBars + 128;
 constexpr int kPtThreads = 320;  // 8 softmax warps, TMA warp 8, MMA warp 9
 constexpr int kPtSoft = 256;
+// The row maximum used for the exponent only moves (and O is rescaled) when a
+// score exceeds it by more than 2^8: P stays <= 256, well inside what the
+// bf16 hi + lo split represents to about 16 bits.
+constexpr float kPtRescaleLog2 = 8.f;
 
 struct PtParams {
   const __nv_bfloat16* q;  // [M, Hq, D]
@@ -1215,10 +1222,10 @@ struct PtParams {
   float scale_log2;
 };
 
-__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t saddr) {
-  // MN-major, 128-byte swizzle: 64-element MN chunks 16 KB apart (LBO), 8-row
-  // K groups 1024 B apart (SBO), descriptor version 1, layout SWIZZLE_128B.
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(kPtHalf >> 4) << 16) | (64ull << 32) | (1ull << 46) |
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t saddr, uint32_t lbo_bytes) {
+  // MN-major, 128-byte swizzle: 64-element MN chunks lbo_bytes apart (LBO),
+  // 8-row K groups 1024 B apart (SBO), descriptor version 1, SWIZZLE_128B.
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(lbo_bytes >> 4) << 16) | (64ull << 32) | (1ull << 46) |
          (2ull << 61);
 }
 
@@ -1235,11 +1242,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float v[16]) {
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 2^x with the hardware's approximate exp2 (MUFU); 2^-inf = 0.  The softmax
+// probabilities are rounded to about 16 bits afterwards.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
-// Byte offset of 16-byte chunk c (0..15) of row r in a K-major [128 x 128] tile
-// stored as two 64-wide halves with the 128-byte swizzle.
-__device__ __forceinline__ uint32_t pt_off(int r, int c) {
-  return (uint32_t)((c >> 3) * kPtHalf + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+// Byte offset of 16-byte chunk c of row r in a K-major tile stored as 64-wide
+// halves of `half` bytes each (128-byte swizzle; c >> 3 selects the half).
+__device__ __forceinline__ uint32_t pt_off(int r, int c, int half) {
+  return (uint32_t)((c >> 3) * half + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
 __global__ void __launch_bounds__(kPtThreads, 1)
@@ -1252,9 +1266,9 @@ __global__ void __launch_bounds__(kPtThreads, 1)
   uint64_t* q_full = kv_empty + kPtStages;
   uint64_t* s_full = q_full + 1;
   uint64_t* s_free = s_full + 1;
-  uint64_t* p_full = s_free + 1;
-  uint64_t* o_done = p_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
+  uint64_t* p_full = s_free + 1;  // [2]: one per P buffer
+  uint64_t* o_done = p_full + 2;  // [2]: the PV product that read P buffer b is complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
   __shared__ int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1269,8 +1283,10 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     mbar_init(q_full, kPtSoft);
     mbar_init(s_full, 1);
     mbar_init(s_free, kPtSoft);
-    mbar_init(p_full, kPtSoft);
-    mbar_init(o_done, 1);
+    for (int u = 0; u < 2; ++u) {
+      mbar_init(&p_full[u], kPtSoft);
+      mbar_init(&o_done[u], 1);
+    }
     s_abort = 0;
     mbar_fence_init();
   }
@@ -1284,7 +1300,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + kPtKeys;
+  const uint32_t tS = tmem, tO = tmem + 128;  // S: columns [0, 64); O: [128, 256)
 
   // The cache and the queries are written by the previous kernel.
   grid_dep_wait();
@@ -1313,9 +1329,9 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         mbar_arrive_expect_tx(&kv_full[s], kPtStage);
         const int y = kv_row0 + kt * kPtKeys;
         tma_load_2d(st, &tm_k, 0, y, &kv_full[s]);
-        tma_load_2d(st + kPtHalf, &tm_k, 64, y, &kv_full[s]);
-        tma_load_2d(st + kPtTile, &tm_v, 0, y, &kv_full[s]);
-        tma_load_2d(st + kPtTile + kPtHalf, &tm_v, 64, y, &kv_full[s]);
+        tma_load_2d(st + kPtKvHalf, &tm_k, 64, y, &kv_full[s]);
+        tma_load_2d(st + 2 * kPtKvHalf, &tm_v, 0, y, &kv_full[s]);
+        tma_load_2d(st + 3 * kPtKvHalf, &tm_v, 64, y, &kv_full[s]);
       }
     }
   } else if (warp == 9) {
@@ -1323,8 +1339,9 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     if (lane == 0 && ntiles > 0) {
       constexpr uint32_t idesc_s = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPtKeys >> 3) << 17) |
                                    ((uint32_t)(kPtRows >> 4) << 24);
-      constexpr uint32_t idesc_pv = idesc_s | (1u << 16);  // B (V) MN-major; N = 128 dims
-      const uint32_t sQ = smem_u32(smem + kPtQ), sPh = smem_u32(smem + kPtPhi), sPl = smem_u32(smem + kPtPlo);
+      constexpr uint32_t idesc_pv = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(128 >> 3) << 17) |
+                                    ((uint32_t)(kPtRows >> 4) << 24);  // B (V) MN-major; N = 128 dims
+      const uint32_t sQ = smem_u32(smem + kPtQ);
       auto issue_s = [&](int kt) -> bool {
         const int s = kt % kPtStages;
         if (!mbar_wait(&kv_full[s], (uint32_t)(kt / kPtStages) & 1u, p.err, 0x22)) return false;
@@ -1333,8 +1350,9 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         const uint32_t sK = smem_u32(smem + kPtRing + s * kPtStage);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (uint32_t)((kk >> 2) * kPtHalf + (kk & 3) * 32);
-          umma_f16(tS, umma_desc_sw128(sQ + off), umma_desc_sw128(sK + off), idesc_s, kk > 0 ? 1u : 0u);
+          const uint32_t qo = (uint32_t)((kk >> 2) * kPtQHalf + (kk & 3) * 32);
+          const uint32_t ko = (uint32_t)((kk >> 2) * kPtKvHalf + (kk & 3) * 32);
+          umma_f16(tS, umma_desc_sw128(sQ + qo), umma_desc_sw128(sK + ko), idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(s_full);
         return true;
@@ -1345,20 +1363,21 @@ __global__ void __launch_bounds__(kPtThreads, 1)
           ok = false;
           break;
         }
-        if (!mbar_wait(p_full, (uint32_t)kt & 1u, p.err, 0x25)) {
+        const int u = kt & 1;
+        if (!mbar_wait(&p_full[u], (uint32_t)(kt >> 1) & 1u, p.err, 0x25)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sV = smem_u32(smem + kPtRing + (kt % kPtStages) * kPtStage + kPtTile);
+        const uint32_t sPh = smem_u32(smem + kPtPbuf + u * 2 * kPtP), sPl = sPh + kPtP;
+        const uint32_t sV = smem_u32(smem + kPtRing + (kt % kPtStages) * kPtStage + 2 * kPtKvHalf);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t bdesc = umma_desc_sw128_mn(sV + kk * 2048);
-          const uint32_t off = (uint32_t)((kk >> 2) * kPtHalf + (kk & 3) * 32);
-          umma_f16(tO, umma_desc_sw128(sPh + off), bdesc, idesc_pv, (kt > 0 || kk > 0) ? 1u : 0u);
-          umma_f16(tO, umma_desc_sw128(sPl + off), bdesc, idesc_pv, 1u);
+        for (int kk = 0; kk < kPtKeys / 16; ++kk) {
+          const uint64_t bdesc = umma_desc_sw128_mn(sV + kk * 2048, kPtKvHalf);
+          umma_f16(tO, umma_desc_sw128(sPh + kk * 32), bdesc, idesc_pv, (kt > 0 || kk > 0) ? 1u : 0u);
+          umma_f16(tO, umma_desc_sw128(sPl + kk * 32), bdesc, idesc_pv, 1u);
         }
-        umma_commit(o_done);
+        umma_commit(&o_done[u]);
         umma_commit(&kv_empty[kt % kPtStages]);
       }
       if (!ok) s_abort = 1;
@@ -1373,13 +1392,14 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     const int gq = valid ? row - i * p.G : 0;
     const int lim = valid ? cp + i : -1;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t own = (uint32_t)(ch * 64), other = (uint32_t)((1 - ch) * 64);
+    constexpr int kHalfKeys = kPtKeys / 2;  // 32 keys of each tile per thread
+    const int own = ch * kHalfKeys, other = (1 - ch) * kHalfKeys;
     {  // this thread's half of the Q row into shared memory (zeros for rows past the end)
       const uint4* qp = reinterpret_cast<const uint4*>(p.q + ((size_t)(b * p.q_len + i) * p.Hq + hkv * p.G + gq) * 128);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint4 v = valid ? qp[ch * 8 + c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(smem + kPtQ + pt_off(r, ch * 8 + c)) = v;
+        *reinterpret_cast<uint4*>(smem + kPtQ + pt_off(r, ch * 8 + c, kPtQHalf)) = v;
       }
       fence_proxy_async_smem();
       mbar_arrive(q_full);
@@ -1395,59 +1415,87 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       }
       tc_fence_after();
       const int j0 = kt * kPtKeys;
-      float sv[64];
-      float mx = -INFINITY;
+      float sv[kHalfKeys], t[kHalfKeys];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {  // the partner's half: only its maximum is needed here
-        float t[16];
-        tmem_ld16(tS + lane_off + other + (uint32_t)(c * 16), t);
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          mx = fmaxf(mx, (j0 + (int)other + c * 16 + e > lim) ? -INFINITY : t[e] * p.scale_log2);
+      for (int c = 0; c < kHalfKeys / 16; ++c) {
+        tmem_ld16(tS + lane_off + (uint32_t)(other + c * 16), t + c * 16);
+        tmem_ld16(tS + lane_off + (uint32_t)(own + c * 16), sv + c * 16);
       }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld16(tS + lane_off + own + (uint32_t)(c * 16), sv + c * 16);
       tc_fence_before();
       mbar_arrive(s_free);  // S is in registers: the next tile's QK^T may overwrite it
+      // Both threads of a row take the maximum over the whole row (the same raw
+      // scores in another order; max is exact and order-free, and the scale is
+      // positive, so the scaled maximum is that of the scaled scores).  Tiles
+      // every row of the warp sees in full skip the causal mask.
+      const bool full = __all_sync(0xffffffffu, j0 + kPtKeys - 1 <= lim);
+      float mraw = -INFINITY;
+      if (full) {
 #pragma unroll
-      for (int e = 0; e < 64; ++e) {
-        const float v = (j0 + (int)own + e > lim) ? -INFINITY : sv[e] * p.scale_log2;
-        sv[e] = v;
-        mx = fmaxf(mx, v);
+        for (int e = 0; e < kHalfKeys; ++e) mraw = fmaxf(mraw, fmaxf(t[e], sv[e]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < kHalfKeys; ++e) {
+          mraw = fmaxf(mraw, (j0 + other + e > lim) ? -INFINITY : t[e]);
+          mraw = fmaxf(mraw, (j0 + own + e > lim) ? -INFINITY : sv[e]);
+        }
       }
-      const float mn = fmaxf(m_run, mx);
-      const float corr = (mn == -INFINITY) ? 1.f : exp2f(m_run - mn);
-      m_run = mn;
+      const float mt = (mraw == -INFINITY) ? -INFINITY : mraw * p.scale_log2;
+      bool resc = false;
+      float corr = 1.f;
+      if (m_run == -INFINITY) {
+        m_run = mt;  // first visible keys of this row: nothing accumulated yet
+      } else if (mt > m_run + kPtRescaleLog2) {
+        corr = ex2_approx(m_run - mt);
+        m_run = mt;
+        resc = true;
+      }
       float ps = 0.f;
+      if (m_run == -INFINITY) {
 #pragma unroll
-      for (int e = 0; e < 64; ++e) {
-        const float pv = (m_run == -INFINITY) ? 0.f : exp2f(sv[e] - m_run);
-        sv[e] = pv;
-        ps += pv;
+        for (int e = 0; e < kHalfKeys; ++e) sv[e] = 0.f;
+      } else if (full) {
+#pragma unroll
+        for (int e = 0; e < kHalfKeys; ++e) {
+          const float pv = ex2_approx(fmaf(sv[e], p.scale_log2, -m_run));
+          sv[e] = pv;
+          ps += pv;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < kHalfKeys; ++e) {
+          const float pv = (j0 + own + e > lim) ? 0.f : ex2_approx(fmaf(sv[e], p.scale_log2, -m_run));
+          sv[e] = pv;
+          ps += pv;
+        }
       }
       l_half = l_half * corr + ps;
-      // The previous PV product must be done before P is overwritten and O rescaled.
-      if (kt > 0) {
-        if (!__all_sync(0xffffffffu, mbar_wait(o_done, (uint32_t)(kt - 1) & 1u, p.err, 0x27))) {
+      const int u = kt & 1;
+      // P buffer u was last read by PV(kt - 2).
+      if (kt >= 2 && !__all_sync(0xffffffffu, mbar_wait(&o_done[u], (uint32_t)((kt >> 1) - 1) & 1u, p.err, 0x27))) {
+        ok = false;
+        break;
+      }
+      // O is rescaled once every PV product so far is in it (PV(kt - 1)); the
+      // whole warp joins when any of its rows needs it (corr is 1 for the others).
+      if (__any_sync(0xffffffffu, resc)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_done[u ^ 1], (uint32_t)((kt - 1) >> 1) & 1u, p.err, 0x2a))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // The whole warp rescales when any of its rows needs it (corr is 1 for the others).
-        if (__any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            float ov[16];
-            tmem_ld16(tO + lane_off + own + (uint32_t)(c * 16), ov);
+        for (int c = 0; c < 4; ++c) {
+          float ov[16];
+          tmem_ld16(tO + lane_off + (uint32_t)(ch * 64 + c * 16), ov);
 #pragma unroll
-            for (int e = 0; e < 16; ++e) ov[e] *= corr;
-            tmem_st16(tO + lane_off + own + (uint32_t)(c * 16), ov);
-          }
-          tmem_st_wait();
+          for (int e = 0; e < 16; ++e) ov[e] *= corr;
+          tmem_st16(tO + lane_off + (uint32_t)(ch * 64 + c * 16), ov);
         }
+        tmem_st_wait();
       }
+      unsigned char* ph = smem + kPtPbuf + u * 2 * kPtP;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < kHalfKeys / 8; ++c) {
         uint32_t hi[4], lo[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -1457,31 +1505,35 @@ __global__ void __launch_bounds__(kPtThreads, 1)
           hi[e] = *reinterpret_cast<uint32_t*>(&hv);
           lo[e] = *reinterpret_cast<uint32_t*>(&lv);
         }
-        *reinterpret_cast<uint4*>(smem + kPtPhi + pt_off(r, ch * 8 + c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(smem + kPtPlo + pt_off(r, ch * 8 + c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        const int chunk = ch * (kHalfKeys / 8) + c;  // 8 keys per 16-byte chunk, 8 chunks per 64-key row
+        *reinterpret_cast<uint4*>(ph + pt_off(r, chunk, kPtP)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(ph + kPtP + pt_off(r, chunk, kPtP)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
       if (j0 + kPtKeys > L_blk) {
-        // Last tile: zero this thread's half of the V rows past the last visible key (row r = key j0 + r).
+        // Last tile: zero the V rows past the last visible key; thread (r < 64,
+        // half ch) clears dims [64 ch, 64 ch + 64) of key j0 + r.
         const int s = kt % kPtStages;
         if (!__all_sync(0xffffffffu, mbar_wait(&kv_full[s], (uint32_t)(kt / kPtStages) & 1u, p.err, 0x28))) {
           ok = false;
           break;
         }
-        if (j0 + r >= L_blk) {
-          unsigned char* vt = smem + kPtRing + s * kPtStage + kPtTile;
+        if (r < kPtKeys && j0 + r >= L_blk) {
+          unsigned char* vt = smem + kPtRing + s * kPtStage + 2 * kPtKvHalf;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vt + pt_off(r, ch * 8 + c)) = make_uint4(0, 0, 0, 0);
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(vt + pt_off(r, ch * 8 + c, kPtKvHalf)) = make_uint4(0, 0, 0, 0);
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[u]);
     }
     // Epilogue: O / l as bf16, l = the two halves' sums (added in a fixed order).
     // Every softmax thread reaches the named barrier, on error paths too.
+    const int ul = (ntiles - 1) & 1;
     const bool fin = __all_sync(0xffffffffu, ok && ntiles > 0 &&
-                                                 mbar_wait(o_done, (uint32_t)(ntiles - 1) & 1u, p.err, 0x29));
-    float* lsum = reinterpret_cast<float*>(smem + kPtPhi);  // P is no longer read once the last PV is done
+                                                 mbar_wait(&o_done[ul], (uint32_t)((ntiles - 1) >> 1) & 1u, p.err, 0x29));
+    float* lsum = reinterpret_cast<float*>(smem + kPtPbuf);  // P is no longer read once the last PV is done
     if (fin) {
       tc_fence_after();
       lsum[ch * kPtRows + r] = l_half;
@@ -1495,7 +1547,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float ov[16];
-        tmem_ld16(tO + lane_off + own + (uint32_t)(c * 16), ov);
+        tmem_ld16(tO + lane_off + (uint32_t)(ch * 64 + c * 16), ov);
         uint32_t pk[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -1556,7 +1608,7 @@ int launch_prefill_attention_tc(const void* q, const void* k_cache, const void* 
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = device_error_ptr();
   CUtensorMap mk, mv;
-  int rc = make_map(&mk, k_cache, kv_rows, 128, kPtKeys);
+  int rc = make_map(&mk, k_cache, kv_rows, 128, kPtKeys);  // boxes of 64 dims x 64 keys
   if (rc) return rc;
   rc = make_map(&mv, v_cache, kv_rows, 128, kPtKeys);
   if (rc) return rc;
