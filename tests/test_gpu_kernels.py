@@ -271,6 +271,42 @@ def test_prefill_attention_matches_fp64(batch, q_len, past):
     assert K.device_error() == 0
 
 
+@pytest.mark.parametrize("hq,hkv,batch,q_len,past", [(16, 8, 2, 150, 19), (32, 8, 1, 300, 0), (32, 8, 3, 70, 1)])
+def test_prefill_attention_ignores_cache_past_the_sequence(hq, hkv, batch, q_len, past):
+    """Cache positions past each sequence's length hold NaN (the cache is the caller's
+    memory): the prefill kernel must keep them out of the result, since 0 x NaN is NaN.
+    Also covers 2 query heads per kv head (the 0.6B draft geometry) and lengths that
+    end inside a key tile."""
+    d, S = 128, 640
+    gen = torch.Generator(device="cpu").manual_seed(31 + q_len)
+    q = torch.randn(batch * q_len, hq, d, generator=gen).bfloat16()
+    kc = torch.randn(batch, hkv, S, d, generator=gen).bfloat16()
+    vc = torch.randn(batch, hkv, S, d, generator=gen).bfloat16()
+    pos = [past + 7 * b for b in range(batch)]
+    for b in range(batch):
+        kc[b, :, pos[b] + q_len:] = float("nan")
+        vc[b, :, pos[b] + q_len:] = float("nan")
+    scale = d ** -0.5
+    out = K.decode_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), batch, q_len, hq, hkv, d, S, scale,
+                             cache_pos=torch.tensor(pos, dtype=torch.int32, device=DEV))
+    torch.cuda.synchronize()
+    G = hq // hkv
+    qd, kd, vd = q.double(), kc.double(), vc.double()
+    ref = torch.empty(batch * q_len, hq, d, dtype=torch.float64)
+    for b in range(batch):
+        L = pos[b] + q_len
+        mask = torch.arange(L)[None, :] > (pos[b] + torch.arange(q_len))[:, None]
+        for h in range(hq):
+            s = (qd[b * q_len:(b + 1) * q_len, h] @ kd[b, h // G, :L].t()) * scale
+            ref[b * q_len:(b + 1) * q_len, h] = torch.softmax(s.masked_fill(mask, float("-inf")), -1) @ vd[b, h // G, :L]
+    ref = ref.view(batch * q_len, hq * d)
+    got = out.double().cpu()
+    assert torch.isfinite(got).all()
+    assert (got - ref).abs().max().item() <= 1e-2
+    assert (out.cpu() == ref.bfloat16()).float().mean().item() > 0.99
+    assert K.device_error() == 0
+
+
 @pytest.mark.parametrize("batch,q_len,past", [(1, 1, 513), (3, 1, 70), (2, 5, 300), (16, 5, 1000), (1, 8, 0)])
 def test_fused_attention_matches_two_kernel_path(batch, q_len, past):
     """ls_decode_attention_fused (q/k norm + RoPE + K/V append inside attention) against
