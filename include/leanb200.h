@@ -173,11 +173,14 @@ int ls_argmax_rows_workspace_bytes(int64_t m, int64_t n, int64_t* bytes);
 
 /*
  * GQA attention of q [m, Hq, D] over the cache (keys 0..cache_pos[b]+i for
- * token i of sequence b), split over the sequence on the tensor cores and
- * merged inside a thread-block cluster.  Covers decode (q_len 1, unmasked) and
- * verify (q_len k+1 with the decode mask of
- * src/leanstack/runtime/qwen_explicit.py:551-563).  Replaces the SDPA calls at
- * src/leanstack/runtime/qwen_explicit.py:886-903 and :1000-1039.
+ * token i of sequence b).  Below 256 query rows per (sequence, kv head) the
+ * keys are split over the sequence on the tensor cores and merged inside a
+ * thread-block cluster: decode (q_len 1, unmasked) and verify (q_len k+1 with
+ * the decode mask of src/leanstack/runtime/qwen_explicit.py:551-563).  From
+ * 256 rows (prefill, causal) a CTA owns 128 rows and walks the keys once with
+ * tcgen05 products (S and O in tensor memory).  Replaces the SDPA calls at
+ * src/leanstack/runtime/qwen_explicit.py:886-903 and :1000-1039.  Cache
+ * positions past cache_pos[b] + q_len are never read into the result.
  * workspace: ls_decode_attention_workspace_bytes() bytes (currently 0; the
  * argument is kept so that a caller's buffer plan stays valid).
  */
