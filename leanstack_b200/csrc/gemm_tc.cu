@@ -901,19 +901,6 @@ static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
   pl.kblocks = (int)((k + kTcBlockK - 1) / kTcBlockK);
   const int64_t units = (int64_t)pl.tiles * pl.kblocks;
   const int sms = sm_count();
-  pl.grid = (int)(units < sms ? units : sms);
-  // Fewer tiles than SMs: with the grid a multiple of the tile count, the even
-  // split of the unit list falls on tile boundaries, so every CTA holds a
-  // k-range of exactly one tile and reduces one share (split-K).  Taken when
-  // it keeps at least 90% of the SMs streaming (Qwen3-4B: QKV 48 tiles -> 144
-  // CTAs, o_proj / down 20 tiles -> 140).  Under full stream-K the CTAs that
-  // hold pieces of two split tiles reduce both, one after the other, and set
-  // the end of the kernel (measured tail after the last MMA: 8-11 us at M 8-80).
-  if (tc_tile_aligned_split() && pl.tiles < sms) {
-    const int per_tile = sms / pl.tiles < pl.kblocks ? sms / pl.tiles : pl.kblocks;
-    const int g = pl.tiles * per_tile;
-    if ((int64_t)g * 10 >= (int64_t)sms * 9) pl.grid = g;
-  }
   pl.stage_bytes = (int)(((size_t)kTcTileN * kTcBlockK * 2 * pl.accs + (size_t)pl.BN * kTcBlockK * 2 + 1023) / 1024 *
                          1024);
   int stages = (int)(((size_t)tc_stage_budget_kb() * 1024) / pl.stage_bytes);
@@ -927,6 +914,29 @@ static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
   while (cols < (uint32_t)(pl.acc_buffers * pl.BN * pl.accs)) cols <<= 1;
   pl.tmem_cols = cols;
   pl.smem = 1024 + (size_t)pl.stages * pl.stage_bytes + (size_t)(2 * pl.stages + 6) * 8 + 16;
+  pl.grid = (int)(units < sms ? units : sms);
+  // Fewer tiles than SMs: with the grid a multiple of the tile count, the even
+  // split of the unit list falls on tile boundaries, so every CTA holds a
+  // k-range of exactly one tile and reduces one share (split-K).  Taken when
+  // it keeps at least 90% of the SMs streaming (Qwen3-4B: QKV 48 tiles -> 144
+  // CTAs, o_proj / down 20 tiles -> 140), or with the next multiple when that
+  // is at most 5% above the SM count and two CTAs fit on one SM, so that the
+  // few SMs that run two CTAs need no second wave (gate_up, 76 pair tiles ->
+  // 152 CTAs at M <= 32: 28.4 -> 25.9 us at M 16; at M 80 the 126 KB ring
+  // does not fit twice and the extra CTAs ran as a second wave, 38% slower).
+  // Under full stream-K the CTAs that hold pieces of two split tiles reduce
+  // both, one after the other, and set the end of the kernel (measured tail
+  // after the last MMA: 8-11 us at M 8-80).
+  if (tc_tile_aligned_split() && pl.tiles < sms) {
+    const int per_tile = sms / pl.tiles < pl.kblocks ? sms / pl.tiles : pl.kblocks;
+    const int g = pl.tiles * per_tile;
+    const int g_up = pl.tiles * (per_tile + 1);
+    if (per_tile + 1 <= pl.kblocks && (int64_t)g_up * 100 <= (int64_t)sms * 105 &&
+        2 * (pl.smem + 1024) <= (size_t)228 * 1024)
+      pl.grid = g_up;
+    else if ((int64_t)g * 10 >= (int64_t)sms * 9)
+      pl.grid = g;
+  }
   pl.counter_bytes = kTcCounterBytes;
   pl.partial_bytes = (size_t)pl.grid * 2 * pl.accs * pl.BN * kTcTileN * 4;
   return pl;
