@@ -1,4 +1,7 @@
-// Causal GQA attention for long query blocks (prefill, config 5) on the tensor cores.
+// Causal GQA attention for long query blocks (prefill, config 5) on the legacy
+// mma.sync tensor path.  The default is the tcgen05 kernel in gemm_tc.cu
+// (prefill_attention_tc_kernel, 2.6x faster at config 5); this one is kept as
+// an option (LEANB200_PREFILL_ATTN=mma) and as its cross-check.
 //
 // Same contract as the split-KV kernel (attention_tc.cu): query row r =
 // (token i, group member g) of kv head h in sequence b sees keys

@@ -27,6 +27,9 @@
 // and rounds again; SILU_MUL pairs gate tile t with up tile t (two TMEM
 // accumulators) and rounds after the projection, after SiLU and after the
 // product.  Every mbarrier wait is bounded (LS_ERR_TIMEOUT).
+// The file also holds the large-M prefill GEMM (gemm_big_kernel) and the causal
+// prefill attention on tcgen05 (prefill_attention_tc_kernel), which share the
+// TMA, UMMA-descriptor and TMEM helpers below.
 #include <cuda.h>
 
 #include "common.cuh"
