@@ -66,7 +66,7 @@ def parse_args():
                     help="tensor-core (tcgen05) or CUDA-core streaming linears for the decode step")
     ap.add_argument("--parallel", choices=("tp", "replicas"), default="tp",
                     help="with N > 1 GPUs: tensor parallelism (one sequence) or independent replicas")
-    ap.add_argument("--batched", default="32",
+    ap.add_argument("--batched", default="8,32,64",
                     help="comma-separated batch sizes of the config-3 batched-decode section ('' to skip)")
     ap.add_argument("--batched-cached", type=int, default=2048, help="cached positions per sequence (config 3)")
     ap.add_argument("--batched-steps", type=int, default=128)
@@ -83,8 +83,9 @@ def measured_peaks() -> dict:
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 class ClockSampler:
@@ -177,11 +178,30 @@ def max_over_ranks(value: float, world: int) -> float:
 # CPU oracle (reference path restated) — the timed CPU baseline
 # ---------------------------------------------------------------------------
 
-def cpu_decode_rate(tensors_cpu: dict, budget_s: float, max_steps: int | None = None):
+def cpu_info(threads: int) -> dict:
+    """Host CPU model, the bf16 matrix/vector extensions it offers, and the threads used."""
+    model, flags = "unknown", set()
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name") and model == "unknown":
+                model = line.split(":", 1)[1].strip()
+            elif line.startswith("flags") and not flags:
+                flags = set(line.split(":", 1)[1].split())
+    except OSError:
+        pass
+    wanted = ("amx_bf16", "amx_tile", "avx512_bf16", "avx512f")
+    return {"model": model, "bf16_flags": [f for f in wanted if f in flags], "threads": threads,
+            "logical_cpus": os.cpu_count()}
+
+
+def cpu_decode_rate(tensors_cpu: dict, budget_s: float, min_steps: int = 1, warmup: int = 3):
     """Time full-model bs1 decode steps of the CPU oracle (bf16, all host cores).
 
-    The KV cache holds 512 seeded positions (a prefill on the CPU would take
-    minutes and is not part of the timed metric).  Returns (tok/s, steps, threads).
+    One model and KV cache serve the warm-up and the timed sample, and the
+    sample runs until both ``min_steps`` steps and ``budget_s`` seconds are done,
+    so every caller times the same steady state.  The KV cache holds 512
+    seeded positions (a prefill on the CPU would take minutes and is not part of
+    the timed metric).  Returns (tok/s, steps, threads, seconds).
     """
     from oracle import qwen_oracle as qo
 
@@ -197,8 +217,9 @@ def cpu_decode_rate(tensors_cpu: dict, budget_s: float, max_steps: int | None = 
     pc = m.rope(MAX_SEQ)
     tok = torch.tensor([[1]])
     with torch.inference_mode():
-        hidden = qo.stack_forward(m, qo.embed(m, tok), kv, pc)  # warm-up step
-        tok = qo.greedy_token(m, hidden).view(1, 1)
+        for _ in range(max(1, warmup)):
+            hidden = qo.stack_forward(m, qo.embed(m, tok), kv, pc)
+            tok = qo.greedy_token(m, hidden).view(1, 1)
         steps = 0
         t0 = time.perf_counter()
         while True:
@@ -206,9 +227,20 @@ def cpu_decode_rate(tensors_cpu: dict, budget_s: float, max_steps: int | None = 
             tok = qo.greedy_token(m, hidden).view(1, 1)
             steps += 1
             el = time.perf_counter() - t0
-            if (max_steps is not None and steps >= max_steps) or (max_steps is None and el >= budget_s):
+            if steps >= min_steps and el >= budget_s:
                 break
     return steps / el, steps, torch.get_num_threads(), el
+
+
+def cpu_sample_text(steps: int, el: float) -> str:
+    return (f"{steps} full-model bs1 decode steps ({el:.1f} s, after 3 warm-up steps) over a 512-position KV "
+            f"cache: CPU oracle (the reference's eager torch path restated), bf16")
+
+
+def bench_config() -> dict:
+    """The workload description both arms print (identical dicts)."""
+    return {"workload": WORKLOAD, "model": "Qwen3-4B (random init)", "global_batch": 1, "seq_len": PROMPT,
+            "max_seq": MAX_SEQ, "l2": "not flushed: each step streams 8.05 GB of weights (> 126 MB L2)"}
 
 
 def cpu_checkpoint():
@@ -224,18 +256,17 @@ def run_reference(args, world, rank):
         return 0
     tensors = cpu_checkpoint()
     torch.cuda.empty_cache() if torch.cuda.is_available() else None
-    # warm-up steps, then exactly `steps` timed steps (each a full decode token)
-    if args.warmup:
-        cpu_decode_rate(tensors, 0, max_steps=min(args.warmup, 3))
-    rate, steps, threads, el = cpu_decode_rate(tensors, 0, max_steps=args.steps)
+    # the same steady-state sample as the native arm's cpu_baseline: W warm-up
+    # steps, then at least K steps and at least --cpu-sample-seconds
+    rate, steps, threads, el = cpu_decode_rate(tensors, args.cpu_sample_seconds, min_steps=args.steps,
+                                               warmup=max(3, args.warmup))
     line = {
         "impl": "reference", "metric": METRIC, "value": rate, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": steps, "warmup": args.warmup, "ms_per_step": 1000.0 * el / steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights)",
-        "config": {"workload": WORKLOAD, "model": "Qwen3-4B (random init)", "global_batch": 1, "seq_len": PROMPT,
-                   "parallelism": "single process (CPU)", "l2": "n/a (CPU)"},
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights, uniform ids)",
+        "config": bench_config(),
         "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": f"{steps} full-model bs1 decode steps over a 512-position KV cache, torch CPU bf16"},
+                         "sample": cpu_sample_text(steps, el), "cpu": cpu_info(threads)},
         "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -263,6 +294,57 @@ def _timed(fn, steps: int, warmup: int, world: int) -> float:
     ms = e0.elapsed_time(e1)
     barrier(world)
     return max_over_ranks(ms, world) / 1000.0
+
+
+def run_layer_linears(rt, eng, peaks) -> dict:
+    """BASELINE config 1's per-linear figures: each decode linear at M = 1 (the
+    engine's CUDA-core kernels with their fused prologues / epilogues), timed
+    with CUDA events over launches that walk the 36 resident layers, so every
+    launch streams its own weights from HBM.  GB/s = (weight + input + output
+    bytes) / time."""
+    from leanstack_b200 import kernels as K
+
+    g = QWEN3_4B
+    a = eng.arenas
+    H, I, Q = g.hidden_size, eng.g.intermediate_size, eng.g.q_dim
+    qkv_out = torch.empty(1, eng.g.qkv_dim, device=rt.device, dtype=torch.bfloat16)
+    attn = torch.zeros(1, Q, device=rt.device, dtype=torch.bfloat16)
+    ws = torch.zeros(K.lmhead_workspace_bytes(1, eng.vocab_rows), device=rt.device, dtype=torch.uint8)
+    ids = torch.empty(1, device=rt.device, dtype=torch.int64)
+    cases = {
+        "qkv (input norm + QKV)": (lambda L: K.linear(a.h[:1], L.attention.qkv_proj_weight,
+                                                      norm_w=L.input_layernorm_weight, eps=g.rms_norm_eps,
+                                                      out=qkv_out),
+                                   eng.g.qkv_dim * H * 2 + H * 2 + eng.g.qkv_dim * 2, len(rt.layers)),
+        "o_proj + residual": (lambda L: K.oproj_residual(attn, L.attention.o_proj_weight, a.h[:1], out=a.x[:1]),
+                              H * Q * 2 + Q * 2 + 2 * H * 2, len(rt.layers)),
+        "gate_up + SiLU*up (post norm)": (lambda L: K.gateup_silu(a.h[:1], L.post_attention_layernorm_weight,
+                                                                   L.mlp.gate_up_proj_weight, g.rms_norm_eps,
+                                                                   out=a.act[:1]),
+                                          2 * I * H * 2 + H * 2 + I * 2, len(rt.layers)),
+        "down + residual": (lambda L: K.down_residual(a.act[:1], L.mlp.down_proj_weight, a.h[:1], out=a.x[:1]),
+                            H * I * 2 + I * 2 + 2 * H * 2, len(rt.layers)),
+        "lm_head + argmax (final norm)": (lambda L: K.lmhead_argmax(a.h[:1], rt.final_norm_weight, rt.lm_head_weight,
+                                                                     g.rms_norm_eps, out_ids=ids, workspace=ws),
+                                          eng.vocab_rows * H * 2 + H * 2 + 8, 1),
+    }
+    out = {}
+    for name, (fn, nbytes, n_layers) in cases.items():
+        reps = 4 if n_layers > 1 else 24
+        for L in rt.layers[:2]:
+            fn(L)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            for L in rt.layers[:n_layers]:
+                fn(L)
+        e1.record()
+        torch.cuda.synchronize()
+        per = e0.elapsed_time(e1) / 1000.0 / (reps * n_layers)
+        out[name] = {"us": per * 1e6, "bytes": nbytes, "gbs": nbytes / per / 1e9,
+                     "hbm_frac": nbytes / per / 1e9 / peaks["hbm_gbs"]}
+    return out
 
 
 def run_batched(rt, comm, shard, batch: int, cached: int, steps: int, warmup: int, world: int, peaks) -> dict:
@@ -314,7 +396,8 @@ def run_prefill(rt, comm, shard, batch: int, plen: int, decode_steps: int, world
     flops = 2.0 * batch * plen * lin_params * g.num_hidden_layers * world  # whole job (all ranks)
     out = {"batch": batch, "prompt_len": plen, "m": batch * plen, "prefill_s": t,
            "prefill_tok_per_s": batch * plen / t, "linear_tflops": flops / t / 1e12,
-           "linear_tensor_frac_per_gpu": flops / world / t / 1e12 / peaks.get("bf16_tflops", 1663.3),
+           "linear_tensor_frac_per_gpu": flops / world / t / 1e12 / peaks["bf16_tflops_sustained"],
+           "tensor_peak": "bf16_tflops_sustained (a prefill pass runs for most of a second)",
            "decode_steps": decode_steps, "decode_tok_per_s": batch * decode_steps / td,
            "attention": "causal prefill attention on tcgen05 (prefill_attention_tc_kernel: S and O in TMEM)"}
     eng.graph = None
@@ -386,6 +469,60 @@ def run_verify(rt, comm, shard, steps: int, warmup: int, world: int, peaks) -> d
     del eng
     torch.cuda.empty_cache()
     return out
+
+def run_draft_cycle(rt, steps: int, warmup: int, world: int, peaks) -> dict:
+    """BASELINE config 4 with the draft model in the loop: a random-init
+    Qwen3-0.6B-geometry draft (28 layers, hidden 1024, 16 / 8 heads,
+    intermediate 3072) decoding 16 sequences over 1024 cached positions, and
+    whole speculative cycles (k = 4 draft steps, one M = 80 target verify, the
+    device accept; one CUDA-graph replay per cycle)."""
+    from leanstack_b200.config import QWEN3_06B_DRAFT
+    from leanstack_b200.engine import DecodeEngine
+    from leanstack_b200.leanserve import materialize_from_tensors
+    from leanstack_b200.speculative import SpeculativeDecoder
+
+    gd = QWEN3_06B_DRAFT
+    B, k, cached = 16, 4, 1024
+    rt_d = materialize_from_tensors(gd, synth.synth_checkpoint(gd, SEED, device=rt.device), device=rt.device,
+                                    free_source=True)
+    S = cached + (warmup + steps + 2) * (k + 1) + 16
+    prompt = synth.token_ids((B, cached), gd.vocab_size, SEED, "cfg4d/prompt")
+    # the draft alone: bs16 greedy decode
+    drf = DecodeEngine(rt_d, batch_size=B, max_seq_len=S, linear_backend="tc")
+    drf.prefill_full(prompt)
+    drf.capture()
+    td = _timed(drf.decode_step, steps, warmup, world)
+    draft_bytes = gd.num_hidden_layers * gd.layer_weight_bytes() + gd.lm_head_bytes() + \
+        B * (cached + warmup + steps // 2) * gd.kv_bytes_per_token()
+    out = {"draft": "Qwen3-0.6B geometry (random init)", "batch": B, "cached_per_seq": cached,
+           "draft_decode_tok_per_s": B * steps / td, "draft_ms_per_step": 1000.0 * td / steps,
+           "draft_step_frac_of_hbm": draft_bytes / (td / steps) / 1e9 / peaks["hbm_gbs"]}
+    drf.graph = None
+    del drf
+    # whole cycles: draft proposes k, target verifies k + 1, device accept
+    tgt = DecodeEngine(rt, batch_size=B, max_seq_len=S, linear_backend="tc")
+    drf = DecodeEngine(rt_d, batch_size=B, max_seq_len=S, linear_backend="tc")
+    spec = SpeculativeDecoder(drf, tgt, k, (warmup + steps + 2) * (k + 1))
+    first = tgt.prefill_full(prompt)
+    drf.prefill_full(prompt)
+    tgt.next_ids.copy_(first)
+    spec.out_len.zero_()
+    tc = _timed(spec.cycle, steps, warmup, world)
+    committed = int(spec.out_len.sum().item())
+    spec.sync_cursors()
+    out.update({"proposal_len": k, "cycles": steps, "ms_per_cycle": 1000.0 * tc / steps,
+                "cycles_per_s": steps / tc,
+                "committed_tok_per_s_incl_warmup_cycles": committed / (tc * (steps + warmup) / steps),
+                "accepted_per_cycle": committed / (B * (steps + warmup)) - 1.0,
+                "proposals": "the draft's greedy tokens (two unrelated random-init models: acceptance ~0)"})
+    spec.graphs.clear()
+    for g_ in tgt.verify_graphs.values():
+        del g_
+    tgt.verify_graphs.clear()
+    del spec, tgt, drf, rt_d
+    torch.cuda.empty_cache()
+    return out
+
 
 def run_ours(args, world, rank, local):
     from leanstack_b200 import kernels as K
@@ -501,11 +638,15 @@ def run_ours(args, world, rank, local):
 
     # --- config 3 (batched decode) and config 4 (speculative verify) sections ---
     extra = {}
+    if not tp_mode and eng.backend != "tc":
+        extra["cfg1_linears_m1"] = run_layer_linears(rt, eng, peaks)
     for bs in [int(x) for x in args.batched.split(",") if x.strip()]:
         extra[f"bs{bs}"] = run_batched(rt, comm, shard, bs, args.batched_cached, args.batched_steps, 4, world,
                                        peaks)
     if not args.no_verify:
         extra["verify_cfg4"] = run_verify(rt, comm, shard, 64, 4, world, peaks)
+        if not tp_mode:
+            extra["draft_cycle_cfg4"] = run_draft_cycle(rt, 64, 4, world, peaks)
     if not args.no_prefill:
         extra["prefill_cfg5"] = run_prefill(rt, comm, shard, args.prefill_batch, args.prefill_len, 64, world, peaks)
 
@@ -516,8 +657,7 @@ def run_ours(args, world, rank, local):
         rate, steps, threads, el = cpu_decode_rate(tensors_cpu, args.cpu_sample_seconds)
         del tensors_cpu
         cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": f"{steps} full-model bs1 decode steps ({el:.1f} s) over a 512-position KV cache, "
-                         f"CPU oracle (reference eager torch path restated), bf16"}
+               "sample": cpu_sample_text(steps, el), "cpu": cpu_info(threads)}
 
     if rank == 0:
         line = {
@@ -525,12 +665,10 @@ def run_ours(args, world, rank, local):
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong" if tp_mode else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights, uniform ids)",
-            "config": {"workload": WORKLOAD, "model": "Qwen3-4B (random init)", "global_batch": seqs,
-                       "seq_len": PROMPT, "max_seq": MAX_SEQ,
-                       "parallelism": (f"tp{world}" + ("" if args.allreduce == "nccl" else " fused-allreduce")
-                                       if tp_mode else f"replicas x{world}") if world > 1
-                       else "single GPU", "l2": "not flushed: each step streams 8.05 GB of weights (> 126 MB L2)",
-                       "linear_backend": "persistent" if eng.persistent else eng.backend},
+            "config": {**bench_config(), "global_batch": seqs},
+            "parallelism": (f"tp{world}" + ("" if args.allreduce == "nccl" else " fused-allreduce")
+                            if tp_mode else f"replicas x{world}") if world > 1 else "single GPU",
+            "linear_backend": "persistent" if eng.persistent else eng.backend,
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
             "gpu_launches": args.steps * eng.kernel_launches_per_step(),
         }

@@ -80,8 +80,21 @@ int ls_version(void);
 const char* ls_last_error(void);
 
 /* Read (and optionally clear) the device-side error flag that kernels set when
- * they skip an out-of-range access.  Synchronizes the current device. */
+ * they skip an out-of-range access or a bounded wait runs out (LS_ERR_TIMEOUT
+ * in the low byte, the wait site above it).  Synchronizes the current device.
+ * No counterpart in the reference, whose eager torch path has no device-side
+ * waits; its nearest failure handling is the ValueError cursor checks of
+ * src/leanstack/runtime/kv_cache.py:100-103. */
 int ls_get_device_error(int* code, int clear);
+
+/* Limit, in ns, of every bounded spin-wait in the kernels (mbarrier waits,
+ * split-K counters, the fused all-reduce's peer wait, the persistent step's
+ * grid barrier) on the current device; 2 s by default, 1 us .. 60 s accepted.
+ * A wait that runs out records LS_ERR_TIMEOUT, the kernel drains and returns,
+ * and the context stays usable.  Synchronizes the device first.  For failure
+ * tests and for callers that must learn of a lost peer sooner. */
+int ls_set_wait_limit_ns(int64_t ns);
+int ls_get_wait_limit_ns(int64_t* ns);
 
 /* Number of SMs of the current device (grid sizing is a multiple of it). */
 int ls_sm_count(int* out);
@@ -188,18 +201,6 @@ int ls_decode_attention(const void* q, const void* k_cache, const void* v_cache,
                         int64_t uniform_past, int64_t batch, int64_t q_len, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
                         int64_t max_seq, float scale, void* out, void* workspace, int64_t workspace_bytes,
                         ls_stream_t stream);
-/* Decode / verify attention with the q/k RMSNorm, RoPE and K/V append of
- * ls_qk_norm_rope_kvappend folded in (one launch instead of two): reads the
- * raw fused-QKV rows qkv [batch * q_len, (Hq + 2 Hkv) * 128], normalises and
- * rotates q in registers, and the CTAs that stream a new position write its
- * K/V into the cache first.  Same rounding as the two-kernel form
- * (qwen_explicit.py:733-806, :886-903, :1000-1039).  Up to 16 * 65535 query
- * rows per kv head. */
-int ls_decode_attention_fused(const void* qkv, int64_t batch, int64_t q_len, int64_t num_heads,
-                              int64_t num_kv_heads, int64_t head_dim, const void* q_norm_w, const void* k_norm_w,
-                              float eps, const void* rope_cos, const void* rope_sin, int64_t rope_len,
-                              int64_t rope_offset, const int32_t* cache_pos, int64_t uniform_past, void* k_cache,
-                              void* v_cache, int64_t max_seq, float scale, void* out, ls_stream_t stream);
 int ls_decode_attention_workspace_bytes(int64_t batch, int64_t q_len, int64_t num_heads, int64_t num_kv_heads,
                                         int64_t head_dim, int64_t max_seq, int64_t* bytes);
 
@@ -235,10 +236,12 @@ int ls_lmhead_workspace_bytes(int64_t m, int64_t vocab, int64_t* bytes);
  * the token-selection path (an FFI host with no device allocator of its own, or
  * a server whose HBM plan is fixed at start-up).  Its scratch is a fixed 16 KiB
  * array per device inside this library; a call that would need more (m rows x
- * head-grid CTAs) fails with LS_ERR_WORKSPACE.  The first call on a device does
- * set-up (address lookup, counter cleared on `stream`): make it before any
- * stream capture.  Calls that overlap on the GPU share the scratch and race:
- * serialise them on one stream. */
+ * head-grid CTAs) fails with LS_ERR_WORKSPACE.  Every call looks up the
+ * array's device address (host-side, no allocation); the first call that sees
+ * an address on a device clears the arrival counter and waits for that on
+ * `stream`: make it before any stream capture and let it finish before other
+ * calls on the device start.  Calls that overlap on the GPU share the scratch
+ * and race: serialise them on one stream. */
 int ls_lmhead_argmax_noalloc(const void* h, int64_t m, int64_t hidden, const void* final_norm_w, float eps,
                              const void* lm_head_w, int64_t vocab, int64_t* out_ids, ls_stream_t stream);
 
@@ -315,27 +318,6 @@ int ls_ipc_open(const void* handle64, void** region);
 int ls_ipc_close(void* region);
 int ls_linear_allreduce_residual(const void* x, int64_t m, int64_t k, const void* w, int64_t n,
                                  const void* residual, void* out, const ls_p2p_exchange* ex, ls_stream_t stream);
-/* Latency probe of the exchange: `iters` flag round trips between rank 0 and
- * rank 1 through two 4-byte words (my_flag in this rank's region, peer_flag in
- * the other's, both zero and unused by the all-reduce), one thread, bounded
- * waits.  times_dev (device, 2 x u64): total ns, and 1 if a wait gave up. */
-int ls_p2p_pingpong(void* my_flag, void* peer_flag, int rank, int iters, unsigned long long* times_dev,
-                    ls_stream_t stream);
-
-/* Skinny-M linears on the tensor cores over pre-tiled weights (mma.sync
- * m16n8k16 with the activations as A, 1 <= m <= 8).  Same contract as
- * ls_linear_bf16 (epilogues LS_EPI_STORE / RESIDUAL / SILU_MUL, optional
- * RMSNorm prologue; reference: qwen_explicit.py:913-949, :1247-1272) but the
- * weight is first rewritten once by ls_gemv_tile_weight into 512-byte tiles
- * of 8 rows x 32 k in MMA fragment order (for SILU_MUL, gate and up rows of
- * the same 8 outputs adjacent).  k must be a multiple of 32, n_rows of 8 (16
- * for SILU_MUL).  workspace: ls_gemv_workspace_bytes() bytes, zero-filled once
- * (the kernel leaves it zeroed).  Deterministic: no result depends on timing. */
-int ls_gemv_tile_weight(const void* w, int64_t n_rows, int64_t k, int silu, void* out, ls_stream_t stream);
-int ls_gemv_workspace_bytes(int64_t m, int64_t n_rows, int epilogue, int64_t* bytes);
-int ls_gemv_bf16(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w_tiled,
-                 int64_t n_rows, int epilogue, const void* residual, void* out, void* workspace,
-                 int64_t workspace_bytes, ls_stream_t stream);
 
 /* Tensor-parallel greedy head.  Each rank holds a vocab shard (rows
  * [vocab_offset, vocab_offset + vocab_rows) of lm_head) and writes, per row, an
@@ -354,23 +336,6 @@ int ls_argmax_keys_to_ids(const int64_t* keys, int64_t m, int64_t* out_ids, ls_s
 /* out = bf16(residual + bf16(y)) over n elements, y fp32: the residual epilogue
  * of o_proj / down applied after the tensor-parallel all-reduce of their
  * fp32 partials (src/leanstack/runtime/qwen_explicit.py:819-829, :1262). */
-/* Profiling hook of ls_decode_step: with a non-NULL device buffer of
- * (barriers per step) x grid x 2 u64, each barrier records every CTA's arrival
- * and release time (globaltimer ns).  NULL turns it off. */
-int ls_decode_step_set_trace(void* buffer);
-/* Profiling hook of ls_linear_bf16 and the fused head / all-reduce forms: with a
- * non-NULL device buffer of grid x 5 u64, every launch records per CTA the
- * globaltimer at start, after the PDL wait, after the activation prologue,
- * after the weight stream, and at the end.  NULL turns it off. */
-int ls_linear_set_trace(void* buffer);
-/* Profiling hook of ls_gemm_bf16_tcgen05(_tiled): with a non-NULL device buffer
- * of grid x 8 u64, each launch records per CTA the globaltimer at start, when
- * the first stage landed, after the last MMA issue, after the epilogue, and
- * for the first and the last split tile when its contributors were complete
- * and when this CTA's share was reduced (0 where there is none).  NULL turns
- * it off. */
-int ls_gemm_tc_set_trace(void* buffer);
-
 int ls_residual_add_f32(const void* residual, const float* y, int64_t n, void* out, ls_stream_t stream);
 
 /* Standalone RMSNorm over the last dim, bf16((x * rsqrt(mean(x^2) + eps)) * w),
@@ -397,6 +362,34 @@ int ls_advance_cursors(int32_t* cache_pos, const int32_t* delta, int64_t batch, 
 int ls_spec_accept(int64_t* ids, const int64_t* verdict, int64_t batch, int64_t k, int64_t* next_ids,
                    int32_t* accepted, int32_t* cache_pos, int32_t* draft_cache_pos, int64_t* out_tokens,
                    int32_t* out_len, int64_t out_cap, ls_stream_t stream);
+
+#ifdef LEANB200_PROFILING
+/* Measurement hooks, compiled only into a library built with
+ * -DLEANB200_PROFILING (python -m leanstack_b200.build --profiling); the
+ * release library exports none of them. */
+/* NVLink latency probe of the exchange: `iters` flag round trips between rank 0 and
+ * rank 1 through two 4-byte words (my_flag in this rank's region, peer_flag in
+ * the other's, both zero and unused by the all-reduce), one thread, bounded
+ * waits.  times_dev (device, 2 x u64): total ns, and 1 if a wait gave up. */
+int ls_p2p_pingpong(void* my_flag, void* peer_flag, int rank, int iters, unsigned long long* times_dev,
+                    ls_stream_t stream);
+/* Profiling hook of ls_decode_step: with a non-NULL device buffer of
+ * (barriers per step) x grid x 2 u64, each barrier records every CTA's arrival
+ * and release time (globaltimer ns).  NULL turns it off. */
+int ls_decode_step_set_trace(void* buffer);
+/* Profiling hook of ls_linear_bf16 and the fused head / all-reduce forms: with a
+ * non-NULL device buffer of grid x 5 u64, every launch records per CTA the
+ * globaltimer at start, after the PDL wait, after the activation prologue,
+ * after the weight stream, and at the end.  NULL turns it off. */
+int ls_linear_set_trace(void* buffer);
+/* Profiling hook of ls_gemm_bf16_tcgen05(_tiled): with a non-NULL device buffer
+ * of grid x 8 u64, each launch records per CTA the globaltimer at start, when
+ * the first stage landed, after the last MMA issue, after the epilogue, and
+ * for the first and the last split tile when its contributors were complete
+ * and when this CTA's share was reduced (0 where there is none).  NULL turns
+ * it off. */
+int ls_gemm_tc_set_trace(void* buffer);
+#endif /* LEANB200_PROFILING */
 
 #ifdef __cplusplus
 }

@@ -58,6 +58,8 @@ SIGNATURES: dict[str, list] = {
     "ls_version": [],
     "ls_last_error": [],
     "ls_get_device_error": [ctypes.POINTER(_int), _int],
+    "ls_set_wait_limit_ns": [_i64],
+    "ls_get_wait_limit_ns": [ctypes.POINTER(_i64)],
     "ls_sm_count": [ctypes.POINTER(_int)],
     "ls_embed_gather": [_p, _i64, _p, _i64, _i64, _p, _p],
     "ls_linear_bf16": [_p, _i64, _i64, _p, _f32, _p, _i64, _int, _p, _p, _p],
@@ -73,19 +75,11 @@ SIGNATURES: dict[str, list] = {
     "ls_lmhead_workspace_bytes": [_i64, _i64, ctypes.POINTER(_i64)],
     "ls_rmsnorm": [_p, _i64, _i64, _p, _f32, _p, _p],
     "ls_residual_add_f32": [_p, _p, _i64, _p, _p],
-    "ls_decode_step_set_trace": [_p],
-    "ls_linear_set_trace": [_p],
-    "ls_gemm_tc_set_trace": [_p],
     "ls_spec_accept": [_p, _p, _i64, _i64, _p, _p, _p, _p, _p, _p, _i64, _p],
     "ls_gemm_bf16_tcgen05_big": [_p, _i64, _i64, _p, _i64, ctypes.c_int, _p, _p, _p],
-    "ls_decode_attention_fused": [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _f32, _p, _p, _i64, _i64, _p, _i64, _p,
-                                  _p, _i64, _f32, _p, _p],
     "ls_gemm_tc_tiled_bytes": [_i64, _i64, ctypes.c_int, _p],
     "ls_gemm_tc_tile_weight": [_p, _i64, _i64, ctypes.c_int, _p, _p],
     "ls_gemm_bf16_tcgen05_tiled": [_p, _i64, _i64, _p, _i64, ctypes.c_int, _p, _p, _p, _i64, _p],
-    "ls_gemv_tile_weight": [_p, _i64, _i64, ctypes.c_int, _p, _p],
-    "ls_gemv_workspace_bytes": [_i64, _i64, ctypes.c_int, _p],
-    "ls_gemv_bf16": [_p, _i64, _i64, _p, _f32, _p, _i64, ctypes.c_int, _p, _p, _p, _i64, _p],
     "ls_p2p_region_bytes": [_i64, _i64, _i64, _p],
     "ls_p2p_alloc": [_i64, _p],
     "ls_p2p_free": [_p],
@@ -93,7 +87,6 @@ SIGNATURES: dict[str, list] = {
     "ls_ipc_open": [_p, _p],
     "ls_ipc_close": [_p],
     "ls_linear_allreduce_residual": [_p, _i64, _i64, _p, _i64, _p, _p, _p, _p],
-    "ls_p2p_pingpong": [_p, _p, ctypes.c_int, ctypes.c_int, _p, _p],
     "ls_lmhead_argmax_keys": [_p, _i64, _i64, _p, _f32, _p, _i64, _i64, _p, _p, _i64, _p],
     "ls_argmax_rows_keys": [_p, _i64, _i64, _i64, _p, _p, _i64, _p],
     "ls_argmax_keys_to_ids": [_p, _i64, _p, _p],
@@ -109,6 +102,13 @@ SIGNATURES: dict[str, list] = {
     "ls_advance_cursors": [_p, _p, _i64, _i64, _p],
 }
 _RESTYPES = {"ls_last_error": ctypes.c_char_p}
+# Measurement hooks, present only in a library built with --profiling (LEANB200_PROFILING).
+PROFILING_SIGNATURES: dict[str, list] = {
+    "ls_decode_step_set_trace": [_p],
+    "ls_linear_set_trace": [_p],
+    "ls_gemm_tc_set_trace": [_p],
+    "ls_p2p_pingpong": [_p, _p, ctypes.c_int, ctypes.c_int, _p, _p],
+}
 
 _LIB: ctypes.CDLL | None = None
 
@@ -128,6 +128,11 @@ def load() -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.argtypes = argtypes
         fn.restype = _RESTYPES.get(name, ctypes.c_int)
+    for name, argtypes in PROFILING_SIGNATURES.items():
+        fn = getattr(lib, name, None)
+        if fn is not None:
+            fn.argtypes = argtypes
+            fn.restype = ctypes.c_int
     _LIB = lib
     return lib
 

@@ -1,7 +1,10 @@
 """Build libleanb200.so in-tree with nvcc for sm_100a.
 
-``python -m leanstack_b200.build [--force] [--verbose]`` compiles every
-``csrc/*.cu`` into ``leanstack_b200/_lib/libleanb200.so``.  The library links
+``python -m leanstack_b200.build [--force] [--verbose] [--profiling]`` compiles
+every ``csrc/*.cu`` into ``leanstack_b200/_lib/libleanb200.so``.
+``--profiling`` defines ``LEANB200_PROFILING``, which adds the measurement
+hooks (per-CTA timestamp buffers, the NVLink ping-pong probe) to the library;
+the default build has none of them.  The library links
 the shared CUDA runtime (``libcudart.so.12``), so inside a PyTorch process it
 binds to the runtime PyTorch already loaded and sees the same current device
 and streams.  No GPU is needed to build.
@@ -48,9 +51,13 @@ def _deps() -> list[Path]:
     return sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
 
 
-def _compile(src: Path, verbose: bool, ptxas_verbose: bool) -> tuple[Path, str]:
+STAMP = OUT_DIR / "build_flags.txt"
+
+
+def _compile(src: Path, verbose: bool, ptxas_verbose: bool, defines: list[str]) -> tuple[Path, str]:
     obj = OBJ_DIR / (src.stem + ".o")
-    cmd = [nvcc_path(), *ARCH_FLAGS, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-c", str(src), "-o", str(obj)]
+    cmd = [nvcc_path(), *ARCH_FLAGS, *NVCC_FLAGS, *defines, "-I", str(INCLUDE), "-I", str(CSRC), "-c", str(src),
+           "-o", str(obj)]
     if ptxas_verbose:
         cmd += ["-Xptxas", "-v"]
     if verbose:
@@ -61,21 +68,27 @@ def _compile(src: Path, verbose: bool, ptxas_verbose: bool) -> tuple[Path, str]:
     return obj, res.stderr
 
 
-def needs_build() -> bool:
+def needs_build(defines: list[str] | None = None) -> bool:
     if not LIB.exists():
+        return True
+    if not STAMP.exists() or STAMP.read_text().split() != (defines or []):
         return True
     lib_mtime = LIB.stat().st_mtime
     return any(p.stat().st_mtime > lib_mtime for p in [*sources(), *_deps(), Path(__file__)])
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> Path:
-    if not force and not needs_build():
+def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False, profiling: bool = False) -> Path:
+    defines = ["-DLEANB200_PROFILING"] if profiling else []
+    if not force and not needs_build(defines):
         return LIB
     OUT_DIR.mkdir(parents=True, exist_ok=True)
     OBJ_DIR.mkdir(parents=True, exist_ok=True)
+    for stale in OBJ_DIR.glob("*.o"):  # objects of sources that no longer exist must not be linked
+        if not (CSRC / (stale.stem + ".cu")).exists():
+            stale.unlink()
     srcs = sources()
     with cf.ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 4)) as ex:
-        results = list(ex.map(lambda s: _compile(s, verbose, ptxas_verbose), srcs))
+        results = list(ex.map(lambda s: _compile(s, verbose, ptxas_verbose, defines), srcs))
     if ptxas_verbose:
         for _, log in results:
             if log.strip():
@@ -90,6 +103,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
     os.replace(tmp, LIB)
+    STAMP.write_text(" ".join(defines) + "\n")
     return LIB
 
 
@@ -98,8 +112,9 @@ def main(argv=None) -> int:
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas-verbose", action="store_true", help="print registers / spills per kernel")
+    ap.add_argument("--profiling", action="store_true", help="add the measurement hooks (LEANB200_PROFILING)")
     args = ap.parse_args(argv)
-    lib = build(force=args.force, verbose=args.verbose, ptxas_verbose=args.ptxas_verbose)
+    lib = build(force=args.force, verbose=args.verbose, ptxas_verbose=args.ptxas_verbose, profiling=args.profiling)
     print(lib)
     return 0
 

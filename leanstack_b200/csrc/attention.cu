@@ -115,7 +115,7 @@ static cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStr
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 1;
   return cfg;
 }
 
@@ -159,23 +159,16 @@ int attention_workspace_bytes(int64_t batch, int64_t q_len, int64_t hq, int64_t 
   return LS_OK;
 }
 
-struct TaFused;
 int launch_decode_attention_tc(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
                                int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv,
-                               int64_t max_seq, float scale, void* out, cudaStream_t stream,
-                               const TaFused* fused = nullptr);
-
-int launch_prefill_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
-                             int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv,
-                             int64_t max_seq, float scale, void* out, cudaStream_t stream);
+                               int64_t max_seq, float scale, void* out, cudaStream_t stream);
 
 int launch_prefill_attention_tc(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
                                 int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv,
                                 int64_t max_seq, float scale, void* out, cudaStream_t stream);
-bool prefill_attention_tc_enabled();
 
-// Query rows per (sequence, kv head) from which the 128-row prefill kernels
-// (one pass over the keys per 128 rows) replace the split-KV kernel.
+// Query rows per (sequence, kv head) from which the 128-row tcgen05 prefill
+// kernel (one pass over the keys per 128 rows) replaces the split-KV kernel.
 constexpr int64_t kPrefillRows = 256;
 
 int launch_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
@@ -184,13 +177,9 @@ int launch_decode_attention(const void* q, const void* k_cache, const void* v_ca
                             cudaStream_t stream) {
   (void)workspace;
   (void)workspace_bytes;
-  if (q_len * (hq / hkv) >= kPrefillRows) {
-    if (prefill_attention_tc_enabled())
-      return launch_prefill_attention_tc(q, k_cache, v_cache, cache_pos, uniform_past, batch, q_len, hq, hkv,
-                                         max_seq, scale, out, stream);
-    return launch_prefill_attention(q, k_cache, v_cache, cache_pos, uniform_past, batch, q_len, hq, hkv, max_seq,
-                                    scale, out, stream);
-  }
+  if (q_len * (hq / hkv) >= kPrefillRows)
+    return launch_prefill_attention_tc(q, k_cache, v_cache, cache_pos, uniform_past, batch, q_len, hq, hkv, max_seq,
+                                       scale, out, stream);
   return launch_decode_attention_tc(q, k_cache, v_cache, cache_pos, uniform_past, batch, q_len, hq, hkv, max_seq,
                                     scale, out, stream);
 }

@@ -52,15 +52,6 @@ struct TaParams {
   int* err;
   int q_len, Hq, Hkv, G, R, RG, splits, max_seq;
   float scale_log2;
-  // Fused prologue (qkv != null): q/k RMSNorm + RoPE from the raw QKV rows and
-  // the K/V append of the step's new positions, instead of reading q.
-  const __nv_bfloat16* qkv;      // [M, (Hq + 2 Hkv) D]
-  const __nv_bfloat16* q_norm_w; // [D]
-  const __nv_bfloat16* k_norm_w;
-  const __nv_bfloat16* cos;      // [rope_len, D/2]
-  const __nv_bfloat16* sin;
-  int rope_len, rope_offset;
-  float eps;
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
@@ -188,73 +179,14 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
     const int i = valid ? row / p.G : 0;
     const int gq = valid ? row - i * p.G : 0;
     lim[hr] = valid ? cp + i : -1;
-    if (!p.qkv) {
-      const __nv_bfloat16* qp = p.q + ((size_t)(b * p.q_len + i) * p.Hq + hkv * p.G + gq) * kTaHeadDim;
+    const __nv_bfloat16* qp = p.q + ((size_t)(b * p.q_len + i) * p.Hq + hkv * p.G + gq) * kTaHeadDim;
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        qa[ks][hr] = valid ? *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 2 * t4) : 0u;
-        qa[ks][2 + hr] = valid ? *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 8 + 2 * t4) : 0u;
-      }
-    } else {
-      // The lane holds dims {16 ks + 2 t4, +1, 16 ks + 8 + 2 t4, +1} of its row for
-      // ks 0..7: the quad (t4 = 0..3) covers the head, and dims d and d + 64 sit
-      // in the same lane (ks and ks + 4), so RMSNorm needs two shuffles and RoPE none.
-      // Rounding as ls_qk_norm_rope_kvappend: n = bf16((x r) w); bf16(bf16(n c) -+ bf16(n' s)).
-      const int qkv_dim = (p.Hq + 2 * p.Hkv) * kTaHeadDim;
-      const __nv_bfloat16* src = p.qkv + (size_t)(b * p.q_len + i) * qkv_dim + (size_t)(hkv * p.G + gq) * kTaHeadDim;
-      float x[8][4];
-      float ss = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(src + ks * 16 + 2 * t4);
-        const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(src + ks * 16 + 8 + 2 * t4);
-        x[ks][0] = __low2float(lo);
-        x[ks][1] = __high2float(lo);
-        x[ks][2] = __low2float(hi);
-        x[ks][3] = __high2float(hi);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) ss = fmaf(x[ks][e], x[ks][e], ss);
-      }
-      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-      const float r = rsqrtf(ss / (float)kTaHeadDim + p.eps);
-      const int trow = cp + i - p.rope_offset;
-      const bool rope_ok = valid && trow >= 0 && trow < p.rope_len;
-      const __nv_bfloat16* cr = p.cos + (size_t)(rope_ok ? trow : 0) * (kTaHeadDim / 2);
-      const __nv_bfloat16* sr = p.sin + (size_t)(rope_ok ? trow : 0) * (kTaHeadDim / 2);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const int d0 = ks * 16 + 2 * t4;
-        const int dd[4] = {d0, d0 + 1, d0 + 8, d0 + 9};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) x[ks][e] = round_bf16((x[ks][e] * r) * bf16_to_f(p.q_norm_w[dd[e]]));
-      }
-      float y[8][4];
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const int d0 = ks * 16 + 2 * t4;
-        const int dd[4] = {d0, d0 + 1, d0 + 8, d0 + 9};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float c = bf16_to_f(cr[dd[e]]), sn = bf16_to_f(sr[dd[e]]);
-          const float a = x[ks][e], a2 = x[ks + 4][e];  // dims d and d + 64
-          y[ks][e] = round_bf16(round_bf16(a * c) - round_bf16(a2 * sn));
-          y[ks + 4][e] = round_bf16(round_bf16(a2 * c) + round_bf16(a * sn));
-        }
-      }
-      if (valid && !rope_ok && t4 == 0 && s == 0) raise_device_error(p.err, LS_ERR_KV_OVERFLOW);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const __nv_bfloat162 lo = __floats2bfloat162_rn(y[ks][0], y[ks][1]);
-        const __nv_bfloat162 hi = __floats2bfloat162_rn(y[ks][2], y[ks][3]);
-        qa[ks][hr] = valid ? *reinterpret_cast<const uint32_t*>(&lo) : 0u;
-        qa[ks][2 + hr] = valid ? *reinterpret_cast<const uint32_t*>(&hi) : 0u;
-      }
+    for (int ks = 0; ks < 8; ++ks) {
+      qa[ks][hr] = valid ? *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 2 * t4) : 0u;
+      qa[ks][2 + hr] = valid ? *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 8 + 2 * t4) : 0u;
     }
   }
 
-
-  const int qkv_dim = (p.Hq + 2 * p.Hkv) * kTaHeadDim;
   for (int n = 0; n < nb; ++n) {
     cp_async_wait<kTaStages - 1>();
     __syncwarp();
@@ -262,52 +194,6 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
     const uint32_t stK = ring + stage * kTaStageBytes;
     const uint32_t stV = stK + kTaTileBytes;
     const int jb = (blk0 + warp + n * kTaWarps) * kTaKeys;
-
-    if (p.qkv && jb + kTaKeys > cp && jb < cp + p.q_len) {
-      // This block holds positions of the step's new tokens: the tile read stale
-      // cache rows there.  Build each new key (k RMSNorm + RoPE, raw v), patch it
-      // into the tile and append it to the cache (CTAs of other row groups
-      // write the same bytes).  Rounding as ls_qk_norm_rope_kvappend.
-      const int e0 = lane * 4;
-      for (int j = max(jb, cp); j < min(jb + kTaKeys, min(cp + p.q_len, L)); ++j) {
-        const int i = j - cp;
-        const __nv_bfloat16* src =
-            p.qkv + (size_t)(b * p.q_len + i) * qkv_dim + (size_t)(p.Hq + hkv) * kTaHeadDim;
-        const uint2 raw_u = *reinterpret_cast<const uint2*>(src + e0);
-        const uint2 v_u = *reinterpret_cast<const uint2*>(src + (size_t)p.Hkv * kTaHeadDim + e0);
-        float raw[4] = {bf16_lo(raw_u.x), bf16_hi(raw_u.x), bf16_lo(raw_u.y), bf16_hi(raw_u.y)};
-        float ss = raw[0] * raw[0] + raw[1] * raw[1] + raw[2] * raw[2] + raw[3] * raw[3];
-        ss = warp_sum(ss);
-        const float r = rsqrtf(ss / (float)kTaHeadDim + p.eps);
-        float nk[4], other[4], o4[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) nk[e] = round_bf16((raw[e] * r) * bf16_to_f(p.k_norm_w[e0 + e]));
-#pragma unroll
-        for (int e = 0; e < 4; ++e) other[e] = __shfl_xor_sync(0xffffffffu, nk[e], 16);
-        const bool first_half = lane < 16;
-        const int idx = first_half ? e0 : e0 - kTaHeadDim / 2;
-        const int trow = min(max(j - p.rope_offset, 0), p.rope_len - 1);
-        if (lane == 0 && (j - p.rope_offset < 0 || j - p.rope_offset >= p.rope_len))
-          raise_device_error(p.err, LS_ERR_KV_OVERFLOW);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float c = bf16_to_f(p.cos[(size_t)trow * (kTaHeadDim / 2) + idx + e]);
-          const float sn = bf16_to_f(p.sin[(size_t)trow * (kTaHeadDim / 2) + idx + e]);
-          o4[e] = first_half ? round_bf16(round_bf16(nk[e] * c) - round_bf16(other[e] * sn))
-                             : round_bf16(round_bf16(nk[e] * c) + round_bf16(other[e] * sn));
-        }
-        const __nv_bfloat162 lo2 = __floats2bfloat162_rn(o4[0], o4[1]);
-        const __nv_bfloat162 hi2 = __floats2bfloat162_rn(o4[2], o4[3]);
-        const uint2 k_u = make_uint2(*reinterpret_cast<const uint32_t*>(&lo2), *reinterpret_cast<const uint32_t*>(&hi2));
-        const size_t off = (size_t)j * kTaHeadDim + e0;
-        *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(kbase) + off) = k_u;
-        *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(vbase) + off) = v_u;
-        const uint32_t so = ta_swz(j - jb, lane >> 1) + (lane & 1) * 8;  // 4 dims = 8 bytes of chunk lane/2
-        asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(stK + so), "r"(k_u.x), "r"(k_u.y) : "memory");
-        asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(stV + so), "r"(v_u.x), "r"(v_u.y) : "memory");
-      }
-      __syncwarp();
-    }
 
     // S = Q K^T for 16 keys (two n-tiles of 8 keys).
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -473,16 +359,6 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
 namespace lsb_host {
 using namespace lsb;
 
-struct TaFused {
-  const void* qkv;
-  const void* q_norm_w;
-  const void* k_norm_w;
-  const void* cos;
-  const void* sin;
-  int64_t rope_len, rope_offset;
-  float eps;
-};
-
 struct TaPlan {
   int G, R, RG, splits;
 };
@@ -507,8 +383,7 @@ static TaPlan ta_plan(int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int
 
 int launch_decode_attention_tc(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
                                int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv,
-                               int64_t max_seq, float scale, void* out, cudaStream_t stream,
-                               const TaFused* fused = nullptr) {
+                               int64_t max_seq, float scale, void* out, cudaStream_t stream) {
   const TaPlan pl = ta_plan(batch, q_len, hq, hkv, max_seq);
   if ((int64_t)hkv * pl.RG > 65535)
     return set_error(LS_ERR_UNSUPPORTED_SHAPE, "decode_attention: %lld kv heads x %d row groups exceed the grid",
@@ -530,16 +405,6 @@ int launch_decode_attention_tc(const void* q, const void* k_cache, const void* v
   p.max_seq = (int)max_seq;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = device_error_ptr();
-  if (fused) {
-    p.qkv = static_cast<const __nv_bfloat16*>(fused->qkv);
-    p.q_norm_w = static_cast<const __nv_bfloat16*>(fused->q_norm_w);
-    p.k_norm_w = static_cast<const __nv_bfloat16*>(fused->k_norm_w);
-    p.cos = static_cast<const __nv_bfloat16*>(fused->cos);
-    p.sin = static_cast<const __nv_bfloat16*>(fused->sin);
-    p.rope_len = (int)fused->rope_len;
-    p.rope_offset = (int)fused->rope_offset;
-    p.eps = fused->eps;
-  }
   static bool attrs_set = false;
   if (!attrs_set) {
     cudaError_t e = cudaFuncSetAttribute(decode_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -561,7 +426,7 @@ int launch_decode_attention_tc(const void* q, const void* k_cache, const void* v
   attr[na].val.clusterDim.y = 1;
   attr[na].val.clusterDim.z = 1;
   ++na;
-  if (pdl_enabled()) {
+  {
     attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
@@ -571,17 +436,6 @@ int launch_decode_attention_tc(const void* q, const void* k_cache, const void* v
   cudaError_t e = cudaLaunchKernelEx(&cfg, decode_attention_tc_kernel, p);
   if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "decode_attention_tc launch: %s", cudaGetErrorString(e));
   return LS_OK;
-}
-
-int launch_decode_attention_fused(const void* qkv, const void* q_norm_w, const void* k_norm_w, float eps,
-                                  const void* cos, const void* sin, int64_t rope_len, int64_t rope_offset,
-                                  void* k_cache, void* v_cache, const int32_t* cache_pos, int64_t uniform_past,
-                                  int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int64_t max_seq,
-                                  float scale, void* out, cudaStream_t stream) {
-  if (q_len * (hq / hkv) > 16 * 65535) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "fused attention: too many rows");
-  TaFused f = {qkv, q_norm_w, k_norm_w, cos, sin, rope_len, rope_offset, eps};
-  return launch_decode_attention_tc(nullptr, k_cache, v_cache, cache_pos, uniform_past, batch, q_len, hq, hkv,
-                                    max_seq, scale, out, stream, &f);
 }
 
 }  // namespace lsb_host

@@ -2,6 +2,7 @@
 // glue kernels (embedding gather, cursor advance).  The heavy kernels live in
 // linear_small_m.cu and attention.cu.
 #include <cstdarg>
+#include <cstddef>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -10,7 +11,9 @@
 #include "common.cuh"
 
 namespace lsb {
-__device__ int g_device_error = 0;
+// The device status block: the error flag kernels raise, and the limit of
+// their bounded waits (ls_set_wait_limit_ns).  Kernels receive &error.
+__device__ DeviceStatus g_device_status = {0, 0, kDefaultWaitNs};
 
 __global__ void embed_gather_kernel(const int64_t* ids, const __nv_bfloat16* embed, int64_t vocab, int hidden,
                                     __nv_bfloat16* out, int* err) {
@@ -230,18 +233,10 @@ int* device_error_ptr() {
   std::lock_guard<std::mutex> lock(mu);
   if (!cached[dev]) {
     void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, lsb::g_device_error) == cudaSuccess) cached[dev] = static_cast<int*>(ptr);
+    if (cudaGetSymbolAddress(&ptr, lsb::g_device_status) == cudaSuccess)
+      cached[dev] = &static_cast<lsb::DeviceStatus*>(ptr)->error;
   }
   return cached[dev];
-}
-
-bool pdl_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("LEANB200_PDL");
-    v = (e && e[0] == '0') ? 0 : 1;
-  }
-  return v == 1;
 }
 
 // Defined in the kernel translation units.
@@ -267,11 +262,6 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
                    void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream,
                    const void* w_tiled = nullptr);
 int64_t tc_tiled_bytes(int64_t n_out, int64_t k, int silu);
-int launch_decode_attention_fused(const void* qkv, const void* q_norm_w, const void* k_norm_w, float eps,
-                                  const void* cos, const void* sin, int64_t rope_len, int64_t rope_offset,
-                                  void* k_cache, void* v_cache, const int32_t* cache_pos, int64_t uniform_past,
-                                  int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int64_t max_seq,
-                                  float scale, void* out, cudaStream_t stream);
 int launch_gemm_big(const void* x, int64_t m, int64_t k, const void* w, int64_t n_out, int epi, const void* residual,
                     void* out, cudaStream_t stream);
 int launch_tc_tile(const void* w, int64_t n_rows, int64_t k, int silu, void* out, cudaStream_t stream);
@@ -309,14 +299,35 @@ int ls_get_device_error(int* code, int clear) {
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "device synchronize: %s", cudaGetErrorString(e));
   int v = 0;
-  e = cudaMemcpyFromSymbol(&v, lsb::g_device_error, sizeof(int));
+  e = cudaMemcpyFromSymbol(&v, lsb::g_device_status, sizeof(int), offsetof(lsb::DeviceStatus, error));
   if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "read device error: %s", cudaGetErrorString(e));
   *code = v;
   if (clear && v) {
     int zero = 0;
-    e = cudaMemcpyToSymbol(lsb::g_device_error, &zero, sizeof(int));
+    e = cudaMemcpyToSymbol(lsb::g_device_status, &zero, sizeof(int), offsetof(lsb::DeviceStatus, error));
     if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "clear device error: %s", cudaGetErrorString(e));
   }
+  return LS_OK;
+}
+
+int ls_set_wait_limit_ns(int64_t ns) {
+  LS_REQUIRE(ns >= 1000 && ns <= 60ll * 1000000000ll, LS_ERR_INVALID_ARGUMENT,
+             "ls_set_wait_limit_ns: %lld ns outside [1 us, 60 s]", (long long)ns);
+  cudaError_t e = cudaDeviceSynchronize();  // no kernel of the old limit still waiting
+  const unsigned long long v = (unsigned long long)ns;
+  if (e == cudaSuccess)
+    e = cudaMemcpyToSymbol(lsb::g_device_status, &v, sizeof(v), offsetof(lsb::DeviceStatus, wait_limit_ns));
+  if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "ls_set_wait_limit_ns: %s", cudaGetErrorString(e));
+  return LS_OK;
+}
+
+int ls_get_wait_limit_ns(int64_t* ns) {
+  LS_REQUIRE(ns, LS_ERR_INVALID_ARGUMENT, "ls_get_wait_limit_ns: ns is null");
+  unsigned long long v = 0;
+  cudaError_t e =
+      cudaMemcpyFromSymbol(&v, lsb::g_device_status, sizeof(v), offsetof(lsb::DeviceStatus, wait_limit_ns));
+  if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "ls_get_wait_limit_ns: %s", cudaGetErrorString(e));
+  *ns = (int64_t)v;
   return LS_OK;
 }
 
@@ -471,27 +482,6 @@ int ls_gemm_bf16_tcgen05(const void* x, int64_t m, int64_t k, const void* w, int
   LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32,
              LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d", epilogue);
   return launch_gemm_tc(x, m, k, w, n, epilogue, residual, out, workspace, workspace_bytes, (cudaStream_t)stream);
-}
-
-int ls_decode_attention_fused(const void* qkv, int64_t batch, int64_t q_len, int64_t num_heads,
-                              int64_t num_kv_heads, int64_t head_dim, const void* q_norm_w, const void* k_norm_w,
-                              float eps, const void* rope_cos, const void* rope_sin, int64_t rope_len,
-                              int64_t rope_offset, const int32_t* cache_pos, int64_t uniform_past, void* k_cache,
-                              void* v_cache, int64_t max_seq, float scale, void* out, ls_stream_t stream) {
-  LS_REQUIRE(qkv && q_norm_w && k_norm_w && rope_cos && rope_sin && k_cache && v_cache && out,
-             LS_ERR_INVALID_ARGUMENT, "ls_decode_attention_fused: null pointer");
-  LS_REQUIRE(head_dim == 128, LS_ERR_UNSUPPORTED_SHAPE, "head_dim=%lld (only 128 is implemented)",
-             (long long)head_dim);
-  LS_REQUIRE(batch > 0 && batch <= 65535 && q_len > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0 &&
-                 max_seq > 0 && rope_len > 0 && rope_offset >= 0,
-             LS_ERR_INVALID_ARGUMENT, "ls_decode_attention_fused: bad sizes");
-  LS_REQUIRE(cache_pos || (uniform_past >= 0 && uniform_past + q_len <= max_seq), LS_ERR_KV_OVERFLOW,
-             "ls_decode_attention_fused: uniform_past + q_len beyond max_seq");
-  LS_REQUIRE(aligned16(qkv) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out), LS_ERR_MISALIGNED,
-             "ls_decode_attention_fused: pointers must be 16-byte aligned");
-  return launch_decode_attention_fused(qkv, q_norm_w, k_norm_w, eps, rope_cos, rope_sin, rope_len, rope_offset,
-                                       k_cache, v_cache, cache_pos, uniform_past, batch, q_len, num_heads,
-                                       num_kv_heads, max_seq, scale, out, (cudaStream_t)stream);
 }
 
 int ls_gemm_bf16_tcgen05_big(const void* x, int64_t m, int64_t k, const void* w, int64_t n, int epilogue,
@@ -674,7 +664,7 @@ int ls_rmsnorm(const void* x, int64_t m, int64_t n, const void* w, float eps, vo
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, lsb::rmsnorm_kernel, static_cast<const __nv_bfloat16*>(x), (int)n,
                                      static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(out), vec);
   return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "rmsnorm launch: %s", cudaGetErrorString(e));

@@ -93,11 +93,34 @@ __device__ __forceinline__ void raise_device_error(int* flag, int code) {
 }
 
 // ---------------------------------------------------------------------------
-// mbarrier + bulk-copy (TMA, non-tensor) helpers.  Every wait is bounded: it
-// gives up after kWaitCycles (about two seconds at the boost clock), records
-// LS_ERR_TIMEOUT and reports failure so the kernel can drain and return.
+// Bounded waits.  Every spin in the kernels gives up after the device's wait
+// limit (2 s unless ls_set_wait_limit_ns changed it), records LS_ERR_TIMEOUT
+// (with the wait site in the bits above the low byte) and reports failure so
+// the kernel can drain and return.  The limit sits in the device status block
+// right after the error flag, so a kernel reads it through the `err` pointer
+// it already receives.
 // ---------------------------------------------------------------------------
-constexpr long long kWaitCycles = 4000000000LL;
+struct DeviceStatus {
+  int error;                      // first LS_ERR_* raised on the device (0: none)
+  int pad;
+  unsigned long long wait_limit_ns;
+};
+constexpr unsigned long long kDefaultWaitNs = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned long long wait_limit_ns(const int* err) {
+  return err ? reinterpret_cast<const volatile DeviceStatus*>(err)->wait_limit_ns : kDefaultWaitNs;
+}
+// Bounded-wait clock: start() once, then expired() per spin iteration.
+struct WaitClock {
+  unsigned long long t0, limit;
+  __device__ __forceinline__ explicit WaitClock(const int* err) : t0(global_timer_ns()), limit(wait_limit_ns(err)) {}
+  __device__ __forceinline__ bool expired() const { return global_timer_ns() - t0 > limit; }
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -125,9 +148,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // the error code is LS_ERR_TIMEOUT in the low byte and the wait site above it.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int site = 0) {
   if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
+  const WaitClock clk(err);
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) {
+    if (clk.expired()) {
       raise_device_error(err, 7 /* LS_ERR_TIMEOUT */ | (site << 8));
       return false;
     }
@@ -181,7 +204,6 @@ __host__ __device__ __forceinline__ size_t p2p_recv_offset(int max_ctas) {
 __host__ __device__ __forceinline__ size_t p2p_region_bytes(int max_ctas, int max_rows, int width) {
   return p2p_recv_offset(max_ctas) + (size_t)2 * LS_MAX_TP_RANKS * max_rows * width * 8;
 }
-constexpr unsigned long long kP2PWaitNs = 2000000000ull;  // bounded flag wait: 2 s
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -199,12 +221,6 @@ __device__ __forceinline__ uint2 ld_pair_sys(const uint2* p) {
   asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ unsigned long long global_timer_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
 }  // namespace lsb
 
 // Host-side helpers shared by the C-ABI translation units.
@@ -213,6 +229,5 @@ int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
 int sm_count();
 bool aligned16(const void* p);
-bool pdl_enabled();
 int* device_error_ptr();
 }  // namespace lsb_host

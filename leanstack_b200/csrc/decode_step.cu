@@ -94,13 +94,13 @@ __device__ bool ds_grid_sync(const DsParams& p, unsigned int& gen, int* s_abort)
     gen += gridDim.x;
     __threadfence();
     atomicAdd(p.barrier, 1u);
-    const long long t0 = clock64();
+    const WaitClock clk(p.err);
     while (ld_acquire_u32(p.barrier) < gen) {
       if (ld_acquire_u32(p.barrier + 1) != 0u) {  // another CTA aborted
         *s_abort = 1;
         break;
       }
-      if (clock64() - t0 > kWaitCycles) {
+      if (clk.expired()) {
         raise_device_error(p.err, 7 | (16 << 8));
         atomicExch(p.barrier + 1, 1u);
         *s_abort = 1;
@@ -556,7 +556,9 @@ __global__ void __launch_bounds__(kDsThreads, 1) decode_step_kernel(DsParams p) 
 namespace lsb_host {
 // Profiling hook: when set, every barrier of the next decode_step launches
 // records (arrival, release) globaltimer stamps per CTA into this buffer.
+#ifdef LEANB200_PROFILING
 static unsigned long long* g_ds_trace = nullptr;
+#endif
 }  // namespace lsb_host
 
 namespace lsb_host {
@@ -671,7 +673,9 @@ int decode_step(const void* layers, int64_t L, int64_t H, int64_t I, int64_t hq,
   p.best_idx = reinterpret_cast<int*>(ws + w.best_idx);
   p.attn_part = reinterpret_cast<float*>(ws + w.attn_part);
   p.err = device_error_ptr();
+#ifdef LEANB200_PROFILING
   p.trace = g_ds_trace;
+#endif
   p.L = (int)L;
   p.H = (int)H;
   p.I = (int)I;
@@ -687,7 +691,9 @@ int decode_step(const void* layers, int64_t L, int64_t H, int64_t I, int64_t hq,
 
 }  // namespace lsb_host
 
+#ifdef LEANB200_PROFILING
 extern "C" int ls_decode_step_set_trace(void* buffer) {
   lsb_host::g_ds_trace = static_cast<unsigned long long*>(buffer);
   return LS_OK;
 }
+#endif

@@ -122,12 +122,12 @@ __device__ __forceinline__ int tc_unit_owner(long long U, int G, long long u) {
 
 // Spin (bounded) until a global counter reaches `target`.
 __device__ __forceinline__ bool wait_counter(const unsigned int* ctr, unsigned int target, int* err, int site) {
-  const long long t0 = clock64();
+  const WaitClock clk(err);
   while (true) {
     unsigned int v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
     if (v >= target) return true;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clk.expired()) {
       raise_device_error(err, 7 /* LS_ERR_TIMEOUT */ | (site << 8));
       return false;
     }
@@ -869,32 +869,15 @@ struct TcPlan {
 
 // Shared memory given to the stage ring.  Under load the HBM round trip is a
 // few microseconds, so the bytes in flight per SM (stages x tile bytes) set the
-// stream rate.  LEANB200_TC_SMEM_KB overrides it (measurement).
-static int tc_stage_budget_kb() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("LEANB200_TC_SMEM_KB");
-    v = e ? atoi(e) : 112;
-    if (v < 64) v = 64;
-    if (v > 208) v = 208;
-  }
-  return v;
-}
+// stream rate; 112 KB measured best (64 to 208 KB swept).
+static int tc_stage_budget_kb() { return 112; }
 
-// LEANB200_TC_ALIGNED=0 keeps full stream-K for every shape (measurement).
-static bool tc_tile_aligned_split() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("LEANB200_TC_ALIGNED");
-    v = (e && e[0] == '0') ? 0 : 1;
-  }
-  return v == 1;
-}
-
+#ifdef LEANB200_PROFILING
 // Profiling hook (ls_gemm_tc_set_trace): per CTA 8 stamps: start, first stage
 // landed, last MMA issued, epilogue done, then for the first and the last
 // split tile: counter complete, share reduced (0 where there is none).
 static unsigned long long* g_tc_trace = nullptr;
+#endif
 
 static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
   TcPlan pl = {};
@@ -930,7 +913,7 @@ static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
   // Under full stream-K the CTAs that hold pieces of two split tiles reduce
   // both, one after the other, and set the end of the kernel (measured tail
   // after the last MMA: 8-11 us at M 8-80).
-  if (tc_tile_aligned_split() && pl.tiles < sms) {
+  if (pl.tiles < sms) {
     const int per_tile = sms / pl.tiles < pl.kblocks ? sms / pl.tiles : pl.kblocks;
     const int g = pl.tiles * per_tile;
     const int g_up = pl.tiles * (per_tile + 1);
@@ -972,7 +955,7 @@ static int launch_tc_t(const CUtensorMap& w, const CUtensorMap& w2, const CUtens
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, w, w2, x, p);
   if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "gemm_tc launch: %s", cudaGetErrorString(e));
   return LS_OK;
@@ -1037,7 +1020,9 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
   p.acc_buffers = pl.acc_buffers;
   p.tmem_cols = pl.tmem_cols;
   p.w_tiled = static_cast<const unsigned char*>(w_tiled);
+#ifdef LEANB200_PROFILING
   p.trace = g_tc_trace;
+#endif
   p.aligned = (n_out % 8 == 0) && aligned16(out) && (!residual || aligned16(residual)) ? 1 : 0;
   p.w2_tiled = w_tiled ? p.w_tiled + tc_tiled_bytes(n_out, k, 0) : nullptr;
   switch (epi) {
@@ -1071,7 +1056,7 @@ static int launch_big_t(const CUtensorMap& w, const CUtensorMap& w2, const CUten
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, w, w2, x, p);
   return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "gemm_big launch: %s", cudaGetErrorString(e));
 }
@@ -1171,10 +1156,12 @@ int launch_tc_tile(const void* w, int64_t n_rows, int64_t k, int silu, void* out
 
 }  // namespace lsb_host
 
+#ifdef LEANB200_PROFILING
 extern "C" int ls_gemm_tc_set_trace(void* buffer) {
   lsb_host::g_tc_trace = static_cast<unsigned long long*>(buffer);
   return LS_OK;
 }
+#endif
 
 // ---------------------------------------------------------------------------
 // Causal GQA prefill attention on tcgen05 (config 5).
@@ -1590,16 +1577,6 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 namespace lsb_host {
 
 // Causal prefill attention on tcgen05 (see prefill_attention_tc_kernel).
-// LEANB200_PREFILL_ATTN=mma selects the mma.sync kernel instead (measurement).
-bool prefill_attention_tc_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("LEANB200_PREFILL_ATTN");
-    v = (e && e[0] == 'm') ? 0 : 1;
-  }
-  return v == 1;
-}
-
 int launch_prefill_attention_tc(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
                                 int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv,
                                 int64_t max_seq, float scale, void* out, cudaStream_t stream) {
@@ -1644,7 +1621,7 @@ int launch_prefill_attention_tc(const void* q, const void* k_cache, const void* 
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_attention_tc_kernel, mk, mv, p);
   return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "prefill_attention_tc launch: %s", cudaGetErrorString(e));
 }

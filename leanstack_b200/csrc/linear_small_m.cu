@@ -278,21 +278,27 @@ __global__ void __launch_bounds__(kLinThreads, LinMinBlocks<M>::value) linear_sm
     }
     if (trace && tid == 0) trace[1] = global_timer_ns();
     const uint2* recv = reinterpret_cast<const uint2*>(mine + recv_off) + slot_base;
+    // One wait limit for the whole CTA: once any element gives up, every
+    // thread skips its remaining waits (sticky abort), so a vanished peer costs
+    // one limit, not one per element.
+    __shared__ int s_ar_abort;
+    if (tid == 0) s_ar_abort = 0;
+    __syncthreads();
+    const WaitClock clk(p.err);
     for (int i = tid; i < M * P; i += kLinThreads) {
       const int m = i / P, t = i - m * P;
       float y = 0.f;
       for (int q = 0; q < ex.world; ++q) {
         const uint2* src = recv + ((size_t)q * ex.max_rows + m) * ex.width + u0 + t;
         uint2 v = ld_pair_sys(src);
-        if (v.y != epoch) {
-          const unsigned long long t0 = global_timer_ns();
-          do {
-            v = ld_pair_sys(src);
-            if (v.y != epoch && global_timer_ns() - t0 > kP2PWaitNs) {
-              raise_device_error(p.err, LS_ERR_TIMEOUT | (0x30 << 8));
-              break;
-            }
-          } while (v.y != epoch);
+        while (v.y != epoch) {
+          if (*reinterpret_cast<volatile int*>(&s_ar_abort)) break;
+          if (clk.expired()) {
+            raise_device_error(p.err, LS_ERR_TIMEOUT | (0x30 << 8));
+            s_ar_abort = 1;
+            break;
+          }
+          v = ld_pair_sys(src);
         }
         y += __uint_as_float(v.x);
       }
@@ -401,9 +407,11 @@ using namespace lsb;
 // keep ~128 KB per SM in flight, what the measured 6 TB/s needs (one CTA per
 // SM reached only 4.5 TB/s on the lm_head).  m > 4 needs more registers and
 // runs one CTA per SM.
+#ifdef LEANB200_PROFILING
 // Profiling hook (ls_linear_set_trace): when set, every launch records per CTA
 // (start, after the PDL wait, after the prologue, after the main loop, end).
 static unsigned long long* g_lin_trace = nullptr;
+#endif
 
 static int linear_grid(int units, int m) {
   const int g = (m <= 4 ? 2 : 1) * sm_count();
@@ -444,7 +452,7 @@ static int launch_linear_t(LinearParams p, int grid, size_t smem, cudaStream_t s
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
   if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "linear launch: %s", cudaGetErrorString(e));
   return LS_OK;
@@ -465,20 +473,6 @@ static int dispatch_m(int M, LinearParams p, int grid, size_t smem, cudaStream_t
   }
 }
 
-bool stream_supported(int64_t m, int64_t k, int64_t n, int epi);
-int launch_linear_stream(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w, int64_t n,
-                         int epi, const void* residual, void* out, cudaStream_t stream, float* part_val,
-                         int* part_idx, unsigned int* counter, int64_t* out_ids);
-
-static bool stream_path_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("LEANB200_LINEAR");
-    v = (e && e[0] == 's') ? 1 : 0;  // "stream" selects the bulk-TMA variant; the default streams through registers
-  }
-  return v == 1;
-}
-
 static int launch_linear_impl(const void* x, int64_t m, int64_t k, const void* norm_w, float eps, const void* w,
                               int64_t n, int epi, const void* residual, void* out, cudaStream_t stream,
                               float* part_val, int* part_idx, unsigned int* counter, int64_t* out_ids,
@@ -495,9 +489,6 @@ static int launch_linear_impl(const void* x, int64_t m, int64_t k, const void* n
     return set_error(LS_ERR_INVALID_ARGUMENT, "linear: residual is null");
   if (epi == EPI_AR_RESIDUAL && (!ex || norm_w)) return set_error(LS_ERR_INVALID_ARGUMENT, "linear: bad all-reduce call");
   if (epi == EPI_SILU_MUL && (n % 2)) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "linear: gate_up rows odd");
-  if (stream_path_enabled() && epi <= EPI_ARGMAX && !out_keys && id_offset == 0 && stream_supported(m, k, n, epi))
-    return launch_linear_stream(x, m, k, norm_w, eps, w, n, epi, residual, out, stream, part_val, part_idx, counter,
-                                out_ids);
   LinearParams p = {};
   p.x = static_cast<const __nv_bfloat16*>(x);
   p.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
@@ -519,7 +510,9 @@ static int launch_linear_impl(const void* x, int64_t m, int64_t k, const void* n
   p.id_offset = id_offset;
   p.out_keys = out_keys ? 1 : 0;
   p.err = device_error_ptr();
+#ifdef LEANB200_PROFILING
   p.trace = g_lin_trace;
+#endif
   if (epi == EPI_AR_RESIDUAL) {
     p.ex = *ex;
     const int g_ar = grid_override > 0 ? grid_override : linear_grid(p.units, (int)m);
@@ -574,7 +567,9 @@ int lmhead_grid(int64_t vocab, int64_t m) { return linear_grid((int)vocab, (int)
 
 }  // namespace lsb_host
 
+#ifdef LEANB200_PROFILING
 extern "C" int ls_linear_set_trace(void* buffer) {
   lsb_host::g_lin_trace = static_cast<unsigned long long*>(buffer);
   return LS_OK;
 }
+#endif

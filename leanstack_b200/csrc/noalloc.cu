@@ -14,10 +14,12 @@
 //    workspace would exceed it (m rows x CTAs of the head grid) is rejected with
 //    LS_ERR_WORKSPACE before anything is launched.  On a 148-SM B200 every
 //    m in 1..8 fits (at most 9,984 bytes).
-//  * The first call on a device sets that device up: it looks up the scratch
-//    array's device address with the device current and zeroes the arrival
-//    counter on the caller's stream.  Make that first call before any stream
-//    capture begins.
+//  * Every call looks up the scratch array's device address with the device
+//    current (a host-side query; it moves no data and allocates nothing), so
+//    a context that was torn down and rebuilt is followed.  The first call
+//    that sees a new address on a device also zeroes the arrival counter and
+//    waits for that on the caller's stream, so it must finish before any other
+//    call on that device starts, and it must come before any stream capture.
 //  * There is one scratch array per device, shared by every caller of this
 //    entry point on that device.  Two calls whose kernels overlap on the GPU
 //    (different streams, or different host threads) race on it and may return
@@ -44,29 +46,31 @@ int lmhead_grid(int64_t vocab, int64_t m);
 namespace {
 constexpr int kMaxDevices = 64;
 
-// Device address of the scratch array on the current device, set up on the
-// first call per device.  Returns LS_OK or an error code (message recorded).
+// Device address of the scratch array on the current device.  The counter is
+// cleared (synchronously) the first time an address is seen on a device.
+// Returns LS_OK or an error code (message recorded).
 int noalloc_scratch(cudaStream_t stream, unsigned char** out) {
-  static unsigned char* cached[kMaxDevices] = {nullptr};
+  static unsigned char* cleared[kMaxDevices] = {nullptr};
   static std::mutex mu;
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "lmhead_argmax_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices)
     return set_error(LS_ERR_UNSUPPORTED_SHAPE, "lmhead_argmax_noalloc: device %d beyond %d", dev, kMaxDevices);
+  void* ptr = nullptr;
+  e = cudaGetSymbolAddress(&ptr, lsb::g_noalloc_scratch);
+  if (e != cudaSuccess || !ptr)
+    return set_error(LS_ERR_CUDA, "lmhead_argmax_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
   std::lock_guard<std::mutex> lock(mu);
-  if (!cached[dev]) {
-    void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, lsb::g_noalloc_scratch);
-    if (e != cudaSuccess || !ptr)
-      return set_error(LS_ERR_CUDA, "lmhead_argmax_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+  if (cleared[dev] != ptr) {
     // The arrival counter must start at zero.
     e = cudaMemsetAsync(ptr, 0, 256, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
     if (e != cudaSuccess)
       return set_error(LS_ERR_CUDA, "lmhead_argmax_noalloc: clearing the counter: %s", cudaGetErrorString(e));
-    cached[dev] = static_cast<unsigned char*>(ptr);
+    cleared[dev] = static_cast<unsigned char*>(ptr);
   }
-  *out = cached[dev];
+  *out = static_cast<unsigned char*>(ptr);
   return LS_OK;
 }
 }  // namespace

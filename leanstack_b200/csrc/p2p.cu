@@ -10,10 +10,11 @@ int launch_linear_allreduce(const void* x, int64_t m, int64_t k, const void* w, 
                             void* out, const lsb::P2PExchange* ex, cudaStream_t stream);
 }  // namespace lsb_host
 
+#ifdef LEANB200_PROFILING
 namespace lsb {
 // Flag ping-pong between two ranks through their exchange regions: rank 0
 // writes i into rank 1's flag word and waits for i in its own, rank 1 answers.
-// One thread; every wait gives up after kP2PWaitNs.  times[0] = total ns,
+// One thread; every wait gives up after kDefaultWaitNs.  times[0] = total ns,
 // times[1] = 1 if a wait gave up.
 __global__ void p2p_pingpong_kernel(uint32_t* mine, uint32_t* peer, int rank, int iters, unsigned long long* times) {
   const unsigned long long t0 = global_timer_ns();
@@ -22,7 +23,7 @@ __global__ void p2p_pingpong_kernel(uint32_t* mine, uint32_t* peer, int rank, in
     if (rank == 0) st_release_sys(peer, (uint32_t)i);
     const unsigned long long w0 = global_timer_ns();
     while (ld_acquire_sys(mine) < (uint32_t)i) {
-      if (global_timer_ns() - w0 > kP2PWaitNs) { failed = 1; break; }
+      if (global_timer_ns() - w0 > kDefaultWaitNs) { failed = 1; break; }
     }
     if (rank == 1) st_release_sys(peer, (uint32_t)i);
   }
@@ -30,11 +31,13 @@ __global__ void p2p_pingpong_kernel(uint32_t* mine, uint32_t* peer, int rank, in
   times[1] = failed;
 }
 }  // namespace lsb
+#endif  // LEANB200_PROFILING
 
 using namespace lsb_host;
 
 extern "C" {
 
+#ifdef LEANB200_PROFILING
 int ls_p2p_pingpong(void* my_region, void* peer_region, int rank, int iters, unsigned long long* times_dev,
                     ls_stream_t stream) {
   if (!my_region || !peer_region || !times_dev || (rank != 0 && rank != 1) || iters < 1 || iters > (1 << 20))
@@ -45,6 +48,7 @@ int ls_p2p_pingpong(void* my_region, void* peer_region, int rank, int iters, uns
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "p2p_pingpong launch: %s", cudaGetErrorString(e));
 }
+#endif  // LEANB200_PROFILING
 
 int ls_p2p_region_bytes(int64_t max_rows, int64_t width, int64_t max_ctas, int64_t* bytes) {
   if (!bytes || max_rows < 1 || max_rows > 64 || width < 1 || width > (1 << 20) || max_ctas < 1 ||

@@ -51,7 +51,7 @@ def resolve_backend(backend: str, batch_size: int) -> str:
 class DecodeEngine:
     def __init__(self, runtime: QwenSemanticStackRuntime, batch_size: int, max_seq_len: int,
                  max_tokens_per_step: int | None = None, use_graph: bool = True, linear_backend: str = "auto",
-                 tp: TPComm | None = None, shard: TPShard | None = None, gemv_tiles: bool = False,
+                 tp: TPComm | None = None, shard: TPShard | None = None,
                  tc_tiles: list[dict] | None = None):
         if runtime.final_norm_weight is None or runtime.lm_head_weight is None:
             raise ValueError("the engine needs the output head (include_output_head=True)")
@@ -101,22 +101,6 @@ class DecodeEngine:
         else:
             self.lm_ws = torch.zeros(K.lmhead_workspace_bytes(self.T, self.vocab_rows), device=dev,
                                      dtype=torch.uint8)
-        # Optional: tensor-core GEMV over pre-tiled weights for the CUDA-core
-        # backend's linears (an extra copy of the layer weights in the tile
-        # layout).  Off by default while it streams slower than the CUDA-core
-        # kernels.
-        self.tiles = None
-        if self.backend == "cuda_core" and gemv_tiles and self._gemv_shapes_ok(g):
-            self.tiles = []
-            for layer in runtime.layers:
-                att, mlp = layer.attention, layer.mlp
-                self.tiles.append({"qkv": K.gemv_tile_weight(att.qkv_proj_weight),
-                                   "gu": K.gemv_tile_weight(mlp.gate_up_proj_weight, silu=True),
-                                   "o": None if self.tp is not None else K.gemv_tile_weight(att.o_proj_weight),
-                                   "down": None if self.tp is not None else K.gemv_tile_weight(mlp.down_proj_weight)})
-            shapes = [(self.T, g.qkv_dim, K.EPI_STORE), (self.T, g.hidden_size, K.EPI_RESIDUAL),
-                      (self.T, 2 * g.intermediate_size, K.EPI_SILU_MUL)]
-            self.gv_ws = torch.zeros(max(K.gemv_workspace_bytes(*s_) for s_ in shapes), device=dev, dtype=torch.uint8)
         if self.tp is not None:
             self.part = torch.zeros(self.T, g.hidden_size, device=dev, dtype=torch.float32)
             self.keys = torch.zeros(self.T, device=dev, dtype=torch.int64)
@@ -125,7 +109,6 @@ class DecodeEngine:
         self.next_ids = torch.zeros(batch_size, device=dev, dtype=torch.int64)
         self.accepted = torch.zeros(batch_size, device=dev, dtype=torch.int32)
         self.verify_graphs: dict[int, torch.cuda.CUDAGraph] = {}
-        self.fuse_attention = False
         # Pre-tiled tcgen05 weight images per layer ({"qkv", "o", "gu", "down"},
         # e.g. from a leanpack/v1 artifact): the tensor-core linears stream them
         # with plain bulk copies instead of TMA tensor maps.
@@ -147,13 +130,6 @@ class DecodeEngine:
             self.ds_ws = torch.zeros(K.decode_step_workspace_bytes(g.num_key_value_heads), device=dev,
                                      dtype=torch.uint8)
 
-    @staticmethod
-    def _gemv_shapes_ok(g) -> bool:
-        sms = K.sm_count()
-        dims = [(g.qkv_dim, g.hidden_size, 1), (g.hidden_size, g.q_dim, 1), (g.intermediate_size, g.hidden_size, 2),
-                (g.hidden_size, g.intermediate_size, 1)]
-        return all(k % 32 == 0 and n % 8 == 0 and (n // 8) * (k // 32) >= 2 * sms for n, k, _ in dims)
-
     # ------------------------------------------------------------------
     def _forward(self, q_len: int, head, advance: bool = True) -> None:
         """Enqueue one step of ``q_len`` tokens per sequence on the current stream.
@@ -171,37 +147,23 @@ class DecodeEngine:
         K.embed_gather(a.ids[:m], rt.embed_tokens_weight, out=a.x[:m])
         for li, layer in enumerate(rt.layers):
             att, mlp = layer.attention, layer.mlp
-            tl = self.tiles[li] if self.tiles is not None else None
             tt = self.tc_tiles[li] if (tc and self.tc_tiles is not None) else {}
             # QKV projection (with the input RMSNorm) into a.qkv
-            if tl is not None:
-                K.gemv(a.x[:m], tl["qkv"], norm_w=layer.input_layernorm_weight, eps=eps, out=a.qkv[:m],
-                       workspace=self.gv_ws)
-            elif tc:
+            if tc:
                 K.rmsnorm(a.x[:m], layer.input_layernorm_weight, eps, out=self.xn[:m])
                 K.gemm_tc(self.xn[:m], att.qkv_proj_weight, out=a.qkv[:m], workspace=self.tc_ws, tiled=tt.get("qkv"))
             else:
                 K.linear(a.x[:m], att.qkv_proj_weight, norm_w=layer.input_layernorm_weight, eps=eps, out=a.qkv[:m])
-            if self._fused_attention(q_len):
-                # q/k norm + RoPE + K/V append inside the attention kernel
-                K.decode_attention_fused(a.qkv[:m], B, q_len, g.num_attention_heads, g.num_key_value_heads,
-                                         g.head_dim, att.q_norm_weight, att.k_norm_weight, self.cos, self.sin,
-                                         kv.key_cache[li], kv.value_cache[li], self.S, att.attention_scale,
-                                         eps=eps, cache_pos=kv.cache_pos, out=a.attn[:m])
-            else:
-                K.qk_norm_rope(a.qkv[:m], B, q_len, g.num_attention_heads, g.num_key_value_heads, g.head_dim,
-                               att.q_norm_weight, att.k_norm_weight, self.cos, self.sin, eps=eps,
-                               cache_pos=kv.cache_pos, k_cache=kv.key_cache[li], v_cache=kv.value_cache[li],
-                               max_seq=self.S, q_out=a.q[:m])
-                K.decode_attention(a.q[:m], kv.key_cache[li], kv.value_cache[li], B, q_len, g.num_attention_heads,
-                                   g.num_key_value_heads, g.head_dim, self.S, att.attention_scale,
-                                   cache_pos=kv.cache_pos, out=a.attn[:m], workspace=self.attn_ws)
+            K.qk_norm_rope(a.qkv[:m], B, q_len, g.num_attention_heads, g.num_key_value_heads, g.head_dim,
+                           att.q_norm_weight, att.k_norm_weight, self.cos, self.sin, eps=eps,
+                           cache_pos=kv.cache_pos, k_cache=kv.key_cache[li], v_cache=kv.value_cache[li],
+                           max_seq=self.S, q_out=a.q[:m])
+            K.decode_attention(a.q[:m], kv.key_cache[li], kv.value_cache[li], B, q_len, g.num_attention_heads,
+                               g.num_key_value_heads, g.head_dim, self.S, att.attention_scale,
+                               cache_pos=kv.cache_pos, out=a.attn[:m], workspace=self.attn_ws)
             if self.tp is not None:
                 self._row_split(a.attn[:m], att.o_proj_weight, a.x[:m], a.h[:m], tc, tt.get("o"))
-                if tl is not None:
-                    K.gemv(a.h[:m], tl["gu"], norm_w=layer.post_attention_layernorm_weight, eps=eps,
-                           epilogue=K.EPI_SILU_MUL, out=a.act[:m], workspace=self.gv_ws)
-                elif tc:
+                if tc:
                     K.rmsnorm(a.h[:m], layer.post_attention_layernorm_weight, eps, out=self.xn[:m])
                     K.gemm_tc(self.xn[:m], mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=a.act[:m],
                               workspace=self.tc_ws, tiled=tt.get("gu"))
@@ -209,13 +171,6 @@ class DecodeEngine:
                     K.gateup_silu(a.h[:m], layer.post_attention_layernorm_weight, mlp.gate_up_proj_weight, eps,
                                   out=a.act[:m])
                 self._row_split(a.act[:m], mlp.down_proj_weight, a.h[:m], a.x[:m], tc, tt.get("down"))
-            elif tl is not None:
-                K.gemv(a.attn[:m], tl["o"], epilogue=K.EPI_RESIDUAL, residual=a.x[:m], out=a.h[:m],
-                       workspace=self.gv_ws)
-                K.gemv(a.h[:m], tl["gu"], norm_w=layer.post_attention_layernorm_weight, eps=eps,
-                       epilogue=K.EPI_SILU_MUL, out=a.act[:m], workspace=self.gv_ws)
-                K.gemv(a.act[:m], tl["down"], epilogue=K.EPI_RESIDUAL, residual=a.h[:m], out=a.x[:m],
-                       workspace=self.gv_ws)
             elif tc:
                 K.gemm_tc(a.attn[:m], att.o_proj_weight, epilogue=K.EPI_RESIDUAL, residual=a.x[:m], out=a.h[:m],
                           workspace=self.tc_ws, tiled=tt.get("o"))
@@ -240,13 +195,6 @@ class DecodeEngine:
             self._head(rows, n, dest, tc)
         if advance:
             K.advance_cursors(kv.cache_pos, q_len)
-
-    def _fused_attention(self, q_len: int) -> bool:
-        """Whether to fold the q/k norm, RoPE and K/V append into the attention kernel
-        (``ls_decode_attention_fused``).  Measured at bs1 on Qwen3-4B: 385 tok/s fused vs
-        389 tok/s with the separate prologue kernel (the CTA that streams the new key
-        carries a second load chain on the critical path), so the engine keeps two kernels."""
-        return self.fuse_attention and q_len * self.g.num_key_value_groups < 256
 
     def _head(self, rows: torch.Tensor, n: int, dest: torch.Tensor, tc: bool) -> None:
         """Greedy head over ``rows [n, H]``: final norm, lm_head (this rank's vocab shard), argmax into ``dest``."""
@@ -493,8 +441,6 @@ class DecodeEngine:
         if self.persistent:
             return 1
         per_layer = 8 if self.backend == "tc" else 6
-        if self.fuse_attention:  # attention carries the q/k norm, RoPE and K/V append
-            per_layer -= 1
         head = 3 if self.backend == "tc" else 1
         if self.tp is not None:  # + residual-add after each row-split linear, + keys-to-ids
             if self.backend == "tc" or self.tp.p2p is None:

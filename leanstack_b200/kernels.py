@@ -49,6 +49,17 @@ def device_error(clear: bool = True) -> int:
     return v.value
 
 
+def set_wait_limit_ns(ns: int) -> None:
+    """Limit of every bounded device wait on the current device (default 2 s)."""
+    nat.call("ls_set_wait_limit_ns", int(ns))
+
+
+def wait_limit_ns() -> int:
+    v = ctypes.c_int64(0)
+    nat.call("ls_get_wait_limit_ns", ctypes.byref(v))
+    return v.value
+
+
 def embed_gather(ids: torch.Tensor, embed: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     _check(ids, "ids", torch.int64)
     _check(embed, "embed")
@@ -366,23 +377,6 @@ def decode_step(layer_table: torch.Tensor, num_layers: int, hidden: int, interme
              qkv.data_ptr(), attn.data_ptr(), act.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
 
 
-def decode_attention_fused(qkv: torch.Tensor, batch: int, q_len: int, num_heads: int, num_kv_heads: int,
-                           head_dim: int, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor, cos: torch.Tensor,
-                           sin: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, max_seq: int, scale: float,
-                           *, eps: float = 1e-6, cache_pos: torch.Tensor | None = None, uniform_past: int = 0,
-                           rope_offset: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Attention from the raw QKV rows with q/k norm, RoPE and the K/V append folded in."""
-    _check(qkv, "qkv")
-    m = batch * q_len
-    if out is None:
-        out = torch.empty((m, num_heads * head_dim), device=qkv.device, dtype=BF16)
-    nat.call("ls_decode_attention_fused", qkv.data_ptr(), batch, q_len, num_heads, num_kv_heads, head_dim,
-             q_norm_w.data_ptr(), k_norm_w.data_ptr(), float(eps), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
-             int(rope_offset), _ptr(cache_pos), int(uniform_past), k_cache.data_ptr(), v_cache.data_ptr(), max_seq,
-             float(scale), out.data_ptr(), _stream())
-    return out
-
-
 def gemm_big(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,
              out: torch.Tensor | None = None) -> torch.Tensor:
     """Large-M tcgen05 GEMM (prefill): ``out = epilogue(x @ w.T)`` for x ``[m, k]`` with m in the thousands."""
@@ -411,45 +405,6 @@ def gemm_tc_tile_weight(w: torch.Tensor, silu: bool = False) -> torch.Tensor:
     out = torch.empty(nbytes.value, device=w.device, dtype=torch.uint8)
     nat.call("ls_gemm_tc_tile_weight", w.data_ptr(), w.shape[0], w.shape[1], int(bool(silu)), out.data_ptr(),
              _stream())
-    return out
-
-
-def gemv_tile_weight(w: torch.Tensor, silu: bool = False) -> torch.Tensor:
-    """Rewrite a ``[N, K]`` bf16 weight into the tensor-core GEMV tile layout (same bytes)."""
-    _check(w, "w")
-    out = torch.empty_like(w)
-    nat.call("ls_gemv_tile_weight", w.data_ptr(), w.shape[0], w.shape[1], int(bool(silu)), out.data_ptr(), _stream())
-    return out
-
-
-def gemv_workspace_bytes(m: int, n_rows: int, epilogue: int) -> int:
-    v = ctypes.c_int64(0)
-    nat.call("ls_gemv_workspace_bytes", m, n_rows, int(epilogue), ctypes.byref(v))
-    return v.value
-
-
-def gemv(x: torch.Tensor, w_tiled: torch.Tensor, *, norm_w: torch.Tensor | None = None, eps: float = 1e-6,
-         epilogue: int = EPI_STORE, residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
-         workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """``epilogue(norm?(x) @ W.T)`` for x ``[m, K]`` (m <= 8) with ``W`` pre-tiled by :func:`gemv_tile_weight`."""
-    _check(x, "x")
-    _check(w_tiled, "w_tiled")
-    k = x.shape[-1]
-    m = x.numel() // k
-    n = w_tiled.shape[0]
-    if w_tiled.shape[1] != k:
-        raise ValueError(f"weight in-features {w_tiled.shape[1]} != activation width {k}")
-    if norm_w is not None:
-        _check(norm_w, "norm_w")
-    if residual is not None:
-        _check(residual, "residual")
-    cols = n // 2 if epilogue == EPI_SILU_MUL else n
-    if out is None:
-        out = torch.empty((*x.shape[:-1], cols), device=x.device, dtype=BF16)
-    if workspace is None:
-        workspace = torch.zeros(gemv_workspace_bytes(m, n, epilogue), device=x.device, dtype=torch.uint8)
-    nat.call("ls_gemv_bf16", x.data_ptr(), m, k, _ptr(norm_w), float(eps), w_tiled.data_ptr(), n, int(epilogue),
-             _ptr(residual), out.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
     return out
 
 

@@ -14,9 +14,14 @@ Differences from the reference, all deliberate:
 * the decode layer fuses the input RMSNorm into the QKV projection, the
   residual add into o_proj / down, and appends K/V from inside the QKV kernel;
   rounding points are the reference's;
-* the general (B x Q) path runs in chunks of at most 8 tokens on the CUDA-core
-  linear kernels; each chunk sees the keys the reference's masked attention
-  would show it.
+* the general (B x Q) path runs all B * Q tokens of a layer at once and picks
+  the linear kernel by token count m: the CUDA-core streaming kernels with the
+  norm fused in for m <= 8, the tcgen05 weight-streaming GEMM for m <= 128 and
+  the persistent large-M tcgen05 GEMM above (prefill); attention applies the
+  reference's causal / decode-mask visibility from the cache cursor and moves
+  to the tcgen05 prefill kernel at 256 query rows per kv head.  These are the
+  kernels and call order of ``DecodeEngine``'s steps, so both give the same
+  bits.
 """
 
 from __future__ import annotations
@@ -31,7 +36,8 @@ import torch
 from . import kernels as K
 from .kv_cache import KVPageLayout, StaticKVBlockManager
 
-SMALL_M = 8  # largest token count of one CUDA-core linear launch
+SMALL_M = 8      # largest token count of one CUDA-core linear launch
+TC_MAX_M = 128   # largest token count of one weight-streaming tcgen05 GEMM launch
 
 
 @dataclass
@@ -166,11 +172,39 @@ def qwen_rmsnorm_vector(hidden_states: torch.Tensor, weight: torch.Tensor, eps: 
     return qwen_rmsnorm(hidden_states.reshape(1, -1), weight, eps).view(-1)
 
 
+def _linear_routed(x: torch.Tensor, w: torch.Tensor, *, norm_w: torch.Tensor | None = None, eps: float = 1e-6,
+                   epilogue: int = K.EPI_STORE, residual: torch.Tensor | None = None) -> torch.Tensor:
+    """``epilogue(w @ rmsnorm?(x))`` for x ``[m, k]``, on the kernel family for m.
+
+    m <= 8: CUDA-core streaming linear with the RMSNorm in its prologue;
+    m <= 128: RMSNorm kernel, then the tcgen05 weight-streaming GEMM;
+    larger: RMSNorm kernel, then the persistent large-M tcgen05 GEMM.
+    """
+    m = x.shape[0]
+    if m <= SMALL_M:
+        return K.linear(x, w, norm_w=norm_w, eps=eps, epilogue=epilogue, residual=residual)
+    xn = K.rmsnorm(x, norm_w, eps) if norm_w is not None else x
+    if m <= TC_MAX_M:
+        return K.gemm_tc(xn, w, epilogue=epilogue, residual=residual)
+    return K.gemm_big(xn, w, epilogue=epilogue, residual=residual)
+
+
 def _qkv(hidden: torch.Tensor, batch: int, q_len: int, qkv_w, hq, hkv, d, qn, kn, cos, sin, eps, input_norm=None,
          kv: StaticKVBlockManager | None = None, layer_idx: int = 0, past: int = 0):
     cos_t, sin_t = _cos_sin_table(cos, sin)
     m = batch * q_len
     x = hidden.reshape(m, -1).contiguous()
+    if m > SMALL_M:
+        qkv = _linear_routed(x, qkv_w, norm_w=input_norm, eps=eps)
+        if kv is not None:
+            q = K.qk_norm_rope(qkv, batch, q_len, hq, hkv, d, qn, kn, cos_t, sin_t, eps=eps, uniform_past=past,
+                               rope_offset=past, k_cache=kv.key_cache[layer_idx], v_cache=kv.value_cache[layer_idx],
+                               max_seq=kv.layout.max_seq_len)
+            return q, None, None
+        k_out = torch.empty((m, hkv, d), device=x.device, dtype=x.dtype)
+        v_out = torch.empty((m, hkv, d), device=x.device, dtype=x.dtype)
+        q = K.qk_norm_rope(qkv, batch, q_len, hq, hkv, d, qn, kn, cos_t, sin_t, eps=eps, k_out=k_out, v_out=v_out)
+        return q, k_out, v_out
     if kv is not None:
         q = K.qkv_rope_append(x, batch, q_len, qkv_w, hq, hkv, d, qn, kn, cos_t, sin_t, input_norm_w=input_norm,
                               eps=eps, uniform_past=past, rope_offset=past, k_cache=kv.key_cache[layer_idx],
@@ -197,8 +231,6 @@ def _semantic_attention_qkv(hidden_states, qkv_proj_weight, q_proj_out_dim, k_pr
                             num_key_value_heads, head_dim, q_norm_weight, k_norm_weight, cos, sin, rms_norm_eps):
     """General fused QKV (``qwen_explicit.py:733-770``) -> q [B,Hq,Q,D], k, v [B,Hkv,Q,D]."""
     b, q_len, _ = hidden_states.shape
-    if b * q_len > SMALL_M:
-        raise ValueError(f"{b * q_len} tokens in one call; the CUDA-core path takes <= {SMALL_M}")
     q, k, v = _qkv(hidden_states, b, q_len, qkv_proj_weight, num_attention_heads, num_key_value_heads, head_dim,
                    q_norm_weight, k_norm_weight, cos, sin, rms_norm_eps)
     return (q.view(b, q_len, num_attention_heads, head_dim).transpose(1, 2),
@@ -234,7 +266,7 @@ def _semantic_decode_attention_output(query_states, key_states, value_states, o_
     """General SDPA + o_proj (``qwen_explicit.py:855-883``) -> [B, Q, H]."""
     b, _, q_len, _ = query_states.shape
     attn = _attend(query_states, key_states, value_states, attention_scale)
-    return K.linear(attn, o_proj_weight).view(b, q_len, -1)
+    return _linear_routed(attn, o_proj_weight).view(b, q_len, -1)
 
 
 def sdpa_qwen_attention_forward(query_states, key_states, value_states, attention_mask, scaling,
@@ -262,8 +294,9 @@ def _semantic_mlp_epilogue(hidden_states, post_attention_layernorm_weight, gate_
                            down_proj_weight, rms_norm_eps):
     shape = hidden_states.shape
     h = hidden_states.reshape(-1, shape[-1]).contiguous()
-    act = K.gateup_silu(h, post_attention_layernorm_weight, gate_up_proj_weight, rms_norm_eps)
-    return K.down_residual(act, down_proj_weight, h).view(shape)
+    act = _linear_routed(h, gate_up_proj_weight, norm_w=post_attention_layernorm_weight, eps=rms_norm_eps,
+                         epilogue=K.EPI_SILU_MUL)
+    return _linear_routed(act, down_proj_weight, epilogue=K.EPI_RESIDUAL, residual=h).view(shape)
 
 
 def _semantic_post_attention_mlp(attention_output, residual, o_proj_weight, post_attention_layernorm_weight,
@@ -271,9 +304,11 @@ def _semantic_post_attention_mlp(attention_output, residual, o_proj_weight, post
     """o_proj + residual, then the MLP epilogue (``qwen_explicit.py:809-852``)."""
     shape = residual.shape
     res = residual.reshape(-1, shape[-1]).contiguous()
-    h = K.oproj_residual(attention_output.reshape(res.shape[0], -1).contiguous(), o_proj_weight, res)
-    act = K.gateup_silu(h, post_attention_layernorm_weight, gate_up_proj_weight, rms_norm_eps)
-    return K.down_residual(act, down_proj_weight, h).view(shape)
+    h = _linear_routed(attention_output.reshape(res.shape[0], -1).contiguous(), o_proj_weight,
+                       epilogue=K.EPI_RESIDUAL, residual=res)
+    act = _linear_routed(h, gate_up_proj_weight, norm_w=post_attention_layernorm_weight, eps=rms_norm_eps,
+                         epilogue=K.EPI_SILU_MUL)
+    return _linear_routed(act, down_proj_weight, epilogue=K.EPI_RESIDUAL, residual=h).view(shape)
 
 
 def _semantic_greedy_head_vector(hidden_states, final_norm_weight, lm_head_weight, rms_norm_eps):
@@ -311,9 +346,11 @@ def semantic_qwen_layer_forward(config, layer: QwenSemanticLayerRuntime, rope_in
                                 kv_cache: StaticKVBlockManager | None = None, position_embeddings=None):
     """General layer over ``[B, Q, H]`` (``qwen_explicit.py:1211-1244``).
 
-    Tokens run in chunks of at most 8 (``B * chunk <= 8``): chunk c appends its
-    K/V at the layer cursor and attends every key up to its own position, which
-    is the reference's causal / decode-mask visibility.
+    All B * Q tokens go through the layer together: the K/V of the Q new
+    positions land at the layer cursor, and query i of each sequence attends
+    every key up to its own position -- the reference's causal prefill and
+    decode-mask visibility.  The linears run on the kernel family for
+    m = B * Q (``_linear_routed``).
     """
     if kv_cache is None:
         raise ValueError("the native general path needs a KV cache (the reference's cache-less path is unused)")
@@ -323,25 +360,19 @@ def semantic_qwen_layer_forward(config, layer: QwenSemanticLayerRuntime, rope_in
     eps = config.rms_norm_eps
     b, q_len, hidden = hidden_states.shape
     cos_all, sin_all = position_embeddings
-    chunk = max(1, SMALL_M // b)
-    outs = []
-    for c0 in range(0, q_len, chunk):
-        c1 = min(q_len, c0 + chunk)
-        n = c1 - c0
-        residual = hidden_states[:, c0:c1].reshape(b * n, hidden).contiguous()
-        past = kv_cache.reserve(att.layer_idx, n)
-        q, _, _ = _qkv(residual, b, n, att.qkv_proj_weight, att.num_attention_heads, att.num_key_value_heads,
-                       att.head_dim, att.q_norm_weight, att.k_norm_weight, cos_all[:, c0:c1], sin_all[:, c0:c1],
-                       eps, input_norm=layer.input_layernorm_weight, kv=kv_cache, layer_idx=att.layer_idx,
-                       past=past)
-        kv_cache.advance_layer(att.layer_idx, n)
-        ks, vs = kv_cache.get(att.layer_idx)
-        attn = _attend(q.view(b, n, att.num_attention_heads, att.head_dim).transpose(1, 2), ks, vs,
-                       att.attention_scale)
-        h = K.oproj_residual(attn, att.o_proj_weight, residual)
-        act = K.gateup_silu(h, layer.post_attention_layernorm_weight, mlp.gate_up_proj_weight, eps)
-        outs.append(K.down_residual(act, mlp.down_proj_weight, h).view(b, n, hidden))
-    return outs[0] if len(outs) == 1 else torch.cat(outs, dim=1)
+    residual = hidden_states.reshape(b * q_len, hidden).contiguous()
+    past = kv_cache.reserve(att.layer_idx, q_len)
+    q, _, _ = _qkv(residual, b, q_len, att.qkv_proj_weight, att.num_attention_heads, att.num_key_value_heads,
+                   att.head_dim, att.q_norm_weight, att.k_norm_weight, cos_all, sin_all, eps,
+                   input_norm=layer.input_layernorm_weight, kv=kv_cache, layer_idx=att.layer_idx, past=past)
+    kv_cache.advance_layer(att.layer_idx, q_len)
+    ks, vs = kv_cache.get(att.layer_idx)
+    attn = _attend(q.view(b, q_len, att.num_attention_heads, att.head_dim).transpose(1, 2), ks, vs,
+                   att.attention_scale)
+    h = _linear_routed(attn, att.o_proj_weight, epilogue=K.EPI_RESIDUAL, residual=residual)
+    act = _linear_routed(h, mlp.gate_up_proj_weight, norm_w=layer.post_attention_layernorm_weight, eps=eps,
+                         epilogue=K.EPI_SILU_MUL)
+    return _linear_routed(act, mlp.down_proj_weight, epilogue=K.EPI_RESIDUAL, residual=h).view(b, q_len, hidden)
 
 
 # ---------------------------------------------------------------------------

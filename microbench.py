@@ -1,6 +1,7 @@
+#!/usr/bin/env python
 """Per-kernel timing at the Qwen3-4B decode shapes (CUDA events, cold weights).
 
-``python -m leanstack_b200.microbench [--kernels a,b] [--reps N] [--m 1] [--seq 600]``
+``python microbench.py [--kernels a,b] [--reps N] [--m 1] [--seq 600]``
 
 Each kernel runs over ``--copies`` distinct weight sets (more bytes than the
 126 MB L2), rotating between them, so every launch streams its weights from
@@ -12,12 +13,16 @@ from __future__ import annotations
 
 import argparse
 import json
+import sys
+from pathlib import Path
 
 import torch
 
-from . import kernels as K
-from . import synth
-from .config import QWEN3_4B
+sys.path.insert(0, str(Path(__file__).resolve().parent))
+
+from leanstack_b200 import kernels as K  # noqa: E402
+from leanstack_b200 import synth  # noqa: E402
+from leanstack_b200.config import QWEN3_4B  # noqa: E402
 
 
 def _events():
@@ -81,7 +86,7 @@ def main(argv=None) -> int:
             t = _time(lambda i: K.linear(x, qkv_w[i % C], norm_w=nw, out=scratch), args.reps)
             out["qkv(norm+gemv)"] = (t, g.qkv_dim * H * 2)
         if "qknorm" in wanted:
-            from . import _native as nat
+            from leanstack_b200 import _native as nat
 
             def qk(i):
                 nat.call("ls_rmsnorm_qkv_rope_kvappend", x.data_ptr(), m, 1, H, nw.data_ptr(), 1e-6,
@@ -159,27 +164,6 @@ def main(argv=None) -> int:
             big_case("gateup", 2 * I, H, K.EPI_SILU_MUL)
         if "big_down" in big:
             big_case("down", H, I, K.EPI_RESIDUAL)
-    gv = {k for k in wanted if k.startswith("gv_")}
-    if gv:
-        def gv_case(name, n_rows, k_dim, epi, silu=False, norm=False):
-            wts = [K.gemv_tile_weight(t, silu=silu) for t in w((n_rows, k_dim), "mb/gv" + name)]
-            xa = synth.normal((m, k_dim), 1.0, 0, "mb/gx" + name, device=dev)
-            n_out = n_rows // 2 if silu else n_rows
-            res = synth.normal((m, n_out), 1.0, 0, "mb/gres" + name, device=dev)
-            nwk = synth.norm_weight((k_dim,), 0, "mb/gnw" + name, device=dev) if norm else None
-            o = torch.empty(m, n_out, device=dev, dtype=torch.bfloat16)
-            ws_ = torch.zeros(K.gemv_workspace_bytes(m, n_rows, epi), device=dev, dtype=torch.uint8)
-            t = _time(lambda i: K.gemv(xa, wts[i % C], norm_w=nwk, epilogue=epi, residual=res, out=o,
-                                       workspace=ws_), args.reps)
-            out[f"gv_{name}(m={m})"] = (t, n_rows * k_dim * 2)
-        if "gv_qkv" in gv:
-            gv_case("qkv", g.qkv_dim, H, K.EPI_STORE, norm=True)
-        if "gv_oproj" in gv:
-            gv_case("oproj", H, g.q_dim, K.EPI_RESIDUAL)
-        if "gv_gateup" in gv:
-            gv_case("gateup", 2 * I, H, K.EPI_SILU_MUL, silu=True, norm=True)
-        if "gv_down" in gv:
-            gv_case("down", H, I, K.EPI_RESIDUAL)
     tc = {k for k in wanted if k.startswith("tc_")}
     if tc:
         def tc_case(name, n_rows, k_dim, epi, n_out, extra=None):
@@ -212,8 +196,8 @@ def main(argv=None) -> int:
         t = _time(lambda i: K.rmsnorm(xr, nw, 1e-6, out=yr), args.reps)
         out["rmsnorm"] = (t, 2 * m * H * 2)
     if "persistent" in wanted:
-        from .engine import DecodeEngine
-        from .leanserve import materialize_from_tensors
+        from leanstack_b200.engine import DecodeEngine
+        from leanstack_b200.leanserve import materialize_from_tensors
         from dataclasses import replace
 
         geo = replace(g, num_hidden_layers=args.layers)

@@ -68,7 +68,7 @@ def rope_cache(inv_freq: torch.Tensor, max_seq_len: int, dtype: torch.dtype,
     Angles are fp32 products ``pos * inv_freq``; cos/sin are taken in fp32 and
     rounded to the model dtype (bf16), exactly as the reference's position cache.
     """
-    pos = torch.arange(max_seq_len, dtype=torch.float32)
+    pos = torch.arange(max_seq_len, dtype=torch.float32, device=inv_freq.device)
     freqs = torch.outer(pos, inv_freq.float())
     return ((freqs.cos() * attention_scaling).to(dtype), (freqs.sin() * attention_scaling).to(dtype))
 
@@ -138,14 +138,25 @@ def qkv_project(xn: torch.Tensor, w: LayerWeights, hq: int, hkv: int, d: int, co
     return apply_rope(q, cos, sin), apply_rope(k, cos, sin), v
 
 
-def decode_mask(query_len: int, total_len: int, dtype: torch.dtype) -> torch.Tensor:
+def decode_mask(query_len: int, total_len: int, dtype: torch.dtype, device="cpu") -> torch.Tensor:
     """Additive mask: key j visible to query i iff ``j <= past + i`` (``qwen_explicit.py:551-563``)."""
     past = total_len - query_len
-    qpos = torch.arange(query_len).unsqueeze(1)
-    kpos = torch.arange(total_len).unsqueeze(0)
-    mask = torch.zeros((query_len, total_len), dtype=dtype)
+    qpos = torch.arange(query_len, device=device).unsqueeze(1)
+    kpos = torch.arange(total_len, device=device).unsqueeze(0)
+    mask = torch.zeros((query_len, total_len), dtype=dtype, device=device)
     mask = mask.masked_fill(~(kpos <= past + qpos), torch.finfo(dtype).min)
     return mask[None, None]
+
+
+def sdpa(*args, **kwargs) -> torch.Tensor:
+    """``F.scaled_dot_product_attention``, the reference's attention op.
+
+    Every attention of the oracle goes through this name, so a measurement
+    script can wrap it (``tests/golden/make_stream_paths.py`` perturbs its
+    output by one ulp in a few elements to measure how sensitive a greedy
+    stream is to such noise).
+    """
+    return F.scaled_dot_product_attention(*args, **kwargs)
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask, scale: float) -> torch.Tensor:
@@ -157,7 +168,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask, scale: fl
     q_len, kv_len = q.shape[-2], k.shape[-2]
     is_decode = q_len == 1 and kv_len >= 1
     causal = (not is_decode) and q_len == kv_len
-    out = F.scaled_dot_product_attention(
+    out = sdpa(
         q, k, v,
         attn_mask=None if (causal or is_decode) else mask,
         dropout_p=0.0, is_causal=causal, scale=scale, enable_gqa=True,
@@ -194,9 +205,10 @@ class OracleKV:
     layer_seq_lens: list[int] = field(default_factory=list)
 
     @classmethod
-    def empty(cls, layers: int, batch: int, hkv: int, max_seq: int, d: int, dtype) -> "OracleKV":
+    def empty(cls, layers: int, batch: int, hkv: int, max_seq: int, d: int, dtype, device="cpu") -> "OracleKV":
         shape = (layers, batch, hkv, max_seq, d)
-        return cls(torch.zeros(shape, dtype=dtype), torch.zeros(shape, dtype=dtype), [0] * layers)
+        return cls(torch.zeros(shape, dtype=dtype, device=device), torch.zeros(shape, dtype=dtype, device=device),
+                   [0] * layers)
 
     def append(self, layer: int, k: torch.Tensor, v: torch.Tensor) -> None:
         start = self.layer_seq_lens[layer]
@@ -266,11 +278,17 @@ class OracleModel:
             precision=precision,
         )
 
+    @property
+    def device(self) -> torch.device:
+        return self.embed_tokens.device
+
     def new_kv(self, batch: int, max_seq: int) -> OracleKV:
-        return OracleKV.empty(len(self.layers), batch, self.num_key_value_heads, max_seq, self.head_dim, self.dtype)
+        return OracleKV.empty(len(self.layers), batch, self.num_key_value_heads, max_seq, self.head_dim, self.dtype,
+                              self.device)
 
     def rope(self, max_seq: int):
-        return rope_cache(rope_inv_freq(self.head_dim, self.rope_theta), max_seq, self.dtype)
+        """Position cache on the model's device (the reference builds it where the model lives)."""
+        return rope_cache(rope_inv_freq(self.head_dim, self.rope_theta).to(self.device), max_seq, self.dtype)
 
 
 def layer_forward(m: OracleModel, layer_idx: int, w: LayerWeights, hidden: torch.Tensor, kv: OracleKV | None,
@@ -303,10 +321,59 @@ def stack_forward(m: OracleModel, hidden: torch.Tensor, kv: OracleKV, position_c
     cos_c, sin_c = position_cache
     cos = cos_c[past:past + q_len].unsqueeze(0)
     sin = sin_c[past:past + q_len].unsqueeze(0)
-    mask = decode_mask(q_len, past + q_len, m.dtype) if (q_len > 1 and past > 0) else None
+    mask = decode_mask(q_len, past + q_len, m.dtype, hidden.device) if (q_len > 1 and past > 0) else None
     for i, w in enumerate(m.layers):
         hidden = layer_forward(m, i, w, hidden, kv, cos, sin, mask)
     return hidden
+
+
+def decode_layer_vector(m: OracleModel, layer_idx: int, w: LayerWeights, hidden: torch.Tensor, kv: OracleKV,
+                        cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """One layer of the bs1 decode path (``semantic_qwen_decode_layer_forward``,
+    ``qwen_explicit.py:1247-1272``, with ``:1147-1177``, ``:773-806``, ``:886-913``,
+    ``:932-949``).
+
+    Same rounding points as :func:`layer_forward`, but every linear is a
+    ``torch.mv`` on a flat vector, the form the reference's decode driver runs.
+    On the CPU ``mv`` and ``F.linear`` reach different bf16 kernels whose fp32
+    sums differ in order, so the two paths are separate restatements.
+    """
+    eps = m.rms_norm_eps
+    hq, hkv, d = m.num_attention_heads, m.num_key_value_heads, m.head_dim
+    residual = hidden.reshape(-1)
+    xn = rmsnorm(residual.view(1, -1), w.input_layernorm, eps).view(-1)
+    qkv = torch.mv(w.qkv_proj, xn)
+    q, k, v = torch.split(qkv, (hq * d, hkv * d, hkv * d), dim=0)
+    q = rmsnorm(q.view(1, hq, d), w.q_norm, eps).view(1, hq, 1, d)
+    k = rmsnorm(k.view(1, hkv, d), w.k_norm, eps).view(1, hkv, 1, d)
+    v = v.view(1, hkv, 1, d)
+    q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+    kv.append(layer_idx, k, v)
+    keys, values = kv.get(layer_idx)
+    attn = sdpa(q, keys, values, dropout_p=0.0, is_causal=False, scale=d ** -0.5, enable_gqa=hq != hkv)
+    h = residual + torch.mv(w.o_proj, attn.reshape(-1))
+    n = rmsnorm(h.view(1, -1), w.post_attention_layernorm, eps).view(-1)
+    gu = torch.mv(w.gate_up_proj, n)
+    g, u = torch.split(gu, (m.intermediate_size, gu.shape[0] - m.intermediate_size), dim=0)
+    return (h + torch.mv(w.down_proj, F.silu(g) * u)).view(1, 1, -1)
+
+
+def decode_step_vector(m: OracleModel, ids: torch.Tensor, kv: OracleKV, position_cache) -> torch.Tensor:
+    """``run_semantic_stack_decode`` for one sequence and one token (``qwen_explicit.py:1617-1644``)."""
+    past = kv.seq_len()
+    cos_c, sin_c = position_cache
+    cos, sin = cos_c[past:past + 1].unsqueeze(0), sin_c[past:past + 1].unsqueeze(0)
+    hidden = embed(m, ids.view(1, 1).to(m.device))
+    for i, w in enumerate(m.layers):
+        hidden = decode_layer_vector(m, i, w, hidden, kv, cos, sin)
+    return hidden
+
+
+def greedy_logits_vector(m: OracleModel, hidden: torch.Tensor) -> torch.Tensor:
+    """The bs1 torch head: ``mv(lm_head, rmsnorm(last))`` (``qwen_explicit.py:952-960``, ``:1814-1832``)."""
+    last = hidden[0, -1]
+    n = rmsnorm(last.view(1, -1), m.final_norm, m.rms_norm_eps).view(-1)
+    return torch.mv(m.lm_head, n)
 
 
 def embed(m: OracleModel, ids: torch.Tensor) -> torch.Tensor:

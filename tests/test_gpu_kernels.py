@@ -305,33 +305,3 @@ def test_prefill_attention_ignores_cache_past_the_sequence(hq, hkv, batch, q_len
     assert (got - ref).abs().max().item() <= 1e-2
     assert (out.cpu() == ref.bfloat16()).float().mean().item() > 0.99
     assert K.device_error() == 0
-
-
-@pytest.mark.parametrize("batch,q_len,past", [(1, 1, 513), (3, 1, 70), (2, 5, 300), (16, 5, 1000), (1, 8, 0)])
-def test_fused_attention_matches_two_kernel_path(batch, q_len, past):
-    """ls_decode_attention_fused (q/k norm + RoPE + K/V append inside attention) against
-    ls_qk_norm_rope_kvappend + ls_decode_attention: the same cache contents, outputs within the bound."""
-    hq, hkv, d, S = 32, 8, 128, 2048
-    qkv_dim = (hq + 2 * hkv) * d
-    qkv = _rand((batch * q_len, qkv_dim), 1.0, f"fq{batch}{q_len}")
-    qn = synth.norm_weight((d,), 11, "fqn", device=DEV)
-    kn = synth.norm_weight((d,), 11, "fkn", device=DEV)
-    ang = torch.arange(S, dtype=torch.float32)[:, None] * (1e6 ** (-torch.arange(0, d, 2, dtype=torch.float32) / d))
-    cos, sin = ang.cos().bfloat16().to(DEV), ang.sin().bfloat16().to(DEV)
-    kc0 = _rand((batch, hkv, S, d), 1.0, "fkc")
-    vc0 = _rand((batch, hkv, S, d), 1.0, "fvc")
-    pos = torch.tensor([past + 3 * b for b in range(batch)], dtype=torch.int32, device=DEV)
-    kc1, vc1 = kc0.clone(), vc0.clone()
-    q = torch.empty(batch * q_len, hq, d, device=DEV, dtype=torch.bfloat16)
-    K.qk_norm_rope(qkv, batch, q_len, hq, hkv, d, qn, kn, cos, sin, eps=1e-6, cache_pos=pos, k_cache=kc1,
-                   v_cache=vc1, max_seq=S, q_out=q)
-    ref = K.decode_attention(q, kc1, vc1, batch, q_len, hq, hkv, d, S, d ** -0.5, cache_pos=pos)
-    kc2, vc2 = kc0.clone(), vc0.clone()
-    out = K.decode_attention_fused(qkv, batch, q_len, hq, hkv, d, qn, kn, cos, sin, kc2, vc2, S, d ** -0.5,
-                                   eps=1e-6, cache_pos=pos)
-    torch.cuda.synchronize()
-    assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
-    err = (out.float() - ref.float()).abs().max().item()
-    assert err <= tol(ref.float()), err
-    assert (out == ref).float().mean().item() > 0.98
-    assert K.device_error() == 0

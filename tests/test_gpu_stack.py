@@ -24,12 +24,6 @@ from oracle import qwen_oracle as qo
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-BF16_ULP_AT_4 = 2 ** -5  # spacing of bf16 logits in [4, 8)
-# Measured drift of this GPU path from the CPU reference on the top logits of
-# config 2: 0.06 mean, 0.14 max (2-4 ulps at the logits' magnitude, 4..8).  A
-# step may disagree only where the reference's own top-2 margin is within that
-# drift: 4 ulps.
-NEAR_TIE = 4 * BF16_ULP_AT_4
 
 
 def _gold(golden_dir, name):
@@ -130,6 +124,66 @@ def test_general_layer_verify_and_prefill(golden_dir, tag):
         (Vn[:, :, past:].cpu().float() - c["v_new"].float()).abs().max().item() <= tol(c["v_new"].float())
 
 
+def _oracle_fp32_last_rows(tensors, g, prompt, verify_ids=None):
+    """fp32 oracle (CPU) of a prefill, optionally followed by one verify pass."""
+    cpu = {k: v.cpu() for k, v in tensors.items()}
+    m = qo.OracleModel.from_checkpoint(g, cpu, precision="fp32")
+    kv, pc = m.new_kv(prompt.shape[0], 1024), m.rope(1024)
+    h = qo.stack_forward(m, qo.embed(m, prompt.cpu()), kv, pc)
+    if verify_ids is not None:
+        h = qo.stack_forward(m, qo.embed(m, verify_ids.cpu()), kv, pc)
+    return h
+
+
+def test_dispatch_general_path_runs_the_engine_kernels():
+    """The reference-shaped drivers take any [B, Q]: a 512-token prefill runs the
+    large-M tcgen05 GEMMs and the tcgen05 prefill attention, a B 16 x Q 5
+    verify the weight-streaming tcgen05 GEMMs -- the kernels and call order of
+    ``DecodeEngine.prefill_full`` and its verify pass, so the hidden states and
+    the cache match the engine bit for bit, and the fp32 oracle within the bound
+    (Qwen3-4B geometry, 4 layers; ``qwen_explicit.py:1211-1244, 1455-1491, 1676-1717``)."""
+    from dataclasses import replace
+
+    g = replace(QWEN3_4B, num_hidden_layers=4)
+    t = synth.synth_checkpoint(g, 2, device=DEV)
+    rt = materialize_from_tensors(g, t, device=DEV)
+    S = 1024
+    H = g.hidden_size
+    # prefill, B 1 x 512
+    prompt = synth.token_ids((1, 512), g.vocab_size, 2, "dispatch/prompt")
+    hid, cache = qe.run_semantic_stack_prefill(rt, prompt.to(DEV), max_seq_len=S)
+    eng = DecodeEngine(rt, batch_size=1, max_seq_len=S, linear_backend="tc", use_graph=False)
+    eng.prefill_full(prompt)
+    assert torch.equal(hid[:, -1], eng.last_head_rows())
+    assert torch.equal(cache.key_cache[:, :, :, :512], eng.kv.key_cache[:, :, :, :512])
+    assert torch.equal(cache.value_cache[:, :, :, :512], eng.kv.value_cache[:, :, :, :512])
+    ref = _oracle_fp32_last_rows(t, g, prompt)[:, -1]
+    err = (hid[:, -1].float().cpu() - ref).abs().max().item()
+    print(f"dispatch prefill 512: max|err| vs fp32 {err:.4g}, tol {tol(ref):.4g}")
+    assert err <= tol(ref)
+    del eng, cache
+    # verify, B 16 x Q 5 over 64 cached positions
+    B, P, Q = 16, 64, 5
+    prompt = synth.token_ids((B, P), g.vocab_size, 2, "dispatch/vprompt")
+    props = synth.token_ids((B, Q), g.vocab_size, 2, "dispatch/vprops")
+    _, cache = qe.run_semantic_stack_prefill(rt, prompt.to(DEV), max_seq_len=S)
+    hv, cache = qe.run_semantic_stack_verify_tokens(rt, props.to(DEV), cache)
+    assert hv.shape == (B, Q, H) and cache.sequence_lens == [P + Q] * B
+    eng = DecodeEngine(rt, batch_size=B, max_seq_len=S, linear_backend="tc", use_graph=False)
+    eng.prefill_full(prompt)
+    eng.verify_inputs(Q - 1).copy_(props.to(DEV))
+    eng.verify_step(Q - 1)
+    torch.cuda.synchronize()
+    assert torch.equal(hv.reshape(B * Q, H), eng.arenas.x[:B * Q])
+    assert torch.equal(cache.key_cache[:, :, :, :P + Q], eng.kv.key_cache[:, :, :, :P + Q])
+    ref = _oracle_fp32_last_rows(t, g, prompt, props)
+    err = (hv.float().cpu() - ref).abs().max().item()
+    print(f"dispatch verify 16 x 5: max|err| vs fp32 {err:.4g}, tol {tol(ref):.4g}")
+    assert err <= tol(ref)
+    from leanstack_b200 import kernels as K
+    assert K.device_error(clear=True) == 0
+
+
 def _tiny_runtime():
     t = synth.synth_checkpoint(TINY, 3, device=DEV)
     return materialize_from_tensors(TINY, t, device=DEV)
@@ -156,18 +210,6 @@ def test_tiny_stack_greedy_engine_and_dispatch(golden_dir):
     assert toks == want
 
 
-def test_tiny_stack_greedy_engine_tiled_gemv(golden_dir):
-    """The engine with the tensor-core GEMV over pre-tiled weights reproduces the reference's greedy stream."""
-    gold = _gold(golden_dir, "tiny_stack.pt")["greedy"]
-    rt = _tiny_runtime()
-    prompt = gold["prompt"]
-    want = gold["tokens"].tolist()
-    eng = DecodeEngine(rt, batch_size=1, max_seq_len=prompt.shape[1] + 40, gemv_tiles=True)
-    assert eng.tiles is not None
-    got = eng.generate(prompt, len(want))[0].tolist()
-    assert got == want
-
-
 def test_persistent_step_matches_layered_step():
     """The one-kernel decode step produces the same tokens as the kernel-per-op step on the tiny stack."""
     rt = _tiny_runtime()
@@ -192,22 +234,81 @@ def test_engine_graph_replay_equals_eager():
     assert torch.equal(a[:1], c)
 
 
-@pytest.mark.parametrize("backend", ["cuda_core", "tc", "persistent"])
-def test_cfg2_4b_greedy_stream_teacher_forced(golden_dir, backend):
-    """First 64 greedy tokens of random-init Qwen3-4B vs the reference (BASELINE config 2).
+def _oracle_stream_on_device(m, gold, vector: bool) -> list[int]:
+    """The reference's torch arithmetic (oracle, bf16) on this GPU, teacher-forced.
 
-    Teacher forcing: every step consumes the reference's previous token, so one
-    disagreement cannot cascade.  A step may differ only where the reference's
-    own top-2 bf16 logits are within two bf16 ulps (a near-tie that the
-    measured numeric drift can flip); the free-running match length is printed.
+    ``vector`` selects the decode driver's bs1 form (``torch.mv`` linears and
+    head, ``qwen_explicit.py:1247-1272``, ``:952-960``) over the general layer
+    (``:1211-1244``).  On CUDA these reach cuBLAS GEMV / GEMM and torch's fused
+    SDPA, each with its own summation order.
     """
+    want = gold["tokens"].tolist()
+    kv, pc = m.new_kv(1, 4096), m.rope(4096)
+    with torch.inference_mode():
+        hidden = qo.stack_forward(m, qo.embed(m, gold["prompt"].to(DEV)), kv, pc)
+        head = (lambda h: int(qo.greedy_logits_vector(m, h).argmax())) if vector else \
+            (lambda h: int(qo.greedy_token(m, h)[0]))
+        got = [head(hidden)]
+        for step in range(1, len(want)):
+            ids = torch.tensor([[want[step - 1]]], device=DEV)
+            hidden = qo.decode_step_vector(m, ids, kv, pc) if vector else \
+                qo.stack_forward(m, qo.embed(m, ids), kv, pc)
+            got.append(head(hidden))
+    return got
+
+
+@pytest.fixture(scope="module")
+def cfg2_reference_paths(golden_dir):
+    """Teacher-forced 64-token streams of the reference's own arithmetic through
+    its different code paths: the fixture (its CPU decode driver), its general
+    layer on the CPU and its decode driver with one ulp of noise in a few
+    attention outputs (``stream_4b_paths.json``, made by
+    ``tests/golden/make_stream_paths.py``), and the oracle's restatement of both
+    paths run by torch on this GPU."""
+    import json
+
     gold = _gold(golden_dir, "stream_4b.pt")
+    paths = json.loads((golden_dir / "stream_4b_paths.json").read_text())
+    assert paths["fixture_tokens"] == gold["tokens"].tolist()
+    assert paths["oracle_vector_path_mismatches"] == [], "oracle must reproduce the reference's decode stream"
     g = QWEN3_4B
     t = synth.synth_checkpoint(g, 1, device=DEV)
     for k, v in gold["weights_sample"].items():
         assert synth.tensor_digest(t[k]) == v, k
-    rt = materialize_from_tensors(g, t, device=DEV, free_source=True)
-    del t
+    m = qo.OracleModel.from_checkpoint(g, t)
+    want = gold["tokens"].tolist()
+    streams = {
+        "reference general layer, CPU": paths["reference_general_path_tokens"],
+        **{f"reference decode driver, CPU, 1-ulp noise in {f} of attention outputs": toks
+           for f, toks in paths["attention_noise_tokens"].items()},
+        "reference torch path on this GPU, general layer": _oracle_stream_on_device(m, gold, vector=False),
+        "reference torch path on this GPU, vector decode": _oracle_stream_on_device(m, gold, vector=True),
+    }
+    del m
+    mism = {k: [i for i, (a, b) in enumerate(zip(v, want)) if a != b] for k, v in streams.items()}
+    return gold, t, mism
+
+
+@pytest.mark.parametrize("backend", ["cuda_core", "tc", "persistent"])
+def test_cfg2_4b_greedy_stream_teacher_forced(cfg2_reference_paths, backend):
+    """First 64 greedy tokens of random-init Qwen3-4B vs the reference (BASELINE config 2).
+
+    Teacher forcing: every step consumes the reference's previous token, so one
+    disagreement cannot cascade.  The fixture's logits hold exact bf16 ties
+    (top-2 margin 0 at steps 16, 23, 28, 30) and 1-2 ulp gaps at a dozen more
+    steps, and the 36 random layers amplify any one-ulp difference: the
+    reference's own arithmetic, run through its general layer instead of its
+    decode driver's ``mv`` form (same rounding points, another fp32 summation
+    order), by torch on this GPU, or with the last bit of one attention output
+    in ten thousand flipped, decides 3 to 8 of these steps differently, all
+    at top-2 gaps of at most 3 ulps.  So the bar measured here: every step
+    where this engine differs has a reference top-2 gap no larger than the
+    largest gap the reference's own variants flipped, and this engine differs
+    at no more steps than the most any of those variants does.
+    """
+    gold, t, ref_mism = cfg2_reference_paths
+    g = QWEN3_4B
+    rt = materialize_from_tensors(g, t, device=DEV)
     want = gold["tokens"].tolist()
     margins = gold["margins"].tolist()
     eng = DecodeEngine(rt, batch_size=1, max_seq_len=4096, linear_backend=backend)
@@ -217,12 +318,16 @@ def test_cfg2_4b_greedy_stream_teacher_forced(golden_dir, backend):
         eng.decode_step()
         got.append(int(eng.current_ids[0]))
     mism = [i for i, (a, b) in enumerate(zip(got, want)) if a != b]
-    free = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), len(want))
-    print(f"cfg2[{backend}] teacher-forced mismatches at {mism} (margins {[margins[i] for i in mism]}); "
-          f"first mismatch at step {free}")
+    for name, steps in ref_mism.items():
+        print(f"cfg2 {name}: teacher-forced mismatches at {steps}")
+    print(f"cfg2 engine[{backend}]: teacher-forced mismatches at {mism} "
+          f"(reference margins {[margins[i] for i in mism]})")
+    # the largest top-2 gap, and the most steps, that the reference's own variants flipped
+    gap = max(margins[i] for v in ref_mism.values() for i in v)
     for i in mism:
-        assert margins[i] <= NEAR_TIE, f"step {i}: mismatch with reference margin {margins[i]}"
-    assert len(mism) <= 8
+        assert margins[i] <= gap, f"step {i}: mismatch with reference margin {margins[i]} > {gap}"
+    assert len(mism) <= max(len(v) for v in ref_mism.values())
+    del eng, rt
 
 
 def test_prefill_full_matches_chunked_prefill():

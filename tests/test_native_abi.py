@@ -14,9 +14,21 @@ from leanstack_b200 import _native as nat
 HEADER = Path(__file__).resolve().parents[1] / "include" / "leanb200.h"
 
 
-def declared_symbols() -> list[str]:
-    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+def _declared(text: str) -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(ls_\w+)\s*\(", text, flags=re.M)))
+
+
+def _split_header() -> tuple[str, str]:
+    """(release part, LEANB200_PROFILING part) of the header."""
+    text = HEADER.read_text()
+    start = text.index("#ifdef LEANB200_PROFILING")
+    end = text.index("#endif /* LEANB200_PROFILING */")
+    return text[:start] + text[end:], text[start:end]
+
+
+def declared_symbols() -> list[str]:
+    return _declared(_split_header()[0])
 
 
 @pytest.fixture(scope="module")
@@ -39,6 +51,18 @@ def test_library_exports_every_declared_symbol(lib):
     for name in declared_symbols():
         assert hasattr(lib, name), f"{name} declared in leanb200.h but not exported"
     assert set(declared_symbols()) <= set(nat.exported_symbols()), "ctypes signature table is incomplete"
+
+
+def test_release_library_has_no_measurement_hooks(lib):
+    """The per-CTA trace hooks and the NVLink probe exist only in a library built
+    with LEANB200_PROFILING; the default build exports none of them."""
+    hooks = _declared(_split_header()[1])
+    assert set(hooks) == set(nat.PROFILING_SIGNATURES)
+    stamp = nat.LIB_PATH.parent / "build_flags.txt"
+    if stamp.exists() and "LEANB200_PROFILING" in stamp.read_text():
+        pytest.skip("library built with --profiling")
+    for name in hooks:
+        assert not hasattr(lib, name), f"{name} exported by the release library"
 
 
 def test_version_and_argument_errors_without_gpu(lib):

@@ -79,6 +79,43 @@ def test_oracle_cfg1_decode_layer_bit_exact(golden_dir):
     kv.set_all(past)
     y = qo.layer_forward(m, 0, w, x, kv, cos, sin, None)
     assert torch.equal(y.reshape(-1), c["out"])
+    # the decode driver's mv form of the same layer
+    kv.set_all(past)
+    yv = qo.decode_layer_vector(m, 0, w, x, kv, cos, sin)
+    assert torch.equal(yv.reshape(-1), c["out"])
+
+
+def test_stream_paths_record(golden_dir):
+    """``stream_4b_paths.json`` (made by ``tests/golden/make_stream_paths.py``
+    from the reference itself): the oracle's restatement of the decode driver
+    reproduced all 64 teacher-forced tokens of the reference's config-2 stream;
+    the reference's own general layer, which differs only in the order of its
+    linears' fp32 sums, decided six of them differently (each at a top-2 gap
+    of at most 2 bf16 ulps), and one flipped bit in 1e-2 .. 1e-4 of the
+    attention outputs flips four to eight (each at a gap of at most 3 ulps)."""
+    import json
+
+    gold = _load(golden_dir, "stream_4b.pt")
+    paths = json.loads((golden_dir / "stream_4b_paths.json").read_text())
+    want = gold["tokens"].tolist()
+    assert paths["fixture_tokens"] == want
+    assert paths["oracle_vector_path_tokens"] == want
+    gen = paths["reference_general_path_tokens"]
+    mism = [i for i, (a, b) in enumerate(zip(gen, want)) if a != b]
+    assert mism == paths["reference_general_path_mismatches"] == [16, 23, 30, 46, 53, 54]
+    margins = gold["margins"].tolist()
+    assert all(margins[i] <= 2 * 2 ** -5 for i in mism)
+    # the disagreeing token is one of the reference's top two each time
+    top5 = gold["top5"]
+    assert all(gen[i] in (int(top5[i][1][0]), int(top5[i][1][1])) for i in mism)
+    # one ulp of noise in 1e-2 .. 1e-4 of the attention outputs flips only near-tie
+    # steps too (top-2 gap at most 3 bf16 ulps at the logits' magnitude, 4 .. 8)
+    noise = paths["attention_noise_mismatches"]
+    assert set(noise) == {f"{p} {f}" for p in ("vector", "general") for f in ("0.01", "0.001", "0.0001")}
+    for f, toks in paths["attention_noise_tokens"].items():
+        steps = [i for i, (a, b) in enumerate(zip(toks, want)) if a != b]
+        assert steps == noise[f] and 0 < len(steps) <= 10
+        assert all(margins[i] <= 3 * 2 ** -5 for i in steps)
 
 
 def test_oracle_verify_and_prefill_layer_bit_exact(golden_dir):

@@ -50,6 +50,16 @@ def test_noalloc_head_matches_workspace_head(m):
     assert K.device_error() == 0
 
 
+def test_noalloc_scratch_limit_arithmetic():
+    """The fixed scratch (16 KiB) holds the head's workspace for every m the entry
+    point accepts (1..8) on this GPU; the workspace arithmetic it checks against
+    grows past the limit for larger m, where the workspace form still works."""
+    limit = 16 * 1024
+    for m in range(1, 9):
+        assert K.lmhead_workspace_bytes(m, 151936) <= limit
+    assert K.lmhead_workspace_bytes(16, 151936) > limit
+
+
 def test_noalloc_rejects_rows_beyond_limit():
     dev = torch.device("cuda:0")
     h = torch.zeros(9, 256, device=dev, dtype=torch.bfloat16)
