@@ -62,7 +62,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
     ap.add_argument("--e2e-steps", type=int, default=64)
-    ap.add_argument("--linear-backend", choices=("auto", "persistent", "tc", "cuda_core"), default="auto",
+    ap.add_argument("--linear-backend", choices=("auto", "tc", "cuda_core"), default="auto",
                     help="tensor-core (tcgen05) or CUDA-core streaming linears for the decode step")
     ap.add_argument("--parallel", choices=("tp", "replicas"), default="tp",
                     help="with N > 1 GPUs: tensor parallelism (one sequence) or independent replicas")
@@ -668,7 +668,7 @@ def run_ours(args, world, rank, local):
             "config": {**bench_config(), "global_batch": seqs},
             "parallelism": (f"tp{world}" + ("" if args.allreduce == "nccl" else " fused-allreduce")
                             if tp_mode else f"replicas x{world}") if world > 1 else "single GPU",
-            "linear_backend": "persistent" if eng.persistent else eng.backend,
+            "linear_backend": eng.backend,
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
             "gpu_launches": args.steps * eng.kernel_launches_per_step(),
         }

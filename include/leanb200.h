@@ -261,44 +261,6 @@ int ls_gemm_bf16_tcgen05(const void* x, int64_t m, int64_t k, const void* w, int
                          ls_stream_t stream);
 int ls_gemm_bf16_tcgen05_workspace_bytes(int64_t m, int64_t k, int64_t n, int epilogue, int64_t* bytes);
 
-/*
- * Weights and cache of one decoder layer for ls_decode_step (device pointers,
- * the layouts of the table at the top of this header; caches are the layer's
- * [Hkv, max_seq, D] slices of a batch-1 arena).
- */
-typedef struct ls_decode_layer {
-  const void* input_norm_w;
-  const void* qkv_w;
-  const void* q_norm_w;
-  const void* k_norm_w;
-  const void* o_w;
-  const void* post_norm_w;
-  const void* gate_up_w;
-  const void* down_w;
-  void* k_cache;
-  void* v_cache;
-} ls_decode_layer;
-
-/*
- * One whole batch-1 decode step as one persistent cooperative kernel: the
- * embedding of ids[0], every layer (input norm, fused QKV, q/k norm, RoPE, KV
- * append at cache_pos[0], attention, o_proj + residual, post norm, gate_up +
- * SiLU*up, down + residual), the final norm, lm_head and argmax.  Writes the
- * next token to ids[0] and advances cache_pos[0]; so consecutive launches (or
- * graph replays) decode autoregressively.  This is the reference's
- * run_semantic_stack_decode + select_semantic_greedy_token
- * (src/leanstack/runtime/qwen_explicit.py:1617-1644, :1814-1832) for batch 1.
- *   layers      device array of num_layers ls_decode_layer
- *   x, h, qkv, attn, act   activation arenas ([H], [H], [(Hq+2Hkv) D], [Hq D], [I])
- *   workspace   ls_decode_step_workspace_bytes() bytes, zero-filled once
- */
-int ls_decode_step(const ls_decode_layer* layers, int64_t num_layers, int64_t hidden, int64_t intermediate,
-                   int64_t num_heads, int64_t num_kv_heads, int64_t head_dim, int64_t vocab, int64_t max_seq,
-                   float eps, const void* embed, const void* final_norm_w, const void* lm_head_w,
-                   const void* rope_cos, const void* rope_sin, int64_t* ids, int32_t* cache_pos, void* x, void* h,
-                   void* qkv, void* attn, void* act, void* workspace, int64_t workspace_bytes, ls_stream_t stream);
-int ls_decode_step_workspace_bytes(int64_t num_kv_heads, int64_t* bytes);
-
 /* Fused one-shot all-reduce over NVLink peer memory (no counterpart in the
  * reference, which runs on one GPU; it replaces the NCCL all-reduce of the
  * tensor-parallel row-split o_proj / down_proj, whose reference-side linear +
@@ -373,10 +335,6 @@ int ls_spec_accept(int64_t* ids, const int64_t* verdict, int64_t batch, int64_t 
  * waits.  times_dev (device, 2 x u64): total ns, and 1 if a wait gave up. */
 int ls_p2p_pingpong(void* my_flag, void* peer_flag, int rank, int iters, unsigned long long* times_dev,
                     ls_stream_t stream);
-/* Profiling hook of ls_decode_step: with a non-NULL device buffer of
- * (barriers per step) x grid x 2 u64, each barrier records every CTA's arrival
- * and release time (globaltimer ns).  NULL turns it off. */
-int ls_decode_step_set_trace(void* buffer);
 /* Profiling hook of ls_linear_bf16 and the fused head / all-reduce forms: with a
  * non-NULL device buffer of grid x 5 u64, every launch records per CTA the
  * globaltimer at start, after the PDL wait, after the activation prologue,

@@ -94,9 +94,6 @@ SIGNATURES: dict[str, list] = {
                                  _p, _i64, _p, _p, _p, _p],
     "ls_argmax_rows": [_p, _i64, _i64, _p, _p, _i64, _p],
     "ls_argmax_rows_workspace_bytes": [_i64, _i64, ctypes.POINTER(_i64)],
-    "ls_decode_step": [_p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _p, _p, _p, _p, _p, _p, _p, _p,
-                       _p, _p, _p, _p, _i64, _p],
-    "ls_decode_step_workspace_bytes": [_i64, ctypes.POINTER(_i64)],
     "ls_gemm_bf16_tcgen05": [_p, _i64, _i64, _p, _i64, _int, _p, _p, _p, _i64, _p],
     "ls_gemm_bf16_tcgen05_workspace_bytes": [_i64, _i64, _i64, _int, ctypes.POINTER(_i64)],
     "ls_advance_cursors": [_p, _p, _i64, _i64, _p],
@@ -104,7 +101,6 @@ SIGNATURES: dict[str, list] = {
 _RESTYPES = {"ls_last_error": ctypes.c_char_p}
 # Measurement hooks, present only in a library built with --profiling (LEANB200_PROFILING).
 PROFILING_SIGNATURES: dict[str, list] = {
-    "ls_decode_step_set_trace": [_p],
     "ls_linear_set_trace": [_p],
     "ls_gemm_tc_set_trace": [_p],
     "ls_p2p_pingpong": [_p, _p, ctypes.c_int, ctypes.c_int, _p, _p],

@@ -266,13 +266,6 @@ int launch_gemm_big(const void* x, int64_t m, int64_t k, const void* w, int64_t 
                     void* out, cudaStream_t stream);
 int launch_tc_tile(const void* w, int64_t n_rows, int64_t k, int silu, void* out, cudaStream_t stream);
 
-int decode_step_workspace_bytes(int64_t hkv, int64_t* bytes);
-int decode_step(const void* layers, int64_t L, int64_t H, int64_t I, int64_t hq, int64_t hkv, int64_t head_dim,
-                int64_t vocab, int64_t max_seq, float eps, const void* embed, const void* final_norm,
-                const void* lm_head, const void* cos, const void* sin, int64_t* ids, int32_t* cache_pos, void* x,
-                void* h, void* qkv, void* attn, void* act, void* workspace, int64_t workspace_bytes,
-                cudaStream_t stream);
-
 }  // namespace lsb_host
 
 using namespace lsb_host;
@@ -617,29 +610,7 @@ int ls_argmax_keys_to_ids(const int64_t* keys, int64_t m, int64_t* out_ids, ls_s
   return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "argmax_keys_to_ids launch: %s", cudaGetErrorString(e));
 }
 
-int ls_decode_step_workspace_bytes(int64_t num_kv_heads, int64_t* bytes) {
-  LS_REQUIRE(bytes && num_kv_heads > 0, LS_ERR_INVALID_ARGUMENT, "ls_decode_step_workspace_bytes: bad arguments");
-  return decode_step_workspace_bytes(num_kv_heads, bytes);
-}
 
-int ls_decode_step(const ls_decode_layer* layers, int64_t num_layers, int64_t hidden, int64_t intermediate,
-                   int64_t num_heads, int64_t num_kv_heads, int64_t head_dim, int64_t vocab, int64_t max_seq,
-                   float eps, const void* embed, const void* final_norm_w, const void* lm_head_w,
-                   const void* rope_cos, const void* rope_sin, int64_t* ids, int32_t* cache_pos, void* x, void* h,
-                   void* qkv, void* attn, void* act, void* workspace, int64_t workspace_bytes, ls_stream_t stream) {
-  LS_REQUIRE(layers && embed && final_norm_w && lm_head_w && rope_cos && rope_sin && ids && cache_pos && x && h &&
-                 qkv && attn && act,
-             LS_ERR_INVALID_ARGUMENT, "ls_decode_step: null pointer");
-  LS_REQUIRE(num_layers > 0 && hidden > 0 && intermediate > 0 && num_heads > 0 && num_kv_heads > 0 && vocab > 0 &&
-                 max_seq > 0,
-             LS_ERR_INVALID_ARGUMENT, "ls_decode_step: bad sizes");
-  LS_REQUIRE(aligned16(embed) && aligned16(lm_head_w) && aligned16(x) && aligned16(h) && aligned16(qkv) &&
-                 aligned16(attn) && aligned16(act),
-             LS_ERR_MISALIGNED, "ls_decode_step: pointers must be 16-byte aligned");
-  return decode_step(layers, num_layers, hidden, intermediate, num_heads, num_kv_heads, head_dim, vocab, max_seq, eps,
-                     embed, final_norm_w, lm_head_w, rope_cos, rope_sin, ids, cache_pos, x, h, qkv, attn, act,
-                     workspace, workspace_bytes, (cudaStream_t)stream);
-}
 
 int ls_residual_add_f32(const void* residual, const float* y, int64_t n, void* out, ls_stream_t stream) {
   LS_REQUIRE(residual && y && out && n > 0, LS_ERR_INVALID_ARGUMENT, "ls_residual_add_f32: bad arguments");

@@ -30,19 +30,15 @@ from .tp import TPComm, TPShard
 
 SMALL_M = 8      # largest token count of the CUDA-core linear kernels
 TC_MAX_M = 128   # largest token count of one tcgen05 GEMM launch
-BACKENDS = ("auto", "persistent", "tc", "cuda_core")
+BACKENDS = ("auto", "tc", "cuda_core")
 
 
 def resolve_backend(backend: str, batch_size: int) -> str:
     """``auto``: tensor cores from 3 sequences on, CUDA-core streaming below.
 
-    ``persistent`` (batch 1 only) runs each decode step as one cooperative
-    kernel (``ls_decode_step``) and the prefill on the tensor cores.
     """
     if backend not in BACKENDS:
         raise ValueError(f"unknown linear backend {backend!r}; choose from {BACKENDS}")
-    if backend == "persistent" and batch_size != 1:
-        raise ValueError("the persistent decode step handles batch 1 only")
     if backend == "auto":
         return "tc" if batch_size >= 3 else "cuda_core"
     return backend
@@ -61,11 +57,6 @@ class DecodeEngine:
         self.vocab_offset = shard.vocab_offset if self.tp is not None else 0
         self.vocab_rows = runtime.lm_head_weight.shape[0]
         self.backend = resolve_backend(linear_backend, batch_size)
-        if self.tp is not None and self.backend == "persistent":
-            raise ValueError("the persistent decode step runs on one GPU only")
-        self.persistent = self.backend == "persistent"
-        if self.persistent:
-            self.backend = "tc"  # prefill path; decode steps use the persistent kernel
         limit = TC_MAX_M if self.backend == "tc" else SMALL_M
         if batch_size < 1 or batch_size > limit:
             raise ValueError(f"batch_size {batch_size}: the {self.backend} step handles 1..{limit} sequences")
@@ -117,18 +108,6 @@ class DecodeEngine:
         self.tc_tiles = tc_tiles
         self.use_graph = use_graph
         self.graph: torch.cuda.CUDAGraph | None = None
-        if self.persistent:
-            rows = []
-            for li, layer in enumerate(runtime.layers):
-                att, mlp = layer.attention, layer.mlp
-                rows.append([layer.input_layernorm_weight.data_ptr(), att.qkv_proj_weight.data_ptr(),
-                             att.q_norm_weight.data_ptr(), att.k_norm_weight.data_ptr(), att.o_proj_weight.data_ptr(),
-                             layer.post_attention_layernorm_weight.data_ptr(), mlp.gate_up_proj_weight.data_ptr(),
-                             mlp.down_proj_weight.data_ptr(), self.kv.key_cache[li].data_ptr(),
-                             self.kv.value_cache[li].data_ptr()])
-            self.layer_table = torch.tensor(rows, dtype=torch.int64, device=dev)
-            self.ds_ws = torch.zeros(K.decode_step_workspace_bytes(g.num_key_value_heads), device=dev,
-                                     dtype=torch.uint8)
 
     # ------------------------------------------------------------------
     def _forward(self, q_len: int, head, advance: bool = True) -> None:
@@ -317,18 +296,8 @@ class DecodeEngine:
     def set_next_ids(self, ids: torch.Tensor) -> None:
         self.arenas.ids[:self.B].copy_(ids.reshape(-1).to(self.arenas.ids.device))
 
-    def _persistent_step(self) -> None:
-        g, a, rt = self.g, self.arenas, self.rt
-        K.decode_step(self.layer_table, len(rt.layers), g.hidden_size, g.intermediate_size, g.num_attention_heads,
-                      g.num_key_value_heads, g.head_dim, g.vocab_size, self.S, g.rms_norm_eps, rt.embed_tokens_weight,
-                      rt.final_norm_weight, rt.lm_head_weight, self.cos, self.sin, a.ids[:1], self.kv.cache_pos,
-                      a.x[:1], a.h[:1], a.qkv[:1], a.attn[:1], a.act[:1], self.ds_ws)
-
     def _decode_once(self) -> None:
-        if self.persistent:
-            self._persistent_step()
-        else:
-            self._forward(1, head=True)
+        self._forward(1, head=True)
 
     def capture(self) -> None:
         """Capture one decode step (q_len 1 + head + cursor advance) as a CUDA graph."""
@@ -438,8 +407,6 @@ class DecodeEngine:
 
     def kernel_launches_per_step(self) -> int:
         """Kernels one decode step launches (embedding, layers, head, cursor advance)."""
-        if self.persistent:
-            return 1
         per_layer = 8 if self.backend == "tc" else 6
         head = 3 if self.backend == "tc" else 1
         if self.tp is not None:  # + residual-add after each row-split linear, + keys-to-ids

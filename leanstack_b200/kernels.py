@@ -352,31 +352,6 @@ def gemm_tc(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = EPI_STORE, resi
     return out
 
 
-def decode_step_workspace_bytes(num_kv_heads: int) -> int:
-    v = ctypes.c_int64(0)
-    nat.call("ls_decode_step_workspace_bytes", num_kv_heads, ctypes.byref(v))
-    return v.value
-
-
-def decode_step(layer_table: torch.Tensor, num_layers: int, hidden: int, intermediate: int, num_heads: int,
-                num_kv_heads: int, head_dim: int, vocab: int, max_seq: int, eps: float, embed: torch.Tensor,
-                final_norm_w: torch.Tensor, lm_head_w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
-                ids: torch.Tensor, cache_pos: torch.Tensor, x: torch.Tensor, h: torch.Tensor, qkv: torch.Tensor,
-                attn: torch.Tensor, act: torch.Tensor, workspace: torch.Tensor) -> None:
-    """One batch-1 decode step as one persistent kernel (``ls_decode_step``).
-
-    ``layer_table`` is an int64 CUDA tensor ``[num_layers, 10]`` of device
-    pointers laid out as ``ls_decode_layer``.
-    """
-    _check(layer_table, "layer_table", torch.int64)
-    _check(ids, "ids", torch.int64)
-    _check(cache_pos, "cache_pos", torch.int32)
-    nat.call("ls_decode_step", layer_table.data_ptr(), num_layers, hidden, intermediate, num_heads, num_kv_heads,
-             head_dim, vocab, max_seq, float(eps), embed.data_ptr(), final_norm_w.data_ptr(), lm_head_w.data_ptr(),
-             cos.data_ptr(), sin.data_ptr(), ids.data_ptr(), cache_pos.data_ptr(), x.data_ptr(), h.data_ptr(),
-             qkv.data_ptr(), attn.data_ptr(), act.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
-
-
 def gemm_big(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,
              out: torch.Tensor | None = None) -> torch.Tensor:
     """Large-M tcgen05 GEMM (prefill): ``out = epilogue(x @ w.T)`` for x ``[m, k]`` with m in the thousands."""

@@ -58,7 +58,6 @@ def main(argv=None) -> int:
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--seq", type=int, default=600, help="cached positions for attention")
     ap.add_argument("--copies", type=int, default=4)
-    ap.add_argument("--layers", type=int, default=2, help="layers of the persistent-step case")
     ap.add_argument("--batch", type=int, default=1, help="sequences of the prefill_attn case")
     args = ap.parse_args(argv)
     g = QWEN3_4B
@@ -195,28 +194,6 @@ def main(argv=None) -> int:
         yr = torch.empty_like(xr)
         t = _time(lambda i: K.rmsnorm(xr, nw, 1e-6, out=yr), args.reps)
         out["rmsnorm"] = (t, 2 * m * H * 2)
-    if "persistent" in wanted:
-        from leanstack_b200.engine import DecodeEngine
-        from leanstack_b200.leanserve import materialize_from_tensors
-        from dataclasses import replace
-
-        geo = replace(g, num_hidden_layers=args.layers)
-        rt = materialize_from_tensors(geo, synth.synth_checkpoint(geo, 1, device=dev), device=dev, free_source=True)
-        eng = DecodeEngine(rt, batch_size=1, max_seq_len=4096, linear_backend="persistent")
-        eng.prefill(synth.token_ids((1, args.seq), geo.vocab_size, 1, "mb/prompt"))
-        eng.capture()
-        step_bytes = args.layers * g.layer_weight_bytes() + g.lm_head_bytes() + args.seq * 2 * g.kv_dim * 2 * args.layers
-
-        for _ in range(3):
-            eng.graph.replay()
-        torch.cuda.synchronize()
-        a0, a1 = _events()
-        a0.record()
-        for _ in range(args.reps):
-            eng.graph.replay()
-        a1.record()
-        torch.cuda.synchronize()
-        out[f"persistent_step(layers={args.layers})"] = (a0.elapsed_time(a1) / 1000.0 / args.reps, step_bytes)
     for name, (t, nbytes) in out.items():
         if name.startswith("big_"):
             print(json.dumps({"kernel": name, "m": m, "us": round(t * 1e6, 2), "flops": nbytes,
