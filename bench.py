@@ -299,9 +299,9 @@ def _timed(fn, steps: int, warmup: int, world: int) -> float:
 def run_layer_linears(rt, eng, peaks) -> dict:
     """BASELINE config 1's per-linear figures: each decode linear at M = 1 (the
     engine's CUDA-core kernels with their fused prologues / epilogues), timed
-    with CUDA events over launches that walk the 36 resident layers, so every
-    launch streams its own weights from HBM.  GB/s = (weight + input + output
-    bytes) / time."""
+    with CUDA events over a CUDA graph of launches that walk the 36 resident
+    layers, so every launch streams its own weights from HBM and no host
+    launch cost sits between them.  GB/s = (weight + input + output bytes) / time."""
     from leanstack_b200 import kernels as K
 
     g = QWEN3_4B
@@ -330,18 +330,31 @@ def run_layer_linears(rt, eng, peaks) -> dict:
     }
     out = {}
     for name, (fn, nbytes, n_layers) in cases.items():
-        reps = 4 if n_layers > 1 else 24
+        # launches over n_layers distinct layers captured in one CUDA graph, as
+        # in the decode step: no host launch cost between them
+        laps = 1 if n_layers > 1 else 8
         for L in rt.layers[:2]:
             fn(L)
         torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(laps):
+                for L in rt.layers[:n_layers]:
+                    fn(L)
+        torch.cuda.current_stream().wait_stream(side)
+        graph.replay()
+        torch.cuda.synchronize()
+        reps = 4
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(reps):
-            for L in rt.layers[:n_layers]:
-                fn(L)
+            graph.replay()
         e1.record()
         torch.cuda.synchronize()
-        per = e0.elapsed_time(e1) / 1000.0 / (reps * n_layers)
+        del graph
+        per = e0.elapsed_time(e1) / 1000.0 / (reps * laps * n_layers)
         out[name] = {"us": per * 1e6, "bytes": nbytes, "gbs": nbytes / per / 1e9,
                      "hbm_frac": nbytes / per / 1e9 / peaks["hbm_gbs"]}
     return out

@@ -266,12 +266,14 @@ int ls_gemm_bf16_tcgen05_workspace_bytes(int64_t m, int64_t k, int64_t n, int ep
  * tensor-parallel row-split o_proj / down_proj, whose reference-side linear +
  * residual is src/leanstack/runtime/qwen_explicit.py:1262 and :819-829).
  * out = bf16(residual + bf16(sum over ranks of W_r x_r)), m <= 8 rows: each CTA
- * computes its slice of the fp32 partial, stores it into every rank's region
- * (plain peer stores), raises its flag on every rank (release, system scope),
- * waits for the same CTA of every rank (acquire; gives up after ~2 s with
- * LS_ERR_TIMEOUT in the device error flag) and sums the partials in rank
- * order, so every rank holds the same bits.  All ranks must issue the same
- * sequence of these calls with the same m, and each rank must own its GPU. */
+ * computes its slice of the fp32 partial and stores every value into every
+ * rank's region together with the CTA's call number (one 8-byte plain peer
+ * store per value and rank, no multicast), then polls its own elements until
+ * every rank's call number matches (bounded by the wait limit, then
+ * LS_ERR_TIMEOUT in the device error flag) and sums in rank order, so every
+ * rank holds the same bits.  All ranks must issue the same sequence of these
+ * calls with the same m, and each rank must own its GPU.  Regions hold up to
+ * 128 rows. */
 int ls_p2p_region_bytes(int64_t max_rows, int64_t width, int64_t max_ctas, int64_t* bytes);
 int ls_p2p_alloc(int64_t bytes, void** region);   /* cudaMalloc + zero, at set-up */
 int ls_p2p_free(void* region);
@@ -280,6 +282,16 @@ int ls_ipc_open(const void* handle64, void** region);
 int ls_ipc_close(void* region);
 int ls_linear_allreduce_residual(const void* x, int64_t m, int64_t k, const void* w, int64_t n,
                                  const void* residual, void* out, const ls_p2p_exchange* ex, ls_stream_t stream);
+/* The same one-shot all-reduce for partials another kernel wrote: part is the
+ * fp32 [m, n] partial of this rank's row-split linear (the tcgen05 GEMM's
+ * LS_EPI_STORE_F32 output, 1 <= m <= ex->max_rows), out = bf16(residual +
+ * bf16(sum over ranks in rank order)).  Replaces an NCCL all-reduce of the
+ * partials plus ls_residual_add_f32 (the reference's o_proj / down residual,
+ * src/leanstack/runtime/qwen_explicit.py:819-829).  Fixed grid of 128 CTAs:
+ * use an exchange of its own (not shared with ls_linear_allreduce_residual),
+ * with max_ctas >= 128. */
+int ls_allreduce_residual_f32(const float* part, int64_t m, int64_t n, const void* residual, void* out,
+                              const ls_p2p_exchange* ex, ls_stream_t stream);
 
 /* Tensor-parallel greedy head.  Each rank holds a vocab shard (rows
  * [vocab_offset, vocab_offset + vocab_rows) of lm_head) and writes, per row, an

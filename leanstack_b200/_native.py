@@ -87,6 +87,7 @@ SIGNATURES: dict[str, list] = {
     "ls_ipc_open": [_p, _p],
     "ls_ipc_close": [_p],
     "ls_linear_allreduce_residual": [_p, _i64, _i64, _p, _i64, _p, _p, _p, _p],
+    "ls_allreduce_residual_f32": [_p, _i64, _i64, _p, _p, _p, _p],
     "ls_lmhead_argmax_keys": [_p, _i64, _i64, _p, _f32, _p, _i64, _i64, _p, _p, _i64, _p],
     "ls_argmax_rows_keys": [_p, _i64, _i64, _i64, _p, _p, _i64, _p],
     "ls_argmax_keys_to_ids": [_p, _i64, _p, _p],

@@ -1,8 +1,9 @@
 // Set-up of the fused tensor-parallel all-reduce: exchange regions in device
 // memory, shared between the ranks' processes through CUDA IPC handles (plain
-// peer mappings over NVLink; no multicast objects), and the C entry point of
-// the row-split linear whose epilogue performs the all-reduce
-// (linear_small_m.cu, EPI_AR_RESIDUAL).
+// peer mappings over NVLink; no multicast objects), the C entry point of the
+// row-split linear whose epilogue performs the all-reduce (linear_small_m.cu,
+// EPI_AR_RESIDUAL), and the standalone one-shot all-reduce + residual of the
+// fp32 partials that the tensor-core row-split linears write.
 #include "common.cuh"
 
 namespace lsb_host {
@@ -33,7 +34,96 @@ __global__ void p2p_pingpong_kernel(uint32_t* mine, uint32_t* peer, int rank, in
 }  // namespace lsb
 #endif  // LEANB200_PROFILING
 
+namespace lsb {
+
+// One-shot all-reduce of a row-split linear's fp32 partials, fused with the
+// residual epilogue: out = bf16(residual + bf16(sum over ranks in rank order)).
+// Every element travels to every rank together with the call number in one
+// 8-byte store; a reader polls its elements until all ranks' call numbers
+// match (no flag, fence or barrier between push and sum).  The grid is fixed
+// (kArGrid CTAs, each with its own call counter in the region), so every
+// CTA's counter equals the number of calls made so far on every rank, and the
+// element -> CTA map may change with m without any reader seeing a stale
+// element of an older call as current.
+constexpr int kArThreads = 256;
+constexpr int kArGrid = 128;
+
+__global__ void __launch_bounds__(kArThreads) allreduce_residual_kernel(const float* part,
+                                                                       const __nv_bfloat16* residual,
+                                                                       __nv_bfloat16* out, int M, int N,
+                                                                       P2PExchange ex, int* err) {
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_abort;
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    uint32_t* ctr = reinterpret_cast<uint32_t*>(ex.peer[ex.rank] + p2p_ctr_offset(ex.max_ctas)) + blockIdx.x;
+    s_epoch = *ctr + 1u;
+    *ctr = s_epoch;
+    s_abort = 0;
+  }
+  grid_dep_wait();  // the partials come from the previous kernel
+  __syncthreads();
+  grid_dep_launch();
+  const uint32_t epoch = s_epoch;
+  const size_t slot_base = (size_t)(epoch & 1u) * LS_MAX_TP_RANKS * ex.max_rows * ex.width;
+  const size_t recv_off = p2p_recv_offset(ex.max_ctas);
+  const int total = M * N;
+  const int stride = gridDim.x * kArThreads;
+  for (int i = blockIdx.x * kArThreads + tid; i < total; i += stride) {
+    const int m = i / N, n = i - m * N;
+    const float v = part[i];
+    const size_t off = slot_base + ((size_t)ex.rank * ex.max_rows + m) * ex.width + n;
+    for (int q = 0; q < ex.world; ++q)
+      st_pair_sys(reinterpret_cast<uint2*>(ex.peer[q] + recv_off) + off, __float_as_uint(v), epoch);
+  }
+  const uint2* recv = reinterpret_cast<const uint2*>(ex.peer[ex.rank] + recv_off) + slot_base;
+  const WaitClock clk(err);
+  for (int i = blockIdx.x * kArThreads + tid; i < total; i += stride) {
+    const int m = i / N, n = i - m * N;
+    float y = 0.f;
+    for (int q = 0; q < ex.world; ++q) {
+      const uint2* src = recv + ((size_t)q * ex.max_rows + m) * ex.width + n;
+      uint2 v = ld_pair_sys(src);
+      while (v.y != epoch) {  // bounded: one limit per CTA, then every thread gives up
+        if (*reinterpret_cast<volatile int*>(&s_abort)) break;
+        if (clk.expired()) {
+          raise_device_error(err, LS_ERR_TIMEOUT | (0x31 << 8));
+          s_abort = 1;
+          break;
+        }
+        v = ld_pair_sys(src);
+      }
+      y += __uint_as_float(v.x);
+    }
+    out[i] = f_to_bf16(bf16_to_f(residual[i]) + round_bf16(y));
+  }
+}
+
+}  // namespace lsb
+
 using namespace lsb_host;
+
+namespace {
+int to_exchange(const ls_p2p_exchange* ex, int64_t n, const char* who, lsb::P2PExchange* e) {
+  if (!ex) return set_error(LS_ERR_INVALID_ARGUMENT, "%s: exchange is null", who);
+  if (ex->world < 1 || ex->world > LS_MAX_TP_RANKS || ex->rank < 0 || ex->rank >= ex->world || ex->max_ctas < 1 ||
+      ex->max_rows < 1 || ex->width != n)
+    return set_error(LS_ERR_INVALID_ARGUMENT, "%s: bad exchange description", who);
+  *e = {};
+  for (int q = 0; q < ex->world; ++q) {
+    if (!ex->peer[q] || !aligned16(ex->peer[q]))
+      return set_error(LS_ERR_INVALID_ARGUMENT, "%s: region of rank %d missing", who, q);
+    e->peer[q] = static_cast<unsigned char*>(ex->peer[q]);
+  }
+  e->rank = ex->rank;
+  e->world = ex->world;
+  e->max_ctas = ex->max_ctas;
+  e->max_rows = ex->max_rows;
+  e->width = (int)ex->width;
+  e->trace = ex->trace;
+  return LS_OK;
+}
+}  // namespace
 
 extern "C" {
 
@@ -51,7 +141,7 @@ int ls_p2p_pingpong(void* my_region, void* peer_region, int rank, int iters, uns
 #endif  // LEANB200_PROFILING
 
 int ls_p2p_region_bytes(int64_t max_rows, int64_t width, int64_t max_ctas, int64_t* bytes) {
-  if (!bytes || max_rows < 1 || max_rows > 64 || width < 1 || width > (1 << 20) || max_ctas < 1 ||
+  if (!bytes || max_rows < 1 || max_rows > 128 || width < 1 || width > (1 << 20) || max_ctas < 1 ||
       max_ctas > 4096)
     return set_error(LS_ERR_INVALID_ARGUMENT, "ls_p2p_region_bytes: bad arguments");
   *bytes = (int64_t)lsb::p2p_region_bytes((int)max_ctas, (int)max_rows, (int)width);
@@ -107,23 +197,38 @@ int ls_ipc_close(void* region) {
 
 int ls_linear_allreduce_residual(const void* x, int64_t m, int64_t k, const void* w, int64_t n, const void* residual,
                                  void* out, const ls_p2p_exchange* ex, ls_stream_t stream) {
-  if (!ex) return set_error(LS_ERR_INVALID_ARGUMENT, "ls_linear_allreduce_residual: exchange is null");
-  if (ex->world < 1 || ex->world > LS_MAX_TP_RANKS || ex->rank < 0 || ex->rank >= ex->world || ex->max_ctas < 1 ||
-      ex->max_rows < 1 || ex->width != n)
-    return set_error(LS_ERR_INVALID_ARGUMENT, "ls_linear_allreduce_residual: bad exchange description");
-  lsb::P2PExchange e = {};
-  for (int q = 0; q < ex->world; ++q) {
-    if (!ex->peer[q] || !aligned16(ex->peer[q]))
-      return set_error(LS_ERR_INVALID_ARGUMENT, "ls_linear_allreduce_residual: region of rank %d missing", q);
-    e.peer[q] = static_cast<unsigned char*>(ex->peer[q]);
-  }
-  e.rank = ex->rank;
-  e.world = ex->world;
-  e.max_ctas = ex->max_ctas;
-  e.max_rows = ex->max_rows;
-  e.width = (int)ex->width;
-  e.trace = ex->trace;
+  lsb::P2PExchange e;
+  int rc = to_exchange(ex, n, "ls_linear_allreduce_residual", &e);
+  if (rc) return rc;
   return launch_linear_allreduce(x, m, k, w, n, residual, out, &e, (cudaStream_t)stream);
+}
+
+int ls_allreduce_residual_f32(const float* part, int64_t m, int64_t n, const void* residual, void* out,
+                              const ls_p2p_exchange* ex, ls_stream_t stream) {
+  if (!part || !residual || !out) return set_error(LS_ERR_INVALID_ARGUMENT, "ls_allreduce_residual_f32: null pointer");
+  lsb::P2PExchange e;
+  int rc = to_exchange(ex, n, "ls_allreduce_residual_f32", &e);
+  if (rc) return rc;
+  if (m < 1 || m > e.max_rows || (int64_t)m * n > (1ll << 31) - 1)
+    return set_error(LS_ERR_UNSUPPORTED_SHAPE, "ls_allreduce_residual_f32: m=%lld outside 1..%d", (long long)m,
+                     e.max_rows);
+  if (lsb::kArGrid > e.max_ctas)
+    return set_error(LS_ERR_UNSUPPORTED_SHAPE, "ls_allreduce_residual_f32: the exchange holds %d CTA counters, %d needed",
+                     e.max_ctas, lsb::kArGrid);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(lsb::kArGrid);
+  cfg.blockDim = dim3(lsb::kArThreads);
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, lsb::allreduce_residual_kernel, part,
+                                       static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out),
+                                       (int)m, (int)n, e, device_error_ptr());
+  return err == cudaSuccess ? LS_OK
+                            : set_error(LS_ERR_CUDA, "allreduce_residual launch: %s", cudaGetErrorString(err));
 }
 
 }  // extern "C"

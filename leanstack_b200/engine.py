@@ -264,6 +264,9 @@ class DecodeEngine:
             K.gemm_tc(x, w, epilogue=K.EPI_STORE_F32, out=part, workspace=self.tc_ws, tiled=tiled)
         else:
             K.linear(x, w, epilogue=K.EPI_STORE_F32, out=part)
+        if self.tp.p2p_tc is not None:  # one-shot all-reduce of the partials + residual, over peer memory
+            K.allreduce_residual_f32(part, residual, self.tp.p2p_tc, out=out)
+            return
         self.tp.all_reduce_sum(part)
         K.residual_add_f32(residual, part, out=out)
 
@@ -409,8 +412,8 @@ class DecodeEngine:
         """Kernels one decode step launches (embedding, layers, head, cursor advance)."""
         per_layer = 8 if self.backend == "tc" else 6
         head = 3 if self.backend == "tc" else 1
-        if self.tp is not None:  # + residual-add after each row-split linear, + keys-to-ids
-            if self.backend == "tc" or self.tp.p2p is None:
+        if self.tp is not None:  # + all-reduce / residual-add kernels after each row-split linear, + keys-to-ids
+            if self.tp.p2p is None or self.backend == "tc":
                 per_layer += 2
             head += 1
         return 1 + per_layer * len(self.rt.layers) + head + 1
@@ -420,5 +423,5 @@ class DecodeEngine:
         all-reduce of the CUDA-core linears is not counted)."""
         if self.tp is None:
             return 0
-        fused = self.backend != "tc" and self.tp.p2p is not None
+        fused = self.tp.p2p is not None  # CUDA-core: in the linear; tensor cores: one-shot kernel after it
         return (0 if fused else 2 * len(self.rt.layers)) + 1

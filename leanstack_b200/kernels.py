@@ -401,6 +401,21 @@ def linear_allreduce_residual(x: torch.Tensor, w: torch.Tensor, residual: torch.
     return out
 
 
+def allreduce_residual_f32(part: torch.Tensor, residual: torch.Tensor, exchange,
+                           out: torch.Tensor | None = None) -> torch.Tensor:
+    """One-shot all-reduce over the ranks of fp32 partials ``part [m, n]`` plus the
+    residual epilogue (``ls_allreduce_residual_f32``): ``bf16(res + bf16(sum))``."""
+    _check(part, "part", torch.float32)
+    _check(residual, "residual")
+    n = part.shape[-1]
+    m = part.numel() // n
+    if out is None:
+        out = torch.empty_like(residual)
+    nat.call("ls_allreduce_residual_f32", part.data_ptr(), m, n, residual.data_ptr(), out.data_ptr(),
+             ctypes.byref(exchange.desc), _stream())
+    return out
+
+
 def residual_add_f32(residual: torch.Tensor, y: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """``out = bf16(residual + bf16(y))`` for an fp32 ``y`` (after a tensor-parallel all-reduce)."""
     _check(residual, "residual")

@@ -170,7 +170,9 @@ class TPComm:
     NCCL for CUDA tensors (captured into the decode graph like any other
     launch); gloo works for the CPU tests of the partition math.  ``p2p`` (set
     by :meth:`enable_p2p`) is the exchange of the fused one-shot all-reduce
-    that the CUDA-core row-split linears use instead of NCCL.
+    that the CUDA-core row-split linears use instead of NCCL; ``p2p_tc`` a
+    second exchange (up to 128 rows) for the one-shot all-reduce of the
+    tensor-core row-split linears' fp32 partials.
     """
 
     def __init__(self, rank: int, world: int, group=None):
@@ -178,16 +180,21 @@ class TPComm:
         self.world = world
         self.group = group
         self.p2p: P2PExchange | None = None
+        self.p2p_tc: P2PExchange | None = None
 
-    def enable_p2p(self, width: int, max_rows: int = 8, max_ctas: int = 512) -> "P2PExchange":
+    def enable_p2p(self, width: int, max_rows: int = 8, max_ctas: int = 512,
+                   tc_rows: int = 128) -> "P2PExchange":
+        """Set up the fused all-reduce exchanges (a collective: every rank calls it)."""
         if self.world > 1 and self.p2p is None:
             self.p2p = P2PExchange(self, width, max_rows, max_ctas)
+            self.p2p_tc = P2PExchange(self, width, tc_rows, max_ctas)
         return self.p2p
 
     def close(self) -> None:
-        if self.p2p is not None:
-            self.p2p.close()
-            self.p2p = None
+        for ex in (self.p2p, self.p2p_tc):
+            if ex is not None:
+                ex.close()
+        self.p2p = self.p2p_tc = None
 
     def all_reduce_sum(self, t: torch.Tensor) -> None:
         if self.world > 1:

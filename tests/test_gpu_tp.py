@@ -5,9 +5,10 @@ seeded checkpoint.  The TP engine's greedy tokens must equal the single-GPU
 engine's (fp32 partial sums differ only in summation order) and its last hidden
 rows must agree within the north-star bound.  Both the eager step and the
 CUDA-graph step (NCCL captured in the graph) are checked, for the CUDA-core
-(batch 1) and tensor-core (batch 4) linears, and for the CUDA-core linears with
-the fused one-shot all-reduce over peer memory instead of NCCL.  Skipped with
-fewer than 2 GPUs.
+(batch 1) and tensor-core (batch 4) linears, each with NCCL and with the
+one-shot all-reduce over peer memory (fused into the CUDA-core linear; a
+kernel after the tcgen05 GEMM's fp32 partials), whose results must equal the
+NCCL path's bit for bit at world size 2.  Skipped with fewer than 2 GPUs.
 """
 
 from __future__ import annotations
@@ -22,7 +23,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 WORLD = 2
-CASES = ((1, "cuda_core", False), (1, "cuda_core", True), (4, "tc", False))
+CASES = ((1, "cuda_core", False), (1, "cuda_core", True), (4, "tc", False), (4, "tc", True))
 
 
 def _free_port() -> int:
@@ -111,3 +112,6 @@ def test_tp2_engine_matches_single_gpu_engine():
             err = (rows0 - ref_rows).abs().max().item()
             if torch.equal(toks0, ref_toks):
                 assert err <= 2e-2 * max(1.0, ref_rows.abs().max().item()), err
+            if p2p:  # two fp32 partials sum the same way on either path
+                assert torch.equal(toks0, out0[(batch, backend, False, use_graph)][0])
+                assert torch.equal(rows0, out0[(batch, backend, False, use_graph)][1])
