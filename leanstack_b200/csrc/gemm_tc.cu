@@ -891,7 +891,11 @@ static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
                          1024);
   int stages = (int)(((size_t)tc_stage_budget_kb() * 1024) / pl.stage_bytes);
   if (stages > kTcMaxStages) stages = kTcMaxStages;
-  if (stages < 3) stages = 3;
+  // At least four stages: with two or three of the large stages of the wider
+  // SiLU pairs (M 48-128: 40-48 KB each) the ring ran dry between HBM round
+  // trips (gate_up at M 80: 39.7 -> 35.9 us; verify pass 5.57 -> 5.32 ms,
+  // bs32 step 5543 -> 5700 tok/s).
+  if (stages < 4) stages = 4;
   pl.stages = stages;
   // Two accumulator buffers while they fit in 256 TMEM columns (half the SM's
   // TMEM, so a co-resident CTA of the next kernel can always allocate).
