@@ -95,6 +95,15 @@ class QwenSemanticStackRuntime:
 KVCacheManager = StaticKVBlockManager
 
 
+def normalize_stop_token_ids(stop_token_ids) -> tuple[int, ...]:
+    """Stop ids as a tuple of ints: None -> (), one int -> (id,) (``qwen_explicit.py:1868-1873``)."""
+    if stop_token_ids is None:
+        return ()
+    if isinstance(stop_token_ids, int):
+        return (int(stop_token_ids),)
+    return tuple(int(t) for t in stop_token_ids)
+
+
 def resolve_semantic_logits_backend() -> str:
     """Kept for interface parity (``qwen_explicit.py:150-151``); every value selects the native head."""
     return os.environ.get("LEANSTACK_SEMANTIC_LOGITS_BACKEND", "auto").strip().lower()
