@@ -38,9 +38,8 @@ constexpr int kTaStageBytes = 2 * kTaTileBytes;               // K + V
 constexpr int kTaRingBytes = kTaWarps * kTaStages * kTaStageBytes;  // 96 KB
 constexpr int kTaMaxSplits = 16;
 constexpr int kTaMergeBytes = kTaWarps * kTaRows * (kTaHeadDim + 2) * 4;  // reuses the ring
-// Receive area of the cluster merge for `rows` query rows per CTA.
-constexpr int ta_recv_bytes(int rows) { return rows * kTaHeadDim * 4 + 2 * kTaMaxSplits * rows * 4; }
-constexpr int ta_smem_bytes(int tiles) { return kTaRingBytes + ta_recv_bytes(kTaRows * tiles); }
+constexpr int kTaRecvBytes = kTaRows * kTaHeadDim * 4 + 2 * kTaMaxSplits * kTaRows * 4;
+constexpr int kTaSmemBytes = kTaRingBytes + kTaRecvBytes;
 static_assert(kTaMergeBytes <= kTaRingBytes, "merge buffers must fit in the ring");
 
 struct TaParams {
@@ -107,21 +106,11 @@ __device__ __forceinline__ uint32_t ta_swz(int key, int chunk) {
   return (uint32_t)(key * (kTaHeadDim * 2) + ((chunk ^ (key & 7)) << 4));
 }
 
-// TILES = 1: the CTA's 4 warps hold the same 16 query rows and stream four
-// interleaved sequences of key blocks, each through a private ring.
-// TILES = 2 (17-32 rows per kv head, e.g. a verify pass of 5 tokens x 4 q
-// heads): warps 0-1 hold rows 0-15 and warps 2-3 rows 16-31; warps w and
-// w + 2 stream the same key blocks through one shared ring (each loads half of
-// every stage), so the CTA reads each K/V block once for all 32 rows.
-template <int TILES>
 __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParams p) {
-  constexpr int NSTREAM = kTaWarps / TILES;  // interleaved key streams
-  constexpr int ROWS = kTaRows * TILES;      // query rows of the CTA
-  constexpr int STAGES = kTaStages * TILES;  // ring depth of one stream (same shared memory)
   extern __shared__ __align__(128) unsigned char ta_smem[];
-  float* recv_o = reinterpret_cast<float*>(ta_smem + kTaRingBytes);  // [splits][ROWS][128/splits]
-  float* recv_m = recv_o + ROWS * kTaHeadDim;                         // [kTaMaxSplits][ROWS]
-  float* recv_l = recv_m + kTaMaxSplits * ROWS;
+  float* recv_o = reinterpret_cast<float*>(ta_smem + kTaRingBytes);  // [splits][16][128/splits]
+  float* recv_m = recv_o + kTaRows * kTaHeadDim;                      // [kTaMaxSplits][16]
+  float* recv_l = recv_m + kTaMaxSplits * kTaRows;
 
   if (p.splits > 1) ta_cluster_arrive_relaxed();  // this CTA is running
   grid_dep_wait();
@@ -142,29 +131,21 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
   const int nblk_all = (L + kTaKeys - 1) / kTaKeys;
   const int blk_per = (nblk_all + p.splits - 1) / p.splits;
   const int blk0 = min(s * blk_per, nblk_all), blk1 = min(blk0 + blk_per, nblk_all);
-  const int r0 = rg * ROWS;
-  const int nrows = min(ROWS, p.R - r0);
-  const int stream = warp % NSTREAM, tile = warp / NSTREAM;
-  const int rt0 = r0 + tile * kTaRows;  // this warp's first query row
+  const int r0 = rg * kTaRows;
+  const int nrows = min(kTaRows, p.R - r0);
 
   const size_t head_base = ((size_t)b * p.Hkv + hkv) * p.max_seq * kTaHeadDim;
   const __nv_bfloat16* kbase = p.k_cache + head_base;
   const __nv_bfloat16* vbase = p.v_cache + head_base;
-  const uint32_t ring = smem_u32(ta_smem) + stream * STAGES * kTaStageBytes;
-  // The warps of one stream reading the same stage: the warp alone, or the
-  // pair on a named barrier (ids 1, 2).
-  auto stream_sync = [&]() {
-    if (TILES == 1) __syncwarp();
-    else named_bar_sync(1 + stream, 32 * TILES);
-  };
+  const uint32_t ring = smem_u32(ta_smem) + warp * kTaStages * kTaStageBytes;
 
-  // This stream's blocks: blk0 + stream, blk0 + stream + NSTREAM, ...
-  const int nb = (blk1 - blk0 - stream + NSTREAM - 1) / NSTREAM;  // may be <= 0
+  // This warp's blocks: blk0 + warp, blk0 + warp + 4, ...
+  const int nb = (blk1 - blk0 - warp + kTaWarps - 1) / kTaWarps;  // may be <= 0
   auto load_block = [&](int n, int stage) {
-    const int kb = (blk0 + stream + n * NSTREAM) * kTaKeys;
+    const int kb = (blk0 + warp + n * kTaWarps) * kTaKeys;
     const uint32_t st = ring + stage * kTaStageBytes;
 #pragma unroll
-    for (int it = tile * (8 / TILES); it < (tile + 1) * (8 / TILES); ++it) {
+    for (int it = 0; it < 8; ++it) {
       const int c = lane + 32 * it;
       const int r = c >> 4, cc = c & 15;
       const int j = kb + r;
@@ -182,7 +163,7 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
 
 #pragma unroll
-  for (int st = 0; st < STAGES; ++st) {
+  for (int st = 0; st < kTaStages; ++st) {
     if (st < nb) load_block(st, st);
     cp_async_commit();
   }
@@ -193,7 +174,7 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
   int lim[2];
 #pragma unroll
   for (int hr = 0; hr < 2; ++hr) {
-    const int row = rt0 + g8 + 8 * hr;
+    const int row = r0 + g8 + 8 * hr;
     const bool valid = row < p.R;
     const int i = valid ? row / p.G : 0;
     const int gq = valid ? row - i * p.G : 0;
@@ -207,12 +188,12 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
   }
 
   for (int n = 0; n < nb; ++n) {
-    cp_async_wait<STAGES - 1>();
-    stream_sync();
-    const int stage = n % STAGES;
+    cp_async_wait<kTaStages - 1>();
+    __syncwarp();
+    const int stage = n % kTaStages;
     const uint32_t stK = ring + stage * kTaStageBytes;
     const uint32_t stV = stK + kTaTileBytes;
-    const int jb = (blk0 + stream + n * NSTREAM) * kTaKeys;
+    const int jb = (blk0 + warp + n * kTaWarps) * kTaKeys;
 
     // S = Q K^T for 16 keys (two n-tiles of 8 keys).
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -291,8 +272,8 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
         mma_bf16(o[2 * c + 1], alo, v2, v3);
       }
     }
-    stream_sync();
-    if (n + STAGES < nb) load_block(n + STAGES, stage);
+    __syncwarp();
+    if (n + kTaStages < nb) load_block(n + kTaStages, stage);
     cp_async_commit();
   }
   cp_async_wait<0>();
@@ -303,7 +284,7 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
   }
   __syncthreads();  // every warp is done with its ring: reuse it for the merge
 
-  // ---- merge the warps of this CTA that hold the same rows ----
+  // ---- merge the 4 warps of this CTA ----
   float* wm = reinterpret_cast<float*>(ta_smem);       // [4][16]
   float* wl = wm + kTaWarps * kTaRows;                 // [4][16]
   float* wo = wl + kTaWarps * kTaRows;                 // [4][16][128]
@@ -327,17 +308,16 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
   const int d = threadIdx.x;  // one output dimension per thread (kTaThreads == kTaHeadDim)
   const int w = kTaHeadDim / p.splits;  // dims each cluster CTA finishes
   for (int r = 0; r < nrows; ++r) {
-    const int wt = (r / kTaRows) * NSTREAM, rr = r % kTaRows;  // first warp holding row r, its row there
     float mx = -INFINITY;
 #pragma unroll
-    for (int k = wt; k < wt + NSTREAM; ++k) mx = fmaxf(mx, wm[k * kTaRows + rr]);
+    for (int k = 0; k < kTaWarps; ++k) mx = fmaxf(mx, wm[k * kTaRows + r]);
     float ls = 0.f, acc = 0.f;
     if (mx != -INFINITY) {
 #pragma unroll
-      for (int k = wt; k < wt + NSTREAM; ++k) {
-        const float sc = exp2f(wm[k * kTaRows + rr] - mx);
-        ls += wl[k * kTaRows + rr] * sc;
-        acc += wo[((size_t)k * kTaRows + rr) * kTaHeadDim + d] * sc;
+      for (int k = 0; k < kTaWarps; ++k) {
+        const float sc = exp2f(wm[k * kTaRows + r] - mx);
+        ls += wl[k * kTaRows + r] * sc;
+        acc += wo[((size_t)k * kTaRows + r) * kTaHeadDim + d] * sc;
       }
     }
     if (p.splits == 1) {
@@ -346,10 +326,10 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
       p.out[((size_t)(b * p.q_len + i) * p.Hq + hkv * p.G + gq) * kTaHeadDim + d] = f_to_bf16(acc / ls);
     } else {
       const int owner = d / w;
-      ta_st_remote(recv_o + ((size_t)s * ROWS + r) * w + (d - owner * w), (uint32_t)owner, acc);
+      ta_st_remote(recv_o + ((size_t)s * kTaRows + r) * w + (d - owner * w), (uint32_t)owner, acc);
       if (d < p.splits) {  // this CTA's (max, sum) of row r to every CTA of the cluster
-        ta_st_remote(recv_m + s * ROWS + r, (uint32_t)d, mx);
-        ta_st_remote(recv_l + s * ROWS + r, (uint32_t)d, ls);
+        ta_st_remote(recv_m + s * kTaRows + r, (uint32_t)d, mx);
+        ta_st_remote(recv_l + s * kTaRows + r, (uint32_t)d, ls);
       }
     }
   }
@@ -359,14 +339,14 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
   for (int idx = threadIdx.x; idx < nrows * w; idx += kTaThreads) {
     const int r = idx / w, dd = idx - r * w;
     float mx = -INFINITY;
-    for (int c = 0; c < p.splits; ++c) mx = fmaxf(mx, recv_m[c * ROWS + r]);
+    for (int c = 0; c < p.splits; ++c) mx = fmaxf(mx, recv_m[c * kTaRows + r]);
     float ls = 0.f, acc = 0.f;
     for (int c = 0; c < p.splits; ++c) {
-      const float mc = recv_m[c * ROWS + r];
+      const float mc = recv_m[c * kTaRows + r];
       if (mc == -INFINITY) continue;
       const float sc = exp2f(mc - mx);
-      ls += recv_l[c * ROWS + r] * sc;
-      acc += recv_o[((size_t)c * ROWS + r) * w + dd] * sc;
+      ls += recv_l[c * kTaRows + r] * sc;
+      acc += recv_o[((size_t)c * kTaRows + r) * w + dd] * sc;
     }
     const int row = r0 + r;
     const int i = row / p.G, gq = row - (row / p.G) * p.G;
@@ -380,58 +360,25 @@ namespace lsb_host {
 using namespace lsb;
 
 struct TaPlan {
-  int G, R, RG, splits, tiles;
+  int G, R, RG, splits;
 };
 
-// Rows per CTA: one 16-row tile, or two (32 rows, each K/V block read once
-// for both) when a kv head has 17-32 query rows.  Splits per (sequence, kv
-// head, row group): a power of two up to 16, until there are about as many
-// CTAs as SMs, keeping at least 32 cache positions a split.  Measured on
-// Qwen3-4B decode steps: at batch 1 (8 pairs) 16 and 8 splits tie and fewer
-// are slower; at batch 32 (256 pairs) one split (no cluster) is 5% faster than
-// two and 9% faster than four.
+// Splits per (sequence, kv head, 16-row group): a power of two up to 16, until
+// there are about as many CTAs as SMs, keeping at least 32 cache positions a
+// split.  Measured on Qwen3-4B decode steps: at batch 1 (8 pairs) 16 and 8
+// splits tie and fewer are slower; at batch 32 (256 pairs) one split (no
+// cluster) is 5% faster than two and 9% faster than four.
 static TaPlan ta_plan(int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int64_t max_seq) {
   TaPlan pl;
   pl.G = (int)(hq / hkv);
   pl.R = (int)(q_len * pl.G);
-  pl.tiles = (pl.R > kTaRows) ? 2 : 1;
-  pl.RG = (pl.R + kTaRows * pl.tiles - 1) / (kTaRows * pl.tiles);
+  pl.RG = (pl.R + kTaRows - 1) / kTaRows;
   const int64_t pairs = batch * hkv * pl.RG;
   int splits = 1;
   while (splits < kTaMaxSplits && pairs * splits < (int64_t)sm_count() && (int64_t)splits * 2 * 32 <= max_seq)
     splits *= 2;
   pl.splits = splits;
   return pl;
-}
-
-template <int TILES>
-static int launch_ta_t(const TaParams& p, const TaPlan& pl, int64_t hkv, int64_t batch, cudaStream_t stream) {
-  auto kern = decode_attention_tc_kernel<TILES>;
-  constexpr int smem = ta_smem_bytes(TILES);
-  static bool attrs_set = false;
-  if (!attrs_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "attention_tc attributes: %s", cudaGetErrorString(e));
-    attrs_set = true;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.splits, (unsigned)(hkv * pl.RG), (unsigned)batch);
-  cfg.blockDim = dim3(kTaThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = pl.splits;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
-  if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "decode_attention_tc launch: %s", cudaGetErrorString(e));
-  return LS_OK;
 }
 
 int launch_decode_attention_tc(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
@@ -458,7 +405,37 @@ int launch_decode_attention_tc(const void* q, const void* k_cache, const void* v
   p.max_seq = (int)max_seq;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = device_error_ptr();
-  return pl.tiles == 2 ? launch_ta_t<2>(p, pl, hkv, batch, stream) : launch_ta_t<1>(p, pl, hkv, batch, stream);
+  static bool attrs_set = false;
+  if (!attrs_set) {
+    cudaError_t e = cudaFuncSetAttribute(decode_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kTaSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(decode_attention_tc_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "attention_tc attributes: %s", cudaGetErrorString(e));
+    attrs_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.splits, (unsigned)(hkv * pl.RG), (unsigned)batch);
+  cfg.blockDim = dim3(kTaThreads);
+  cfg.dynamicSmemBytes = kTaSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeClusterDimension;
+  attr[na].val.clusterDim.x = pl.splits;
+  attr[na].val.clusterDim.y = 1;
+  attr[na].val.clusterDim.z = 1;
+  ++na;
+  {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_attention_tc_kernel, p);
+  if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "decode_attention_tc launch: %s", cudaGetErrorString(e));
+  return LS_OK;
 }
 
 }  // namespace lsb_host
