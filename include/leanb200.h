@@ -70,7 +70,9 @@ typedef enum ls_epilogue {
   LS_EPI_STORE = 0,     /* out = bf16(W x) */
   LS_EPI_RESIDUAL = 1,  /* out = bf16(residual + bf16(W x)) */
   LS_EPI_SILU_MUL = 2,  /* W = [gate; up] (2I rows): out[I] = bf16(bf16(silu(bf16 g)) * bf16 u) */
-  LS_EPI_STORE_F32 = 4  /* out (float*) = W x unrounded: the partial of a tensor-parallel row-split linear */
+  LS_EPI_STORE_F32 = 4, /* out (float*) = W x unrounded: the partial of a tensor-parallel row-split linear */
+  LS_EPI_SPLIT_F32 = 8  /* tcgen05 GEMM only: out (float*) = [splits][m][n] per-split unrounded sums of W x
+                           (ls_gemm_bf16_tcgen05_splits); the consumer adds them in split order */
 } ls_epilogue;
 
 typedef void* ls_stream_t; /* a cudaStream_t */
@@ -173,6 +175,16 @@ int ls_qk_norm_rope_kvappend(const void* qkv, int64_t batch, int64_t q_len, int6
                              const void* rope_cos, const void* rope_sin, int64_t rope_len, int64_t rope_offset,
                              const int32_t* cache_pos, int64_t uniform_past, void* k_cache, void* v_cache,
                              int64_t max_seq, void* k_out, void* v_out, void* q_out, ls_stream_t stream);
+/* The same on the split fp32 partials of the QKV projection
+ * (ls_gemm_bf16_tcgen05 with LS_EPI_SPLIT_F32): qkv = bf16(sum over the
+ * splits in order) first, the rounding of the reference's F.linear
+ * (src/leanstack/runtime/qwen_explicit.py:748). */
+int ls_qk_norm_rope_kvappend_splits(const float* qkv_part, int64_t splits, int64_t batch, int64_t q_len,
+                                    int64_t num_heads, int64_t num_kv_heads, int64_t head_dim, const void* q_norm_w,
+                                    const void* k_norm_w, float eps, const void* rope_cos, const void* rope_sin,
+                                    int64_t rope_len, int64_t rope_offset, const int32_t* cache_pos,
+                                    int64_t uniform_past, void* k_cache, void* v_cache, int64_t max_seq, void* k_out,
+                                    void* v_out, void* q_out, ls_stream_t stream);
 
 /*
  * Row-wise argmax of bf16 logits [m, n] (lowest index on ties): the
@@ -260,6 +272,12 @@ int ls_gemm_bf16_tcgen05(const void* x, int64_t m, int64_t k, const void* w, int
                          const void* residual, void* out, void* workspace, int64_t workspace_bytes,
                          ls_stream_t stream);
 int ls_gemm_bf16_tcgen05_workspace_bytes(int64_t m, int64_t k, int64_t n, int epilogue, int64_t* bytes);
+/* Number of k-splits of the LS_EPI_SPLIT_F32 form: its out holds splits * m * n
+ * floats and the call needs no workspace (NULL is accepted).  The split form
+ * leaves the cross-split sum to the next kernel (ls_residual_rmsnorm_splits,
+ * ls_qk_norm_rope_kvappend_splits) instead of reducing partials inside the
+ * GEMM behind a grid-wide wait: the decode step's QKV, o_proj and down. */
+int ls_gemm_bf16_tcgen05_splits(int64_t m, int64_t k, int64_t n, int64_t* splits);
 
 /* Fused one-shot all-reduce over NVLink peer memory (no counterpart in the
  * reference, which runs on one GPU; it replaces the NCCL all-reduce of the
@@ -315,6 +333,15 @@ int ls_residual_add_f32(const void* residual, const float* y, int64_t n, void* o
 /* Standalone RMSNorm over the last dim, bf16((x * rsqrt(mean(x^2) + eps)) * w),
  * for m rows of length n (src/leanstack/runtime/qwen_explicit.py:621-637). */
 int ls_rmsnorm(const void* x, int64_t m, int64_t n, const void* w, float eps, void* out, ls_stream_t stream);
+
+/* Residual add of a linear's split partials (LS_EPI_SPLIT_F32), then RMSNorm:
+ * out_residual = bf16(residual + bf16(sum over the splits of part[s][m][n]))
+ * (the o_proj / down residual of src/leanstack/runtime/qwen_explicit.py:819-829,
+ * :852) and, when norm_w is not NULL, out_norm = the RMSNorm of out_residual
+ * (:621-637), the post-attention / next input / final norm that follows. */
+int ls_residual_rmsnorm_splits(const float* part, int64_t splits, int64_t m, int64_t n, const void* residual,
+                               const void* norm_w, float eps, void* out_residual, void* out_norm,
+                               ls_stream_t stream);
 
 /* cache_pos[b] += delta[b] (delta NULL: += q_len): moves the device cursors
  * after a step, the device-side counterpart of the reference's host cursor

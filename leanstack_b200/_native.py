@@ -24,7 +24,7 @@ STATUS_NAMES = {
     8: "LS_ERR_NOT_SUPPORTED",
 }
 
-EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_STORE_F32 = 0, 1, 2, 4
+EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_STORE_F32, EPI_SPLIT_F32 = 0, 1, 2, 4, 8
 
 
 class NativeLibraryMissing(RuntimeError):
@@ -97,6 +97,10 @@ SIGNATURES: dict[str, list] = {
     "ls_argmax_rows_workspace_bytes": [_i64, _i64, ctypes.POINTER(_i64)],
     "ls_gemm_bf16_tcgen05": [_p, _i64, _i64, _p, _i64, _int, _p, _p, _p, _i64, _p],
     "ls_gemm_bf16_tcgen05_workspace_bytes": [_i64, _i64, _i64, _int, ctypes.POINTER(_i64)],
+    "ls_gemm_bf16_tcgen05_splits": [_i64, _i64, _i64, ctypes.POINTER(_i64)],
+    "ls_qk_norm_rope_kvappend_splits": [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _f32, _p, _p, _i64, _i64, _p,
+                                        _i64, _p, _p, _i64, _p, _p, _p, _p],
+    "ls_residual_rmsnorm_splits": [_p, _i64, _i64, _i64, _p, _p, _f32, _p, _p, _p],
     "ls_advance_cursors": [_p, _p, _i64, _i64, _p],
 }
 _RESTYPES = {"ls_last_error": ctypes.c_char_p}

@@ -18,7 +18,9 @@ namespace lsb {
 constexpr int kHeadDim = 128;
 
 struct QkRopeParams {
-  const __nv_bfloat16* qkv;  // [M, (Hq + 2 Hkv) D]
+  const __nv_bfloat16* qkv;  // [M, (Hq + 2 Hkv) D], or null: the split partials below
+  const float* part;         // [splits][M][(Hq + 2 Hkv) D] fp32 (tcgen05 GEMM, LS_EPI_SPLIT_F32)
+  int splits;
   const __nv_bfloat16* q_norm_w;
   const __nv_bfloat16* k_norm_w;
   const __nv_bfloat16* cos;  // [rope_len, D/2]
@@ -47,8 +49,24 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(QkRopeParams p
   const bool is_q = h < p.Hq;
   const int hk = h - p.Hq;
   const int qkv_dim = (p.Hq + 2 * p.Hkv) * kHeadDim;
-  const __nv_bfloat16* src = p.qkv + (size_t)t * qkv_dim + (size_t)h * kHeadDim;
   const int e0 = lane * 4;
+  // Four bf16 elements of the projection at column col of token t: loaded, or
+  // the split partials summed in split order and rounded once.
+  auto load4 = [&](int col) -> uint2 {
+    if (p.qkv) return *reinterpret_cast<const uint2*>(p.qkv + (size_t)t * qkv_dim + col);
+    const size_t slab = (size_t)gridDim.x * qkv_dim;
+    const float* q = p.part + (size_t)t * qkv_dim + col;
+    float4 a = __ldcg(reinterpret_cast<const float4*>(q));
+    for (int j = 1; j < p.splits; ++j) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(q + j * slab));
+      a.x += v.x;
+      a.y += v.y;
+      a.z += v.z;
+      a.w += v.w;
+    }
+    __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y), hi = __floats2bfloat162_rn(a.z, a.w);
+    return make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+  };
 
   const int row = pos - p.rope_offset;  // row of the cos/sin table
   if (pos < 0 || row < 0 || row >= p.rope_len || (!is_q && (p.k_cache != nullptr) && pos >= p.max_seq)) {
@@ -56,7 +74,7 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(QkRopeParams p
     return;
   }
 
-  const uint2 raw_u = *reinterpret_cast<const uint2*>(src + e0);
+  const uint2 raw_u = load4(h * kHeadDim + e0);
   float raw[4] = {bf16_lo(raw_u.x), bf16_hi(raw_u.x), bf16_lo(raw_u.y), bf16_hi(raw_u.y)};
   float ss = raw[0] * raw[0] + raw[1] * raw[1] + raw[2] * raw[2] + raw[3] * raw[3];
   ss = warp_sum(ss);
@@ -87,7 +105,7 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(QkRopeParams p
     *reinterpret_cast<uint2*>(p.q_out + ((size_t)t * p.Hq + h) * kHeadDim + e0) = packed;
     return;
   }
-  const uint2 v_u = *reinterpret_cast<const uint2*>(src + (size_t)p.Hkv * kHeadDim + e0);
+  const uint2 v_u = load4((h + p.Hkv) * kHeadDim + e0);
   if (p.k_cache) {
     const size_t off = (((size_t)b * p.Hkv + hk) * p.max_seq + pos) * kHeadDim + e0;
     *reinterpret_cast<uint2*>(p.k_cache + off) = packed;
@@ -119,12 +137,14 @@ static cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStr
   return cfg;
 }
 
-int launch_qk_norm_rope(const void* qkv, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, const void* qn,
+int launch_qk_norm_rope(const void* qkv, const float* part, int64_t splits, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, const void* qn,
                         const void* kn, const void* cos, const void* sin, int64_t rope_len, int64_t rope_offset,
                         const int32_t* cache_pos, int64_t uniform_past, void* k_cache, void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* q_out,
                         float eps, cudaStream_t stream) {
   QkRopeParams p = {};
   p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  p.part = part;
+  p.splits = (int)splits;
   p.q_norm_w = static_cast<const __nv_bfloat16*>(qn);
   p.k_norm_w = static_cast<const __nv_bfloat16*>(kn);
   p.cos = static_cast<const __nv_bfloat16*>(cos);

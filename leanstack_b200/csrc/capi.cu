@@ -83,6 +83,73 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const __nv_bfloat
   }
 }
 
+// Residual add of split fp32 partials, then RMSNorm (one CTA per row):
+// h = bf16(residual + bf16(sum_j part[j])), the splits added in order j = 0,
+// 1, ... (the order of the GEMM's in-kernel reduction), and, when w is not
+// null, y = bf16((h * rsqrt(mean(h^2) + eps)) * w) with the sum of squares
+// taken in rmsnorm_kernel's order, so both paths give identical bits.
+__global__ void __launch_bounds__(kNormThreads) residual_norm_splits_kernel(const float* part, int splits, int m, int n,
+                                                                            const __nv_bfloat16* residual,
+                                                                            const __nv_bfloat16* w, float eps,
+                                                                            __nv_bfloat16* out_res,
+                                                                            __nv_bfloat16* out_norm) {
+  grid_dep_launch();
+  grid_dep_wait();
+  __shared__ float red[kNormThreads / 32];
+  const size_t slab = (size_t)m * n;
+  const float* pr = part + (size_t)blockIdx.x * n;
+  const __nv_bfloat16* rr = residual + (size_t)blockIdx.x * n;
+  __nv_bfloat16* hr = out_res + (size_t)blockIdx.x * n;
+  float ss = 0.f;
+  for (int v = threadIdx.x; v < n / 8; v += kNormThreads) {
+    float4 a0 = __ldcg(reinterpret_cast<const float4*>(pr + v * 8));
+    float4 a1 = __ldcg(reinterpret_cast<const float4*>(pr + v * 8 + 4));
+    for (int j = 1; j < splits; ++j) {
+      const float4 b0 = __ldcg(reinterpret_cast<const float4*>(pr + j * slab + v * 8));
+      const float4 b1 = __ldcg(reinterpret_cast<const float4*>(pr + j * slab + v * 8 + 4));
+      a0.x += b0.x, a0.y += b0.y, a0.z += b0.z, a0.w += b0.w;
+      a1.x += b1.x, a1.y += b1.y, a1.z += b1.z, a1.w += b1.w;
+    }
+    const float y[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    float f[8];
+    unpack8(ldg16(rr + v * 8), f);
+    uint4 o;
+    uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 pr2 = __floats2bfloat162_rn(f[2 * j] + round_bf16(y[2 * j]), f[2 * j + 1] + round_bf16(y[2 * j + 1]));
+      op[j] = *reinterpret_cast<uint32_t*>(&pr2);
+    }
+    *reinterpret_cast<uint4*>(hr + v * 8) = o;
+    float h[8];
+    unpack8(o, h);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(h[j], h[j], ss);
+  }
+  if (!out_norm) return;
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+  const float r = rsqrtf(tot / (float)n + eps);
+  __nv_bfloat16* orow = out_norm + (size_t)blockIdx.x * n;
+  for (int v = threadIdx.x; v < n / 8; v += kNormThreads) {
+    float f[8], g[8];
+    unpack8(*reinterpret_cast<const uint4*>(hr + v * 8), f);  // this thread's own stores above
+    unpack8(ldg16(w + v * 8), g);
+    uint4 o;
+    uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 pr2 = __floats2bfloat162_rn((f[2 * j] * r) * g[2 * j], (f[2 * j + 1] * r) * g[2 * j + 1]);
+      op[j] = *reinterpret_cast<uint32_t*>(&pr2);
+    }
+    *reinterpret_cast<uint4*>(orow + v * 8) = o;
+  }
+}
+
 // Row argmax over bf16 logits: grid (chunks, m); each CTA reduces one chunk of
 // one row, the last CTA of the row reduces the chunk winners.
 constexpr int kArgmaxThreads = 256;
@@ -247,7 +314,7 @@ int lmhead_grid(int64_t vocab, int64_t m);
 int launch_lmhead_keys(const void* h, int64_t m, int64_t k, const void* norm_w, float eps, const void* w,
                        int64_t rows, int64_t vocab_offset, int64_t* out_keys, cudaStream_t stream, float* part_val,
                        int* part_idx, unsigned int* counter, int grid);
-int launch_qk_norm_rope(const void* qkv, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, const void* qn,
+int launch_qk_norm_rope(const void* qkv, const float* part, int64_t splits, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, const void* qn,
                         const void* kn, const void* cos, const void* sin, int64_t rope_len, int64_t rope_offset,
                         const int32_t* cache_pos, int64_t uniform_past, void* k_cache, void* v_cache, int64_t max_seq, void* k_out, void* v_out, void* q_out,
                         float eps, cudaStream_t stream);
@@ -258,6 +325,7 @@ int launch_decode_attention(const void* q, const void* k_cache, const void* v_ca
                             void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream);
 
 int tc_workspace_bytes(int64_t m, int64_t k, int64_t n_out, int epi, int64_t* bytes);
+int tc_split_count(int64_t m, int64_t k, int64_t n_out, int64_t* splits);
 int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n_out, int epi, const void* residual,
                    void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream,
                    const void* w_tiled = nullptr);
@@ -380,7 +448,7 @@ int ls_rmsnorm_qkv_rope_kvappend(const void* x, int64_t batch, int64_t q_len, in
   int rc = launch_linear(x, m, hidden, input_norm_w, eps, qkv_w, qkv_dim, 0, nullptr, qkv_scratch,
                          (cudaStream_t)stream, nullptr, nullptr, nullptr, nullptr, 0);
   if (rc) return rc;
-  return launch_qk_norm_rope(qkv_scratch, batch, q_len, num_heads, num_kv_heads, q_norm_w, k_norm_w, rope_cos,
+  return launch_qk_norm_rope(qkv_scratch, nullptr, 0, batch, q_len, num_heads, num_kv_heads, q_norm_w, k_norm_w, rope_cos,
                              rope_sin, rope_len, rope_offset, cache_pos, uniform_past, k_cache, v_cache, max_seq, k_out, v_out, q_out, eps,
                              (cudaStream_t)stream);
 }
@@ -464,15 +532,23 @@ int ls_lmhead_argmax(const void* h, int64_t m, int64_t hidden, const void* final
 int ls_gemm_bf16_tcgen05_workspace_bytes(int64_t m, int64_t k, int64_t n, int epilogue, int64_t* bytes) {
   LS_REQUIRE(bytes && m > 0 && m <= 128 && k > 0 && n > 0, LS_ERR_INVALID_ARGUMENT,
              "ls_gemm_bf16_tcgen05_workspace_bytes: bad arguments");
-  LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32,
+  LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32 ||
+                 epilogue == LS_EPI_SPLIT_F32,
              LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d", epilogue);
   return tc_workspace_bytes(m, k, n, epilogue, bytes);
+}
+
+int ls_gemm_bf16_tcgen05_splits(int64_t m, int64_t k, int64_t n, int64_t* splits) {
+  LS_REQUIRE(splits && m > 0 && m <= 128 && k > 0 && n > 0, LS_ERR_INVALID_ARGUMENT,
+             "ls_gemm_bf16_tcgen05_splits: bad arguments");
+  return tc_split_count(m, k, n, splits);
 }
 
 int ls_gemm_bf16_tcgen05(const void* x, int64_t m, int64_t k, const void* w, int64_t n, int epilogue,
                          const void* residual, void* out, void* workspace, int64_t workspace_bytes,
                          ls_stream_t stream) {
-  LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32,
+  LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32 ||
+                 epilogue == LS_EPI_SPLIT_F32,
              LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d", epilogue);
   return launch_gemm_tc(x, m, k, w, n, epilogue, residual, out, workspace, workspace_bytes, (cudaStream_t)stream);
 }
@@ -499,7 +575,8 @@ int ls_gemm_bf16_tcgen05_tiled(const void* x, int64_t m, int64_t k, const void* 
                                const void* residual, void* out, void* workspace, int64_t workspace_bytes,
                                ls_stream_t stream) {
   LS_REQUIRE(w_tiled, LS_ERR_INVALID_ARGUMENT, "ls_gemm_bf16_tcgen05_tiled: null weights");
-  LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32,
+  LS_REQUIRE((epilogue >= LS_EPI_STORE && epilogue <= LS_EPI_SILU_MUL) || epilogue == LS_EPI_STORE_F32 ||
+                 epilogue == LS_EPI_SPLIT_F32,
              LS_ERR_INVALID_ARGUMENT, "unknown epilogue %d", epilogue);
   return launch_gemm_tc(x, m, k, nullptr, n, epilogue, residual, out, workspace, workspace_bytes,
                         (cudaStream_t)stream, w_tiled);
@@ -523,9 +600,33 @@ int ls_qk_norm_rope_kvappend(const void* qkv, int64_t batch, int64_t q_len, int6
   LS_REQUIRE(cache_pos || (uniform_past >= rope_offset && uniform_past + q_len <= rope_offset + rope_len),
              LS_ERR_KV_OVERFLOW, "positions outside the rope table");
   LS_REQUIRE(cache_pos || !k_cache || uniform_past + q_len <= max_seq, LS_ERR_KV_OVERFLOW, "cache overflow");
-  return launch_qk_norm_rope(qkv, batch, q_len, num_heads, num_kv_heads, q_norm_w, k_norm_w, rope_cos, rope_sin,
+  return launch_qk_norm_rope(qkv, nullptr, 0, batch, q_len, num_heads, num_kv_heads, q_norm_w, k_norm_w, rope_cos, rope_sin,
                              rope_len, rope_offset, cache_pos, uniform_past, k_cache, v_cache, max_seq, k_out, v_out,
                              q_out, eps, (cudaStream_t)stream);
+}
+
+int ls_qk_norm_rope_kvappend_splits(const float* qkv_part, int64_t splits, int64_t batch, int64_t q_len,
+                                    int64_t num_heads, int64_t num_kv_heads, int64_t head_dim, const void* q_norm_w,
+                                    const void* k_norm_w, float eps, const void* rope_cos, const void* rope_sin,
+                                    int64_t rope_len, int64_t rope_offset, const int32_t* cache_pos,
+                                    int64_t uniform_past, void* k_cache, void* v_cache, int64_t max_seq, void* k_out,
+                                    void* v_out, void* q_out, ls_stream_t stream) {
+  LS_REQUIRE(qkv_part && splits >= 1 && aligned16(qkv_part) && q_norm_w && k_norm_w && rope_cos && rope_sin && q_out,
+             LS_ERR_INVALID_ARGUMENT, "ls_qk_norm_rope_kvappend_splits: null or misaligned pointer");
+  LS_REQUIRE(head_dim == 128, LS_ERR_UNSUPPORTED_SHAPE, "head_dim=%lld (only 128 is implemented)",
+             (long long)head_dim);
+  LS_REQUIRE(batch > 0 && q_len > 0 && num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0 &&
+                 batch * q_len < (1ll << 31) && (num_heads + num_kv_heads + 3) / 4 <= 65535,
+             LS_ERR_INVALID_ARGUMENT, "ls_qk_norm_rope_kvappend_splits: bad sizes");
+  LS_REQUIRE((k_cache == nullptr) == (v_cache == nullptr) && (k_out == nullptr) == (v_out == nullptr),
+             LS_ERR_INVALID_ARGUMENT, "k/v cache and k/v out come in pairs");
+  LS_REQUIRE(rope_len > 0 && rope_offset >= 0, LS_ERR_INVALID_ARGUMENT, "bad rope table");
+  LS_REQUIRE(cache_pos || (uniform_past >= rope_offset && uniform_past + q_len <= rope_offset + rope_len),
+             LS_ERR_KV_OVERFLOW, "positions outside the rope table");
+  LS_REQUIRE(cache_pos || !k_cache || uniform_past + q_len <= max_seq, LS_ERR_KV_OVERFLOW, "cache overflow");
+  return launch_qk_norm_rope(nullptr, qkv_part, splits, batch, q_len, num_heads, num_kv_heads, q_norm_w, k_norm_w,
+                             rope_cos, rope_sin, rope_len, rope_offset, cache_pos, uniform_past, k_cache, v_cache,
+                             max_seq, k_out, v_out, q_out, eps, (cudaStream_t)stream);
 }
 
 static int argmax_chunks(int64_t m, int64_t n) {
@@ -639,6 +740,32 @@ int ls_rmsnorm(const void* x, int64_t m, int64_t n, const void* w, float eps, vo
   cudaError_t e = cudaLaunchKernelEx(&cfg, lsb::rmsnorm_kernel, static_cast<const __nv_bfloat16*>(x), (int)n,
                                      static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(out), vec);
   return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "rmsnorm launch: %s", cudaGetErrorString(e));
+}
+
+int ls_residual_rmsnorm_splits(const float* part, int64_t splits, int64_t m, int64_t n, const void* residual,
+                               const void* norm_w, float eps, void* out_residual, void* out_norm,
+                               ls_stream_t stream) {
+  LS_REQUIRE(part && residual && out_residual && (norm_w == nullptr) == (out_norm == nullptr),
+             LS_ERR_INVALID_ARGUMENT, "ls_residual_rmsnorm_splits: null pointer");
+  LS_REQUIRE(splits >= 1 && m > 0 && m < (1ll << 31) && n > 0 && n <= (1 << 20) && splits * m * n < (1ll << 40),
+             LS_ERR_INVALID_ARGUMENT, "ls_residual_rmsnorm_splits: bad sizes");
+  LS_REQUIRE(n % 8 == 0 && aligned16(part) && aligned16(residual) && aligned16(out_residual) &&
+                 (!norm_w || (aligned16(norm_w) && aligned16(out_norm))),
+             LS_ERR_MISALIGNED, "ls_residual_rmsnorm_splits: rows must be multiples of 8 on 16-byte boundaries");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)m);
+  cfg.blockDim = dim3(lsb::kNormThreads);
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, lsb::residual_norm_splits_kernel, part, (int)splits, (int)m, (int)n,
+                                     static_cast<const __nv_bfloat16*>(residual),
+                                     static_cast<const __nv_bfloat16*>(norm_w), eps,
+                                     static_cast<__nv_bfloat16*>(out_residual), static_cast<__nv_bfloat16*>(out_norm));
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "residual_norm_splits launch: %s", cudaGetErrorString(e));
 }
 
 int ls_advance_cursors(int32_t* cache_pos, const int32_t* delta, int64_t batch, int64_t q_len, ls_stream_t stream) {

@@ -47,7 +47,12 @@ constexpr int kTcMaxStages = 16;
 constexpr int kTcMaxTiles = 2048;
 constexpr size_t kTcCounterBytes = (size_t)2 * kTcMaxTiles * sizeof(unsigned int);
 
-enum { TEPI_STORE = 0, TEPI_RESIDUAL = 1, TEPI_SILU_MUL = 2, TEPI_STORE_F32 = 4 };
+// TEPI_SPLIT_F32: no reduction in the kernel.  The grid is tile-aligned (every
+// CTA holds the k-range of exactly one tile) and CTA j of a tile's splits
+// writes its unrounded fp32 sum to out[j][b][n]; the consumer kernel adds the
+// splits in order j = 0, 1, ... (the order the in-kernel reduction uses, so
+// the result is bit-identical) and applies the epilogue itself.
+enum { TEPI_STORE = 0, TEPI_RESIDUAL = 1, TEPI_SILU_MUL = 2, TEPI_STORE_F32 = 4, TEPI_SPLIT_F32 = 8 };
 
 struct TcParams {
   const __nv_bfloat16* residual;  // [B, N]
@@ -594,11 +599,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int n = t * kTcTileN + row;
       const int slot = (t == (int)(ub / KB)) ? 0 : 1;
       float* mypart = p.partial + (((size_t)cta * 2 + slot) * ACCS * p.BN) * kTcTileN;
+      const int split = (EPI == TEPI_SPLIT_F32) ? cta - tc_unit_owner(U, G, tile_begin) : 0;
       for (int cb = 0; cb < p.BN; cb += 16) {
         float v[16], w2[16];
         tmem_ld16(acc_addr + (uint32_t)cb, v);
         if (SILU) tmem_ld16(acc_addr + (uint32_t)(p.BN + cb), w2);
-        if (whole) {
+        if (EPI == TEPI_SPLIT_F32) {
+          if (n < p.N) {
+            float* dst = reinterpret_cast<float*>(p.out) + (size_t)split * p.B * p.N + n;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (cb + j < p.B) dst[(size_t)(cb + j) * p.N] = v[j];
+          }
+        } else if (whole) {
           if (n < p.N) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -619,7 +632,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[a]);  // the MMA warp may reuse this accumulator buffer
-      if (!whole) {
+      if (!whole && EPI != TEPI_SPLIT_F32) {
         // Publish this contributor's partial; the reduction waits until the
         // whole mainloop is done (below), so no CTA ever waits mid-stream.
         named_bar_sync(1, kTcEpiThreads);
@@ -631,7 +644,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (tr && threadIdx.x == 0) tr[3] = global_timer_ns();
     // ---- deferred stream-K reduction of this CTA's partial tiles ----
-    if (!*(volatile int*)&s_abort)
+    if (EPI != TEPI_SPLIT_F32 && !*(volatile int*)&s_abort)
       tc_stream_k_fixup<EPI>(p, U, G, KB, ub, ue, cta, smem, (size_t)NS * p.stage_bytes, red_bar, &s_abort, tr);
   }
 
@@ -863,6 +876,7 @@ static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t co
 
 struct TcPlan {
   int grid, BN, tiles, kblocks, stages, stage_bytes, accs, acc_buffers;
+  int splits;  // CTAs per tile on a tile-aligned grid (TEPI_SPLIT_F32)
   uint32_t tmem_cols;
   size_t smem, counter_bytes, partial_bytes;
 };
@@ -917,6 +931,11 @@ static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
   // Under full stream-K the CTAs that hold pieces of two split tiles reduce
   // both, one after the other, and set the end of the kernel (measured tail
   // after the last MMA: 8-11 us at M 8-80).
+  // The split-partial epilogue always takes the tile-aligned grid (with one
+  // CTA per tile when there are more tiles than SMs): its consumer needs every
+  // tile split the same way.
+  const bool split_out = (epi == TEPI_SPLIT_F32);
+  if (pl.tiles >= sms && split_out) pl.grid = pl.tiles;
   if (pl.tiles < sms) {
     const int per_tile = sms / pl.tiles < pl.kblocks ? sms / pl.tiles : pl.kblocks;
     const int g = pl.tiles * per_tile;
@@ -924,12 +943,18 @@ static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
     if (per_tile + 1 <= pl.kblocks && (int64_t)g_up * 100 <= (int64_t)sms * 105 &&
         2 * (pl.smem + 1024) <= (size_t)228 * 1024)
       pl.grid = g_up;
-    else if ((int64_t)g * 10 >= (int64_t)sms * 9)
+    else if ((int64_t)g * 10 >= (int64_t)sms * 9 || split_out)
       pl.grid = g;
   }
-  pl.counter_bytes = kTcCounterBytes;
-  pl.partial_bytes = (size_t)pl.grid * 2 * pl.accs * pl.BN * kTcTileN * 4;
+  pl.splits = pl.grid / pl.tiles;
+  pl.counter_bytes = split_out ? 0 : kTcCounterBytes;
+  pl.partial_bytes = split_out ? 0 : (size_t)pl.grid * 2 * pl.accs * pl.BN * kTcTileN * 4;
   return pl;
+}
+
+int tc_split_count(int64_t m, int64_t k, int64_t n_out, int64_t* splits) {
+  *splits = tc_plan(m, k, n_out, TEPI_SPLIT_F32).splits;
+  return LS_OK;
 }
 
 int tc_workspace_bytes(int64_t m, int64_t k, int64_t n_out, int epi, int64_t* bytes) {
@@ -978,7 +1003,7 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
   if (m < 1 || m > 128) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "gemm_tc: m=%lld outside 1..128", (long long)m);
   if (k < 8 || k % 8 || n_out < 1) return set_error(LS_ERR_MISALIGNED, "gemm_tc: k=%lld must be a positive multiple of 8",
                                                     (long long)k);
-  if (!aligned16(x) || (!w_tiled && !aligned16(w)) || !aligned16(workspace))
+  if (!aligned16(x) || (!w_tiled && !aligned16(w)) || (workspace && !aligned16(workspace)))
     return set_error(LS_ERR_MISALIGNED, "gemm_tc: x, w and the workspace must be 16-byte aligned");
   if (epi == TEPI_RESIDUAL && !residual) return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_tc: residual is null");
   TcPlan pl = tc_plan(m, k, n_out, epi);
@@ -986,7 +1011,9 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
   if (pl.tiles > kTcMaxTiles)
     return set_error(LS_ERR_UNSUPPORTED_SHAPE, "gemm_tc: n=%lld has more than %d row tiles", (long long)n_out,
                      kTcMaxTiles);
-  if (!workspace || workspace_bytes < (int64_t)(pl.counter_bytes + pl.partial_bytes))
+  if (epi == TEPI_SPLIT_F32 && !aligned16(out))
+    return set_error(LS_ERR_MISALIGNED, "gemm_tc: split partial output must be 16-byte aligned");
+  if (epi != TEPI_SPLIT_F32 && (!workspace || workspace_bytes < (int64_t)(pl.counter_bytes + pl.partial_bytes)))
     return set_error(LS_ERR_WORKSPACE, "gemm_tc: workspace needs %zu bytes", pl.counter_bytes + pl.partial_bytes);
   if (!w_tiled && epi == TEPI_SILU_MUL && ((n_out * k * 2) % 16))
     return set_error(LS_ERR_MISALIGNED, "gemm_tc: up-projection view misaligned");
@@ -1011,8 +1038,8 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
   TcParams p = {};
   p.residual = static_cast<const __nv_bfloat16*>(residual);
   p.out = static_cast<__nv_bfloat16*>(out);
-  p.counters = static_cast<unsigned int*>(workspace);
-  p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.counter_bytes);
+  p.counters = workspace ? static_cast<unsigned int*>(workspace) : nullptr;
+  p.partial = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.counter_bytes) : nullptr;
   p.err = device_error_ptr();
   p.B = (int)m;
   p.BN = pl.BN;
@@ -1034,6 +1061,7 @@ int launch_gemm_tc(const void* x, int64_t m, int64_t k, const void* w, int64_t n
     case TEPI_RESIDUAL: return launch_tc_t<TEPI_RESIDUAL>(mw, mw2, mx, p, pl, stream);
     case TEPI_SILU_MUL: return launch_tc_t<TEPI_SILU_MUL>(mw, mw2, mx, p, pl, stream);
     case TEPI_STORE_F32: return launch_tc_t<TEPI_STORE_F32>(mw, mw2, mx, p, pl, stream);
+    case TEPI_SPLIT_F32: return launch_tc_t<TEPI_SPLIT_F32>(mw, mw2, mx, p, pl, stream);
     default: return set_error(LS_ERR_INVALID_ARGUMENT, "gemm_tc: unknown epilogue %d", epi);
   }
 }

@@ -96,6 +96,16 @@ class DecodeEngine:
             self.xn = torch.zeros(T, g.hidden_size, device=dev, dtype=runtime.dtype)
             self.logits = torch.zeros(T, self.vocab_rows, device=dev, dtype=runtime.dtype)
             self.lm_ws = torch.zeros(K.argmax_workspace_bytes(T, self.vocab_rows), device=dev, dtype=torch.uint8)
+            # Split fp32 partials of QKV / o_proj / down (one GPU): the GEMMs
+            # leave the cross-split sum to the next kernel (q/k norm, residual +
+            # RMSNorm) instead of reducing behind a grid-wide wait.
+            self.tc_part = None
+            if self.tp is None:
+                part = max(K.gemm_splits(mm, k_, n_) * mm * n_
+                           for mm in range(batch_size, T + 1, batch_size)
+                           for k_, n_ in ((g.hidden_size, g.qkv_dim), (g.q_dim, g.hidden_size),
+                                          (g.intermediate_size, g.hidden_size)))
+                self.tc_part = torch.zeros(part, device=dev, dtype=torch.float32)
         else:
             self.lm_ws = torch.zeros(K.lmhead_workspace_bytes(self.T, self.vocab_rows), device=dev,
                                      dtype=torch.uint8)
@@ -130,20 +140,37 @@ class DecodeEngine:
         eps = g.rms_norm_eps
         kv = self.kv
         tc = self.backend == "tc"
+        split = tc and self.tp is None  # split-partial GEMMs, summed by the consumer kernels
+        part = self.tc_part if split else None
+        s_down = 0
         K.embed_gather(a.ids[:m], rt.embed_tokens_weight, out=a.x[:m])
         for li, layer in enumerate(rt.layers):
             att, mlp = layer.attention, layer.mlp
             tt = self.tc_tiles[li] if (tc and self.tc_tiles is not None) else {}
             # QKV projection (with the input RMSNorm) into a.qkv
-            if tc:
-                K.rmsnorm(a.x[:m], layer.input_layernorm_weight, eps, out=self.xn[:m])
-                K.gemm_tc(self.xn[:m], att.qkv_proj_weight, out=a.qkv[:m], workspace=self.tc_ws, tiled=tt.get("qkv"))
+            if split:
+                if li == 0:
+                    K.rmsnorm(a.x[:m], layer.input_layernorm_weight, eps, out=self.xn[:m])
+                else:  # the previous layer's down residual, then this layer's input norm
+                    K.residual_rmsnorm_splits(part, s_down, a.h[:m], out_residual=a.x[:m],
+                                              norm_w=layer.input_layernorm_weight, eps=eps, out_norm=self.xn[:m])
+                s_qkv = K.gemm_tc_splits(self.xn[:m], att.qkv_proj_weight, part, tiled=tt.get("qkv"))
+                K.qk_norm_rope_splits(part, s_qkv, B, q_len, g.num_attention_heads, g.num_key_value_heads,
+                                      g.head_dim, att.q_norm_weight, att.k_norm_weight, self.cos, self.sin, eps=eps,
+                                      cache_pos=kv.cache_pos, k_cache=kv.key_cache[li], v_cache=kv.value_cache[li],
+                                      max_seq=self.S, q_out=a.q[:m])
             else:
-                K.linear(a.x[:m], att.qkv_proj_weight, norm_w=layer.input_layernorm_weight, eps=eps, out=a.qkv[:m])
-            K.qk_norm_rope(a.qkv[:m], B, q_len, g.num_attention_heads, g.num_key_value_heads, g.head_dim,
-                           att.q_norm_weight, att.k_norm_weight, self.cos, self.sin, eps=eps,
-                           cache_pos=kv.cache_pos, k_cache=kv.key_cache[li], v_cache=kv.value_cache[li],
-                           max_seq=self.S, q_out=a.q[:m])
+                if tc:
+                    K.rmsnorm(a.x[:m], layer.input_layernorm_weight, eps, out=self.xn[:m])
+                    K.gemm_tc(self.xn[:m], att.qkv_proj_weight, out=a.qkv[:m], workspace=self.tc_ws,
+                              tiled=tt.get("qkv"))
+                else:
+                    K.linear(a.x[:m], att.qkv_proj_weight, norm_w=layer.input_layernorm_weight, eps=eps,
+                             out=a.qkv[:m])
+                K.qk_norm_rope(a.qkv[:m], B, q_len, g.num_attention_heads, g.num_key_value_heads, g.head_dim,
+                               att.q_norm_weight, att.k_norm_weight, self.cos, self.sin, eps=eps,
+                               cache_pos=kv.cache_pos, k_cache=kv.key_cache[li], v_cache=kv.value_cache[li],
+                               max_seq=self.S, q_out=a.q[:m])
             K.decode_attention(a.q[:m], kv.key_cache[li], kv.value_cache[li], B, q_len, g.num_attention_heads,
                                g.num_key_value_heads, g.head_dim, self.S, att.attention_scale,
                                cache_pos=kv.cache_pos, out=a.attn[:m], workspace=self.attn_ws)
@@ -157,19 +184,24 @@ class DecodeEngine:
                     K.gateup_silu(a.h[:m], layer.post_attention_layernorm_weight, mlp.gate_up_proj_weight, eps,
                                   out=a.act[:m])
                 self._row_split(a.act[:m], mlp.down_proj_weight, a.h[:m], a.x[:m], tc, tt.get("down"))
-            elif tc:
-                K.gemm_tc(a.attn[:m], att.o_proj_weight, epilogue=K.EPI_RESIDUAL, residual=a.x[:m], out=a.h[:m],
-                          workspace=self.tc_ws, tiled=tt.get("o"))
-                K.rmsnorm(a.h[:m], layer.post_attention_layernorm_weight, eps, out=self.xn[:m])
+            elif split:
+                s_o = K.gemm_tc_splits(a.attn[:m], att.o_proj_weight, part, tiled=tt.get("o"))
+                K.residual_rmsnorm_splits(part, s_o, a.x[:m], out_residual=a.h[:m],
+                                          norm_w=layer.post_attention_layernorm_weight, eps=eps, out_norm=self.xn[:m])
                 K.gemm_tc(self.xn[:m], mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=a.act[:m],
                           workspace=self.tc_ws, tiled=tt.get("gu"))
-                K.gemm_tc(a.act[:m], mlp.down_proj_weight, epilogue=K.EPI_RESIDUAL, residual=a.h[:m],
-                          out=a.x[:m], workspace=self.tc_ws, tiled=tt.get("down"))
+                s_down = K.gemm_tc_splits(a.act[:m], mlp.down_proj_weight, part, tiled=tt.get("down"))
             else:
                 K.oproj_residual(a.attn[:m], att.o_proj_weight, a.x[:m], out=a.h[:m])
                 K.gateup_silu(a.h[:m], layer.post_attention_layernorm_weight, mlp.gate_up_proj_weight, eps,
                               out=a.act[:m])
                 K.down_residual(a.act[:m], mlp.down_proj_weight, a.h[:m], out=a.x[:m])
+        normed = False
+        if split:  # the last layer's down residual (+ the final norm when the head takes every row)
+            normed = bool(head) and (head == "all" or q_len == 1)
+            K.residual_rmsnorm_splits(part, s_down, a.h[:m], out_residual=a.x[:m],
+                                      norm_w=rt.final_norm_weight if normed else None, eps=eps,
+                                      out_norm=self.xn[:m] if normed else None)
         if head:
             if head == "all":
                 rows, n, dest = a.x[:m], m, self.verdict[:m]
@@ -178,12 +210,13 @@ class DecodeEngine:
             else:
                 a.head_rows.copy_(a.x[:m].view(B, q_len, -1)[:, -1])
                 rows, n, dest = a.head_rows, B, a.ids[:B]
-            self._head(rows, n, dest, tc)
+            self._head(rows, n, dest, tc, normed=normed)
         if advance:
             K.advance_cursors(kv.cache_pos, q_len)
 
-    def _head(self, rows: torch.Tensor, n: int, dest: torch.Tensor, tc: bool) -> None:
-        """Greedy head over ``rows [n, H]``: final norm, lm_head (this rank's vocab shard), argmax into ``dest``."""
+    def _head(self, rows: torch.Tensor, n: int, dest: torch.Tensor, tc: bool, normed: bool = False) -> None:
+        """Greedy head over ``rows [n, H]``: final norm, lm_head (this rank's vocab shard), argmax into ``dest``.
+        ``normed``: ``xn[:n]`` already holds the final norm of ``rows`` (tensor-core path)."""
         rt, eps = self.rt, self.g.rms_norm_eps
         self._head_rows = rows
         if self.tp is not None:
@@ -198,7 +231,8 @@ class DecodeEngine:
             self.tp.all_reduce_max(keys)
             K.argmax_keys_to_ids(keys, out_ids=dest)
         elif tc:
-            K.rmsnorm(rows, rt.final_norm_weight, eps, out=self.xn[:n])
+            if not normed:
+                K.rmsnorm(rows, rt.final_norm_weight, eps, out=self.xn[:n])
             K.gemm_tc(self.xn[:n], rt.lm_head_weight, out=self.logits[:n], workspace=self.tc_ws)
             K.argmax_rows(self.logits[:n], out_ids=dest, workspace=self.lm_ws)
         else:

@@ -13,7 +13,7 @@ import ctypes
 import torch
 
 from . import _native as nat
-from ._native import EPI_RESIDUAL, EPI_SILU_MUL, EPI_STORE, EPI_STORE_F32  # noqa: F401
+from ._native import EPI_RESIDUAL, EPI_SILU_MUL, EPI_SPLIT_F32, EPI_STORE, EPI_STORE_F32  # noqa: F401
 
 BF16 = torch.bfloat16
 
@@ -154,6 +154,26 @@ def qk_norm_rope(qkv: torch.Tensor, batch: int, q_len: int, num_heads: int, num_
              q_norm_w.data_ptr(), k_norm_w.data_ptr(), float(eps), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
              int(rope_offset), _ptr(cache_pos), int(uniform_past), _ptr(k_cache), _ptr(v_cache), int(max_seq),
              _ptr(k_out), _ptr(v_out), q_out.data_ptr(), _stream())
+    return q_out
+
+
+def qk_norm_rope_splits(part: torch.Tensor, splits: int, batch: int, q_len: int, num_heads: int,
+                        num_kv_heads: int, head_dim: int, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor,
+                        cos: torch.Tensor, sin: torch.Tensor, *, eps: float = 1e-6,
+                        cache_pos: torch.Tensor | None = None, uniform_past: int = 0, rope_offset: int = 0,
+                        k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None, max_seq: int = 0,
+                        q_out: torch.Tensor) -> torch.Tensor:
+    """:func:`qk_norm_rope` on the split fp32 partials of the QKV projection (``gemm_tc_splits``)."""
+    _check(part, "part", torch.float32)
+    m = batch * q_len
+    if part.numel() < splits * m * (num_heads + 2 * num_kv_heads) * head_dim:
+        raise ValueError("split partials smaller than splits x m x qkv_dim")
+    if cache_pos is not None:
+        _check(cache_pos, "cache_pos", torch.int32)
+    nat.call("ls_qk_norm_rope_kvappend_splits", part.data_ptr(), splits, batch, q_len, num_heads, num_kv_heads,
+             head_dim, q_norm_w.data_ptr(), k_norm_w.data_ptr(), float(eps), cos.data_ptr(), sin.data_ptr(),
+             cos.shape[0], int(rope_offset), _ptr(cache_pos), int(uniform_past), _ptr(k_cache), _ptr(v_cache),
+             int(max_seq), None, None, q_out.data_ptr(), _stream())
     return q_out
 
 
@@ -350,6 +370,56 @@ def gemm_tc(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = EPI_STORE, resi
         nat.call("ls_gemm_bf16_tcgen05", x.data_ptr(), m, k, w.data_ptr(), n, int(epilogue), _ptr(residual),
                  out.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream())
     return out
+
+
+def gemm_splits(m: int, k: int, n: int) -> int:
+    """k-splits of the ``EPI_SPLIT_F32`` form of :func:`gemm_tc` (its output is ``[splits, m, n]`` fp32)."""
+    v = ctypes.c_int64(0)
+    nat.call("ls_gemm_bf16_tcgen05_splits", m, k, n, ctypes.byref(v))
+    return v.value
+
+
+def gemm_tc_splits(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *,
+                   tiled: torch.Tensor | None = None) -> int:
+    """tcgen05 GEMM with the split-partial epilogue: ``out[:splits*m*n]`` (fp32,
+    viewed as ``[splits, m, n]``) receives one unrounded partial of ``x @ w.T``
+    per k-split; returns ``splits``.  The consumer adds them in split order."""
+    _check(x, "x")
+    _check(w, "w")
+    _check(out, "out", torch.float32)
+    k = x.shape[-1]
+    m = x.numel() // k
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"weight in-features {w.shape[1]} != activation width {k}")
+    s = gemm_splits(m, k, n)
+    if out.numel() < s * m * n:
+        raise ValueError(f"split output holds {out.numel()} floats, needs {s} x {m} x {n}")
+    if tiled is not None:
+        nat.call("ls_gemm_bf16_tcgen05_tiled", x.data_ptr(), m, k, tiled.data_ptr(), n, EPI_SPLIT_F32, None,
+                 out.data_ptr(), None, 0, _stream())
+    else:
+        nat.call("ls_gemm_bf16_tcgen05", x.data_ptr(), m, k, w.data_ptr(), n, EPI_SPLIT_F32, None, out.data_ptr(),
+                 None, 0, _stream())
+    return s
+
+
+def residual_rmsnorm_splits(part: torch.Tensor, splits: int, residual: torch.Tensor, *, out_residual: torch.Tensor,
+                            norm_w: torch.Tensor | None = None, eps: float = 1e-6,
+                            out_norm: torch.Tensor | None = None) -> None:
+    """``out_residual = bf16(residual + bf16(sum_s part[s]))`` over ``[m, n]`` rows,
+    then (with ``norm_w``) ``out_norm = rmsnorm(out_residual) * norm_w``."""
+    _check(part, "part", torch.float32)
+    _check(residual, "residual")
+    _check(out_residual, "out_residual")
+    n = residual.shape[-1]
+    m = residual.numel() // n
+    if part.numel() < splits * m * n:
+        raise ValueError("split partials smaller than splits x m x n")
+    if (norm_w is None) != (out_norm is None):
+        raise ValueError("norm_w and out_norm come together")
+    nat.call("ls_residual_rmsnorm_splits", part.data_ptr(), splits, m, n, residual.data_ptr(), _ptr(norm_w),
+             float(eps), out_residual.data_ptr(), _ptr(out_norm), _stream())
 
 
 def gemm_big(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,

@@ -179,6 +179,27 @@ def main(argv=None) -> int:
                                           tiled=tl[i % C]), args.reps)
             out[f"tc_tiled_{name}(m={m})"] = (t, n_rows * k_dim * 2)
             del tl
+            if epi in (K.EPI_STORE, K.EPI_RESIDUAL) and n_out != g.vocab_size:
+                # split-partial form: the GEMM alone, and for the residual
+                # linears the pair (GEMM + residual/RMSNorm consumer) against
+                # (residual GEMM + RMSNorm)
+                part = torch.empty(K.gemm_splits(m, k_dim, n_out) * m * n_out, device=dev)
+                t = _time(lambda i: K.gemm_tc_splits(xa, wts[i % C], part), args.reps)
+                out[f"tc_split_{name}(m={m})"] = (t, n_rows * k_dim * 2)
+                if epi == K.EPI_RESIDUAL:
+                    s_ = K.gemm_splits(m, k_dim, n_out)
+                    xn_ = torch.empty_like(o)
+
+                    def pair_new(i):
+                        K.gemm_tc_splits(xa, wts[i % C], part)
+                        K.residual_rmsnorm_splits(part, s_, res, out_residual=o, norm_w=nw[:n_out], eps=1e-6,
+                                                  out_norm=xn_)
+
+                    def pair_old(i):
+                        K.gemm_tc(xa, wts[i % C], epilogue=epi, residual=res, out=o, workspace=ws_)
+                        K.rmsnorm(o, nw[:n_out], 1e-6, out=xn_)
+                    out[f"tc_pair_split_{name}+norm(m={m})"] = (_time(pair_new, args.reps), n_rows * k_dim * 2)
+                    out[f"tc_pair_reduce_{name}+norm(m={m})"] = (_time(pair_old, args.reps), n_rows * k_dim * 2)
         if "tc_qkv" in tc:
             tc_case("qkv", g.qkv_dim, H, K.EPI_STORE, g.qkv_dim)
         if "tc_oproj" in tc:
