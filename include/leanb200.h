@@ -343,6 +343,15 @@ int ls_residual_rmsnorm_splits(const float* part, int64_t splits, int64_t m, int
                                const void* norm_w, float eps, void* out_residual, void* out_norm,
                                ls_stream_t stream);
 
+/* SiLU(gate) * up over the split partials of the fused gate_up projection run
+ * as a plain [2I, k] linear (LS_EPI_SPLIT_F32, part = [splits][m][2I]):
+ * act[m, I] = bf16(bf16(silu(bf16(g))) * bf16(u)), the MLP epilogue of
+ * src/leanstack/runtime/qwen_explicit.py:932-949.  With whole-K tiles (one
+ * split when the gate_up rows give at least one 128-row tile per SM) the
+ * GEMM needs no cross-CTA reduction at all. */
+int ls_silu_mul_splits(const float* part, int64_t splits, int64_t m, int64_t intermediate, void* act,
+                       ls_stream_t stream);
+
 /* cache_pos[b] += delta[b] (delta NULL: += q_len): moves the device cursors
  * after a step, the device-side counterpart of the reference's host cursor
  * bookkeeping (src/leanstack/runtime/kv_cache.py:239-245, :298-318). */

@@ -150,6 +150,41 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_splits_kernel(cons
   }
 }
 
+// SiLU(gate) * up from the split fp32 partials of the gate_up projection run
+// as a plain [2I, K] GEMM (LS_EPI_SPLIT_F32): g = bf16(sum_j part[j][b][i]),
+// u = bf16(sum_j part[j][b][I + i]), act = bf16(bf16(silu(g)) * u) -- the
+// rounding points of the reference's MLP (qwen_explicit.py:932-949) and of
+// the GEMM's paired SiLU epilogue.  Four outputs per thread.
+__global__ void silu_mul_splits_kernel(const float* part, int splits, int m, int inter, __nv_bfloat16* act) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const int q = inter / 4;
+  const size_t slab = (size_t)m * 2 * inter;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < (int64_t)m * q;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(e / q), i = (int)(e - (int64_t)b * q) * 4;
+    const float* pg = part + (size_t)b * 2 * inter + i;
+    float4 g = __ldcg(reinterpret_cast<const float4*>(pg));
+    float4 u = __ldcg(reinterpret_cast<const float4*>(pg + inter));
+    for (int j = 1; j < splits; ++j) {
+      const float4 g2 = __ldcg(reinterpret_cast<const float4*>(pg + j * slab));
+      const float4 u2 = __ldcg(reinterpret_cast<const float4*>(pg + j * slab + inter));
+      g.x += g2.x, g.y += g2.y, g.z += g2.z, g.w += g2.w;
+      u.x += u2.x, u.y += u2.y, u.z += u2.z, u.w += u2.w;
+    }
+    const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
+    float o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float gr = round_bf16(gv[j]);
+      o[j] = round_bf16(gr / (1.0f + expf(-gr))) * round_bf16(uv[j]);
+    }
+    __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]), hi = __floats2bfloat162_rn(o[2], o[3]);
+    *reinterpret_cast<uint2*>(act + (size_t)b * inter + i) =
+        make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+  }
+}
+
 // Row argmax over bf16 logits: grid (chunks, m); each CTA reduces one chunk of
 // one row, the last CTA of the row reduces the chunk winners.
 constexpr int kArgmaxThreads = 256;
@@ -766,6 +801,31 @@ int ls_residual_rmsnorm_splits(const float* part, int64_t splits, int64_t m, int
                                      static_cast<const __nv_bfloat16*>(norm_w), eps,
                                      static_cast<__nv_bfloat16*>(out_residual), static_cast<__nv_bfloat16*>(out_norm));
   return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "residual_norm_splits launch: %s", cudaGetErrorString(e));
+}
+
+int ls_silu_mul_splits(const float* part, int64_t splits, int64_t m, int64_t intermediate, void* act,
+                       ls_stream_t stream) {
+  LS_REQUIRE(part && act, LS_ERR_INVALID_ARGUMENT, "ls_silu_mul_splits: null pointer");
+  LS_REQUIRE(splits >= 1 && m > 0 && intermediate > 0 && m * intermediate < (1ll << 40), LS_ERR_INVALID_ARGUMENT,
+             "ls_silu_mul_splits: bad sizes");
+  LS_REQUIRE(intermediate % 4 == 0 && aligned16(part) && aligned16(act), LS_ERR_MISALIGNED,
+             "ls_silu_mul_splits: intermediate must be a multiple of 4, pointers 16-byte aligned");
+  const int64_t items = m * intermediate / 4;
+  const int threads = 256;
+  int64_t blocks = (items + threads - 1) / threads;
+  if (blocks > 4 * (int64_t)sm_count()) blocks = 4 * (int64_t)sm_count();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(threads);
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, lsb::silu_mul_splits_kernel, part, (int)splits, (int)m, (int)intermediate,
+                                     static_cast<__nv_bfloat16*>(act));
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "silu_mul_splits launch: %s", cudaGetErrorString(e));
 }
 
 int ls_advance_cursors(int32_t* cache_pos, const int32_t* delta, int64_t batch, int64_t q_len, ls_stream_t stream) {

@@ -935,7 +935,15 @@ static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
   // CTA per tile when there are more tiles than SMs): its consumer needs every
   // tile split the same way.
   const bool split_out = (epi == TEPI_SPLIT_F32);
-  if (pl.tiles >= sms && split_out) pl.grid = pl.tiles;
+  if (pl.tiles >= sms && split_out) {
+    // One CTA per whole-K tile.  Up to twice the SM count, two CTAs share an
+    // SM, so the ring is cut until two fit (at least two stages).
+    pl.grid = pl.tiles;
+    while (pl.stages > 2 && 2 * (1024 + (size_t)pl.stages * pl.stage_bytes + (size_t)(2 * pl.stages + 6) * 8 + 16 +
+                                 1024) > (size_t)228 * 1024)
+      --pl.stages;
+    pl.smem = 1024 + (size_t)pl.stages * pl.stage_bytes + (size_t)(2 * pl.stages + 6) * 8 + 16;
+  }
   if (pl.tiles < sms) {
     const int per_tile = sms / pl.tiles < pl.kblocks ? sms / pl.tiles : pl.kblocks;
     const int g = pl.tiles * per_tile;

@@ -85,6 +85,7 @@ class DecodeEngine:
         ws = max(K.attention_workspace_bytes(batch_size, q, g.num_attention_heads, g.num_key_value_heads, g.head_dim,
                                              self.S) for q in range(1, self.T // batch_size + 1))
         self.attn_ws = torch.zeros(max(ws, 256), device=dev, dtype=torch.uint8)
+        self.gu_plain = False
         if self.backend == "tc":
             T = self.T
             row_epi = K.EPI_STORE_F32 if self.tp is not None else K.EPI_RESIDUAL
@@ -100,11 +101,18 @@ class DecodeEngine:
             # leave the cross-split sum to the next kernel (q/k norm, residual +
             # RMSNorm) instead of reducing behind a grid-wide wait.
             self.tc_part = None
+            # gate_up as a plain [2I, H] linear with whole-K tiles (one split:
+            # no reduction across CTAs) when its 128-row tiles cover the SMs,
+            # followed by the SiLU*up combine; else the paired SiLU epilogue.
+            self.gu_plain = self.tp is None and all(
+                K.gate_up_whole_k(mm, g.hidden_size, 2 * g.intermediate_size)
+                for mm in range(batch_size, T + 1, batch_size))
             if self.tp is None:
+                shapes_ = [(g.hidden_size, g.qkv_dim), (g.q_dim, g.hidden_size), (g.intermediate_size, g.hidden_size)]
+                if self.gu_plain:
+                    shapes_.append((g.hidden_size, 2 * g.intermediate_size))
                 part = max(K.gemm_splits(mm, k_, n_) * mm * n_
-                           for mm in range(batch_size, T + 1, batch_size)
-                           for k_, n_ in ((g.hidden_size, g.qkv_dim), (g.q_dim, g.hidden_size),
-                                          (g.intermediate_size, g.hidden_size)))
+                           for mm in range(batch_size, T + 1, batch_size) for k_, n_ in shapes_)
                 self.tc_part = torch.zeros(part, device=dev, dtype=torch.float32)
         else:
             self.lm_ws = torch.zeros(K.lmhead_workspace_bytes(self.T, self.vocab_rows), device=dev,
@@ -188,8 +196,12 @@ class DecodeEngine:
                 s_o = K.gemm_tc_splits(a.attn[:m], att.o_proj_weight, part, tiled=tt.get("o"))
                 K.residual_rmsnorm_splits(part, s_o, a.x[:m], out_residual=a.h[:m],
                                           norm_w=layer.post_attention_layernorm_weight, eps=eps, out_norm=self.xn[:m])
-                K.gemm_tc(self.xn[:m], mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=a.act[:m],
-                          workspace=self.tc_ws, tiled=tt.get("gu"))
+                if self.gu_plain:  # (the paired tile image is the plain one when I is a multiple of 128)
+                    s_gu = K.gemm_tc_splits(self.xn[:m], mlp.gate_up_proj_weight, part, tiled=tt.get("gu"))
+                    K.silu_mul_splits(part, s_gu, m, g.intermediate_size, out=a.act[:m])
+                else:
+                    K.gemm_tc(self.xn[:m], mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=a.act[:m],
+                              workspace=self.tc_ws, tiled=tt.get("gu"))
                 s_down = K.gemm_tc_splits(a.act[:m], mlp.down_proj_weight, part, tiled=tt.get("down"))
             else:
                 K.oproj_residual(a.attn[:m], att.o_proj_weight, a.x[:m], out=a.h[:m])
@@ -451,7 +463,7 @@ class DecodeEngine:
 
     def kernel_launches_per_step(self) -> int:
         """Kernels one decode step launches (embedding, layers, head, cursor advance)."""
-        per_layer = 8 if self.backend == "tc" else 6
+        per_layer = (9 if self.gu_plain else 8) if self.backend == "tc" else 6
         head = 3 if self.backend == "tc" else 1
         if self.tp is not None:  # + all-reduce / residual-add kernels after each row-split linear, + keys-to-ids
             if self.tp.p2p is None or self.backend == "tc":

@@ -422,6 +422,27 @@ def residual_rmsnorm_splits(part: torch.Tensor, splits: int, residual: torch.Ten
              float(eps), out_residual.data_ptr(), _ptr(out_norm), _stream())
 
 
+def gate_up_whole_k(m: int, k: int, n_rows: int) -> bool:
+    """Whether the fused gate_up linear ``[n_rows = 2I, k]`` at ``m`` rows runs as a
+    plain linear with whole-K tiles (split-partial form with one split, then
+    :func:`silu_mul_splits`): its 128-row tiles cover at least 90% of the SMs,
+    I is a multiple of 128 (the paired tile image is then the plain one) and the
+    plan gives one split.  Otherwise the paired SiLU epilogue runs."""
+    tiles = -(-n_rows // 128)
+    return ((n_rows // 2) % 128 == 0 and tiles * 10 >= 9 * sm_count()
+            and gemm_splits(m, k, n_rows) == 1)
+
+
+def silu_mul_splits(part: torch.Tensor, splits: int, m: int, intermediate: int, *, out: torch.Tensor) -> None:
+    """``out[m, I] = bf16(bf16(silu(bf16(g))) * bf16(u))`` from the split partials
+    ``part [splits, m, 2I]`` of the gate_up projection run as a plain linear."""
+    _check(part, "part", torch.float32)
+    _check(out, "out")
+    if part.numel() < splits * m * 2 * intermediate or out.numel() < m * intermediate:
+        raise ValueError("silu_mul_splits: buffers smaller than the shapes")
+    nat.call("ls_silu_mul_splits", part.data_ptr(), splits, m, intermediate, out.data_ptr(), _stream())
+
+
 def gemm_big(x: torch.Tensor, w: torch.Tensor, *, epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,
              out: torch.Tensor | None = None) -> torch.Tensor:
     """Large-M tcgen05 GEMM (prefill): ``out = epilogue(x @ w.T)`` for x ``[m, k]`` with m in the thousands."""

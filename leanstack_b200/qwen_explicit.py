@@ -186,7 +186,9 @@ def _linear_routed(x: torch.Tensor, w: torch.Tensor, *, norm_w: torch.Tensor | N
     """``epilogue(w @ rmsnorm?(x))`` for x ``[m, k]``, on the kernel family for m.
 
     m <= 8: CUDA-core streaming linear with the RMSNorm in its prologue;
-    m <= 128: RMSNorm kernel, then the tcgen05 weight-streaming GEMM;
+    m <= 128: RMSNorm kernel, then the tcgen05 weight-streaming GEMM (gate_up
+    as a plain whole-K linear + the SiLU*up combine where the engine's step
+    runs it so, giving the engine's bits);
     larger: RMSNorm kernel, then the persistent large-M tcgen05 GEMM.
     """
     m = x.shape[0]
@@ -194,6 +196,12 @@ def _linear_routed(x: torch.Tensor, w: torch.Tensor, *, norm_w: torch.Tensor | N
         return K.linear(x, w, norm_w=norm_w, eps=eps, epilogue=epilogue, residual=residual)
     xn = K.rmsnorm(x, norm_w, eps) if norm_w is not None else x
     if m <= TC_MAX_M:
+        if epilogue == K.EPI_SILU_MUL and K.gate_up_whole_k(m, w.shape[1], w.shape[0]):
+            part = torch.empty(m * w.shape[0], device=x.device, dtype=torch.float32)
+            s = K.gemm_tc_splits(xn, w, part)
+            act = torch.empty(m, w.shape[0] // 2, device=x.device, dtype=x.dtype)
+            K.silu_mul_splits(part, s, m, w.shape[0] // 2, out=act)
+            return act
         return K.gemm_tc(xn, w, epilogue=epilogue, residual=residual)
     return K.gemm_big(xn, w, epilogue=epilogue, residual=residual)
 

@@ -206,6 +206,19 @@ def main(argv=None) -> int:
             tc_case("oproj", H, g.q_dim, K.EPI_RESIDUAL, H)
         if "tc_gateup" in tc:
             tc_case("gateup", 2 * I, H, K.EPI_SILU_MUL, I)
+            # plain [2I, H] linear with whole-K tiles (split-partial form) + the SiLU*up combine
+            wts = w((2 * I, H), "mb/gateup")
+            xa = synth.normal((m, H), 1.0, 0, "mb/xagateup", device=dev)
+            s_ = K.gemm_splits(m, H, 2 * I)
+            part = torch.empty(s_ * m * 2 * I, device=dev)
+            act = torch.empty(m, I, device=dev, dtype=torch.bfloat16)
+            out[f"tc_split_gateup(m={m})"] = (_time(lambda i: K.gemm_tc_splits(xa, wts[i % C], part), args.reps),
+                                              2 * I * H * 2)
+
+            def gu_pair(i):
+                K.gemm_tc_splits(xa, wts[i % C], part)
+                K.silu_mul_splits(part, s_, m, I, out=act)
+            out[f"tc_pair_split_gateup+silu(m={m})"] = (_time(gu_pair, args.reps), 2 * I * H * 2)
         if "tc_down" in tc:
             tc_case("down", H, I, K.EPI_RESIDUAL, H)
         if "tc_lmhead" in tc:

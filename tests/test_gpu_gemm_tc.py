@@ -254,3 +254,31 @@ def test_qk_norm_rope_on_split_partials(batch, q_len):
         outs.append((q, kc, vc))
     for a, b in zip(*outs):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("m", [1, 32, 80, 128])
+def test_gate_up_plain_split_and_silu_combine(m):
+    """gate_up as a plain [2I, H] linear in the split-partial form (whole-K
+    tiles: one split) followed by the SiLU*up combine: equal to the combine
+    computed in torch from the same partials (up to the last bit of expf), and
+    to the fp32 reference within the bound."""
+    inter, hidden = 9728, 2560
+    x = _rand((m, hidden), 1.0, "gpx")
+    w = _rand((2 * inter, hidden), 0.02, "gpw")
+    s = K.gemm_splits(m, hidden, 2 * inter)
+    part = torch.empty(s * m * 2 * inter, device=DEV)
+    assert K.gemm_tc_splits(x, w, part) == s
+    act = torch.empty(m, inter, device=DEV, dtype=torch.bfloat16)
+    K.silu_mul_splits(part, s, m, inter, out=act)
+    p = part.view(s, m, 2 * inter)
+    y = p[0].clone()
+    for j in range(1, s):
+        y += p[j]
+    g_u = y.bfloat16().float()
+    g = g_u[:, :inter]
+    want = ((g / (1.0 + torch.exp(-g))).bfloat16().float() * g_u[:, inter:]).bfloat16()
+    # same partials, same rounding points: equal up to the last bit of expf
+    assert (act == want).float().mean().item() > 0.999
+    assert (act.float() - want.float()).abs().max().item() <= 2 ** -6 * max(1.0, want.float().abs().max().item())
+    ref_gu = (x.float() @ w.float().t()).bfloat16()
+    _check(act, F.silu(ref_gu[:, :inter].float()).bfloat16().float() * ref_gu[:, inter:].float())
