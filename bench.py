@@ -453,14 +453,19 @@ def run_verify(rt, comm, shard, steps: int, warmup: int, world: int, peaks) -> d
     xs = eng.xn[:m]
     reps = 8
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    K.gemm_tc(xs, layer.mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=eng.arenas.act[:m],
-              workspace=eng.tc_ws)
+
+    def gate_up(w):  # what the verify step runs: whole-K linear + SiLU*up combine, or the paired GEMM
+        if eng.gu_plain:
+            s_ = K.gemm_tc_splits(xs, w, eng.tc_part)
+            K.silu_mul_splits(eng.tc_part, s_, m, gl.intermediate_size, out=eng.arenas.act[:m])
+        else:
+            K.gemm_tc(xs, w, epilogue=K.EPI_SILU_MUL, out=eng.arenas.act[:m], workspace=eng.tc_ws)
+    gate_up(layer.mlp.gate_up_proj_weight)
     torch.cuda.synchronize()
     e0.record()
     for i in range(reps):
         for lay in rt.layers:
-            K.gemm_tc(xs, lay.mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=eng.arenas.act[:m],
-                      workspace=eng.tc_ws)
+            gate_up(lay.mlp.gate_up_proj_weight)
     e1.record()
     torch.cuda.synchronize()
     per = e0.elapsed_time(e1) / 1000.0 / (reps * len(rt.layers))
@@ -470,7 +475,9 @@ def run_verify(rt, comm, shard, steps: int, warmup: int, world: int, peaks) -> d
            "verify_steps_per_s": steps / t, "ms_per_verify": 1000.0 * t / steps,
            "positions_per_s": steps * m / t, "committed_tok_per_s": committed / t,
            "proposals": "uniform random ids (accept rate ~0)",
-           "dominant_gemm": {"kernel": "gemm_tc_kernel<SILU_MUL> (gate_up + SiLU*up, M=80)", "us": per * 1e6,
+           "dominant_gemm": {"kernel": ("gemm_tc_kernel<SPLIT_F32> whole-K gate_up + silu_mul_splits (M=80)"
+                                        if eng.gu_plain else "gemm_tc_kernel<SILU_MUL> (gate_up + SiLU*up, M=80)"),
+                             "us": per * 1e6,
                              "gbs": w_bytes / per / 1e9, "hbm_frac": w_bytes / per / 1e9 / peaks["hbm_gbs"],
                              "tflops": flops / per / 1e12,
                              "tensor_frac": flops / per / 1e12 / peaks.get("bf16_tflops", 1663.3),

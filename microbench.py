@@ -51,6 +51,43 @@ def _time(fn, reps: int) -> float:
     return a.elapsed_time(b) / 1000.0 / reps
 
 
+def profile_step(kind: str) -> int:
+    """Random-init Qwen3-4B, prompt through ``prefill_full``, one captured step
+    replayed once untimed, then timed twice (CUDA events) inside NVTX 'step'."""
+    from leanstack_b200.engine import DecodeEngine
+    from leanstack_b200.leanserve import materialize_from_tensors
+
+    g = QWEN3_4B
+    dev = torch.device("cuda")
+    rt = materialize_from_tensors(g, synth.synth_checkpoint(g, 1, device=dev), device=dev, free_source=True)
+    B, cached, k = (32, 2048, 0) if kind == "bs32" else (16, 1024, 4)
+    eng = DecodeEngine(rt, batch_size=B, max_seq_len=cached + 64, linear_backend="tc")
+    eng.prefill_full(synth.token_ids((B, cached), g.vocab_size, 1, f"mb/step/{kind}"))
+    if kind == "bs32":
+        eng.capture()
+        step = eng.decode_step
+    else:
+        inp = eng.verify_inputs(k)
+        props = synth.token_ids((B, k), g.vocab_size, 1, "mb/step/props").to(dev)
+
+        def step():
+            inp[:, 1:].copy_(props)
+            eng.verify_step(k)
+    step()
+    torch.cuda.synchronize()
+    a, b = _events()
+    torch.cuda.nvtx.range_push("step")
+    a.record()
+    for _ in range(2):
+        step()
+    b.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print(json.dumps({"step": kind, "batch": B, "cached": cached, "ms_per_step": a.elapsed_time(b) / 2,
+                      "launches_per_step": eng.kernel_launches_per_step() if kind == "bs32" else None}))
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernels", default="qkv,attention,oproj,gateup,down,lmhead,qknorm,embed")
@@ -59,7 +96,13 @@ def main(argv=None) -> int:
     ap.add_argument("--seq", type=int, default=600, help="cached positions for attention")
     ap.add_argument("--copies", type=int, default=4)
     ap.add_argument("--batch", type=int, default=1, help="sequences of the prefill_attn case")
+    ap.add_argument("--step", choices=("bs32", "verify"), default=None,
+                    help="instead of kernels: one whole captured step of Qwen3-4B (config 3 bs32 decode over 2048 "
+                         "cached, or the config-4 verify pass), two replays inside the NVTX range 'step' "
+                         "(for `ncu --nvtx --nvtx-include step/`)")
     args = ap.parse_args(argv)
+    if args.step:
+        return profile_step(args.step)
     g = QWEN3_4B
     dev = torch.device("cuda")
     m, H, I = args.m, g.hidden_size, g.intermediate_size
