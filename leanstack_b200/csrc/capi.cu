@@ -31,27 +31,38 @@ __global__ void embed_gather_kernel(const int64_t* ids, const __nv_bfloat16* emb
 }
 
 // One CTA per row: y = bf16((x * rsqrt(mean(x^2) + eps)) * w).  Rows whose
-// length is a multiple of 8 (16-byte aligned) go through 16-byte vectors; the
-// second pass re-reads x from L1.  Launched with programmatic dependent launch:
-// the next kernel may start its own prologue (weight prefetch) at once.
-constexpr int kNormThreads = 256;
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const __nv_bfloat16* x, int n, const __nv_bfloat16* w,
-                                                               float eps, __nv_bfloat16* out, int vec) {
+// length is a multiple of 8 (16-byte aligned) go through 16-byte vectors, one
+// 8-column group per thread (norm_threads); the second pass re-reads x from
+// L1.  The sum of squares is taken per thread over its groups, then over the
+// lanes of a warp, then over the warps in order -- the order
+// residual_norm_splits_kernel uses with the same launch, so the two give
+// identical bits.  Launched with programmatic dependent launch: the next
+// kernel may start its own prologue (weight prefetch) at once.
+constexpr int kNormThreads = 256;     // scalar path
+constexpr int kNormMaxThreads = 1024;
+static inline int norm_threads(int64_t n, int vec) {
+  if (!vec) return kNormThreads;
+  const int64_t t = (n / 8 + 31) / 32 * 32;
+  return (int)(t < 32 ? 32 : (t > kNormMaxThreads ? kNormMaxThreads : t));
+}
+__global__ void __launch_bounds__(kNormMaxThreads) rmsnorm_kernel(const __nv_bfloat16* x, int n, const __nv_bfloat16* w,
+                                                                  float eps, __nv_bfloat16* out, int vec) {
   grid_dep_launch();
   grid_dep_wait();
-  __shared__ float red[kNormThreads / 32];
+  __shared__ float red[kNormMaxThreads / 32];
   const __nv_bfloat16* xr = x + (size_t)blockIdx.x * n;
   __nv_bfloat16* orow = out + (size_t)blockIdx.x * n;
+  const int nt = blockDim.x;
   float ss = 0.f;
   if (vec) {
-    for (int v = threadIdx.x; v < n / 8; v += kNormThreads) {
+    for (int v = threadIdx.x; v < n / 8; v += nt) {
       float f[8];
       unpack8(ldg16(xr + v * 8), f);
 #pragma unroll
       for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
     }
   } else {
-    for (int i = threadIdx.x; i < n; i += kNormThreads) {
+    for (int i = threadIdx.x; i < n; i += nt) {
       const float v = bf16_to_f(xr[i]);
       ss = fmaf(v, v, ss);
     }
@@ -60,11 +71,10 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const __nv_bfloat
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+  for (int i = 0; i < nt / 32; ++i) tot += red[i];
   const float r = rsqrtf(tot / (float)n + eps);
   if (vec) {
-    for (int v = threadIdx.x; v < n / 8; v += kNormThreads) {
+    for (int v = threadIdx.x; v < n / 8; v += nt) {
       float f[8], g[8];
       unpack8(ldg16(xr + v * 8), f);
       unpack8(ldg16(w + v * 8), g);
@@ -78,7 +88,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const __nv_bfloat
       *reinterpret_cast<uint4*>(orow + v * 8) = o;
     }
   } else {
-    for (int i = threadIdx.x; i < n; i += kNormThreads)
+    for (int i = threadIdx.x; i < n; i += nt)
       orow[i] = f_to_bf16((bf16_to_f(xr[i]) * r) * bf16_to_f(w[i]));
   }
 }
@@ -88,20 +98,24 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const __nv_bfloat
 // 1, ... (the order of the GEMM's in-kernel reduction), and, when w is not
 // null, y = bf16((h * rsqrt(mean(h^2) + eps)) * w) with the sum of squares
 // taken in rmsnorm_kernel's order, so both paths give identical bits.
-__global__ void __launch_bounds__(kNormThreads) residual_norm_splits_kernel(const float* part, int splits, int m, int n,
-                                                                            const __nv_bfloat16* residual,
-                                                                            const __nv_bfloat16* w, float eps,
-                                                                            __nv_bfloat16* out_res,
-                                                                            __nv_bfloat16* out_norm) {
+__global__ void __launch_bounds__(kNormMaxThreads) residual_norm_splits_kernel(const float* part, int splits, int m,
+                                                                                 int n, const __nv_bfloat16* residual,
+                                                                                 const __nv_bfloat16* w, float eps,
+                                                                                 __nv_bfloat16* out_res,
+                                                                                 __nv_bfloat16* out_norm) {
   grid_dep_launch();
   grid_dep_wait();
-  __shared__ float red[kNormThreads / 32];
+  __shared__ float red[kNormMaxThreads / 32];
   const size_t slab = (size_t)m * n;
   const float* pr = part + (size_t)blockIdx.x * n;
   const __nv_bfloat16* rr = residual + (size_t)blockIdx.x * n;
   __nv_bfloat16* hr = out_res + (size_t)blockIdx.x * n;
+  const int nv = n / 8;
+  // Thread t owns the 8-column groups t, t + blockDim, ... (one group when the
+  // launch gives a thread per group); the first group's h stays in registers.
+  uint4 h0 = make_uint4(0, 0, 0, 0);
   float ss = 0.f;
-  for (int v = threadIdx.x; v < n / 8; v += kNormThreads) {
+  for (int v = threadIdx.x; v < nv; v += blockDim.x) {
     float4 a0 = __ldcg(reinterpret_cast<const float4*>(pr + v * 8));
     float4 a1 = __ldcg(reinterpret_cast<const float4*>(pr + v * 8 + 4));
     for (int j = 1; j < splits; ++j) {
@@ -121,23 +135,25 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_splits_kernel(cons
       op[j] = *reinterpret_cast<uint32_t*>(&pr2);
     }
     *reinterpret_cast<uint4*>(hr + v * 8) = o;
+    if (v == threadIdx.x) h0 = o;
     float h[8];
     unpack8(o, h);
 #pragma unroll
     for (int j = 0; j < 8; ++j) ss = fmaf(h[j], h[j], ss);
   }
   if (!out_norm) return;
+  // Sum of squares in rmsnorm_kernel's order (same launch shape).
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+  const int nw = (blockDim.x + 31) / 32;
+  for (int i = 0; i < nw; ++i) tot += red[i];
   const float r = rsqrtf(tot / (float)n + eps);
   __nv_bfloat16* orow = out_norm + (size_t)blockIdx.x * n;
-  for (int v = threadIdx.x; v < n / 8; v += kNormThreads) {
+  for (int v = threadIdx.x; v < nv; v += blockDim.x) {
     float f[8], g[8];
-    unpack8(*reinterpret_cast<const uint4*>(hr + v * 8), f);  // this thread's own stores above
+    unpack8(v == threadIdx.x ? h0 : *reinterpret_cast<const uint4*>(hr + v * 8), f);  // own stores above
     unpack8(ldg16(w + v * 8), g);
     uint4 o;
     uint32_t* op = reinterpret_cast<uint32_t*>(&o);
@@ -765,7 +781,7 @@ int ls_rmsnorm(const void* x, int64_t m, int64_t n, const void* w, float eps, vo
   const int vec = (n % 8 == 0) && aligned16(x) && aligned16(w) && aligned16(out) ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)m);
-  cfg.blockDim = dim3(lsb::kNormThreads);
+  cfg.blockDim = dim3(lsb::norm_threads(n, vec));
   cfg.stream = (cudaStream_t)stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -789,7 +805,7 @@ int ls_residual_rmsnorm_splits(const float* part, int64_t splits, int64_t m, int
              LS_ERR_MISALIGNED, "ls_residual_rmsnorm_splits: rows must be multiples of 8 on 16-byte boundaries");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)m);
-  cfg.blockDim = dim3(lsb::kNormThreads);
+  cfg.blockDim = dim3(lsb::norm_threads(n, 1));
   cfg.stream = (cudaStream_t)stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

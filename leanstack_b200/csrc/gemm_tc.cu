@@ -944,7 +944,23 @@ static TcPlan tc_plan(int64_t m, int64_t k, int64_t n_out, int epi) {
       --pl.stages;
     pl.smem = 1024 + (size_t)pl.stages * pl.stage_bytes + (size_t)(2 * pl.stages + 6) * 8 + 16;
   }
-  if (pl.tiles < sms) {
+  if (pl.tiles < sms && split_out) {
+    // Two CTAs per SM (twice the splits), each with a ring cut to fit beside
+    // the other: a CTA's stream rate is bound by the bytes its ring keeps in
+    // flight, so an SM with two streams about twice as fast.
+    int st = pl.stages;
+    auto smem_of = [&](int stages) {
+      return 1024 + (size_t)stages * pl.stage_bytes + (size_t)(2 * stages + 6) * 8 + 16;
+    };
+    while (st > 3 && 2 * (smem_of(st) + 1024) > (size_t)228 * 1024) --st;
+    const int per2 = (2 * sms) / pl.tiles < pl.kblocks ? (2 * sms) / pl.tiles : pl.kblocks;
+    if (2 * (smem_of(st) + 1024) <= (size_t)228 * 1024 && per2 > sms / pl.tiles) {
+      pl.stages = st;
+      pl.smem = smem_of(st);
+      pl.grid = pl.tiles * per2;
+    }
+  }
+  if (pl.tiles < sms && pl.grid <= sms) {
     const int per_tile = sms / pl.tiles < pl.kblocks ? sms / pl.tiles : pl.kblocks;
     const int g = pl.tiles * per_tile;
     const int g_up = pl.tiles * (per_tile + 1);

@@ -162,6 +162,7 @@ def qk_norm_rope_splits(part: torch.Tensor, splits: int, batch: int, q_len: int,
                         cos: torch.Tensor, sin: torch.Tensor, *, eps: float = 1e-6,
                         cache_pos: torch.Tensor | None = None, uniform_past: int = 0, rope_offset: int = 0,
                         k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None, max_seq: int = 0,
+                        k_out: torch.Tensor | None = None, v_out: torch.Tensor | None = None,
                         q_out: torch.Tensor) -> torch.Tensor:
     """:func:`qk_norm_rope` on the split fp32 partials of the QKV projection (``gemm_tc_splits``)."""
     _check(part, "part", torch.float32)
@@ -173,7 +174,7 @@ def qk_norm_rope_splits(part: torch.Tensor, splits: int, batch: int, q_len: int,
     nat.call("ls_qk_norm_rope_kvappend_splits", part.data_ptr(), splits, batch, q_len, num_heads, num_kv_heads,
              head_dim, q_norm_w.data_ptr(), k_norm_w.data_ptr(), float(eps), cos.data_ptr(), sin.data_ptr(),
              cos.shape[0], int(rope_offset), _ptr(cache_pos), int(uniform_past), _ptr(k_cache), _ptr(v_cache),
-             int(max_seq), None, None, q_out.data_ptr(), _stream())
+             int(max_seq), _ptr(k_out), _ptr(v_out), q_out.data_ptr(), _stream())
     return q_out
 
 

@@ -196,6 +196,13 @@ def _linear_routed(x: torch.Tensor, w: torch.Tensor, *, norm_w: torch.Tensor | N
         return K.linear(x, w, norm_w=norm_w, eps=eps, epilogue=epilogue, residual=residual)
     xn = K.rmsnorm(x, norm_w, eps) if norm_w is not None else x
     if m <= TC_MAX_M:
+        if epilogue == K.EPI_RESIDUAL:  # split partials + residual consumer, the engine's kernels
+            part = torch.empty(K.gemm_splits(m, w.shape[1], w.shape[0]) * m * w.shape[0], device=x.device,
+                               dtype=torch.float32)
+            s = K.gemm_tc_splits(xn, w, part)
+            out = torch.empty(m, w.shape[0], device=x.device, dtype=x.dtype)
+            K.residual_rmsnorm_splits(part, s, residual, out_residual=out)
+            return out
         if epilogue == K.EPI_SILU_MUL and K.gate_up_whole_k(m, w.shape[1], w.shape[0]):
             part = torch.empty(m * w.shape[0], device=x.device, dtype=torch.float32)
             s = K.gemm_tc_splits(xn, w, part)
@@ -211,6 +218,22 @@ def _qkv(hidden: torch.Tensor, batch: int, q_len: int, qkv_w, hq, hkv, d, qn, kn
     cos_t, sin_t = _cos_sin_table(cos, sin)
     m = batch * q_len
     x = hidden.reshape(m, -1).contiguous()
+    if SMALL_M < m <= TC_MAX_M:  # the engine's kernels: QKV split partials summed by the q/k norm
+        xn = K.rmsnorm(x, input_norm, eps) if input_norm is not None else x
+        part = torch.empty(K.gemm_splits(m, x.shape[1], qkv_w.shape[0]) * m * qkv_w.shape[0], device=x.device,
+                           dtype=torch.float32)
+        s = K.gemm_tc_splits(xn, qkv_w, part)
+        if kv is not None:
+            q = K.qk_norm_rope_splits(part, s, batch, q_len, hq, hkv, d, qn, kn, cos_t, sin_t, eps=eps,
+                                      uniform_past=past, rope_offset=past, k_cache=kv.key_cache[layer_idx],
+                                      v_cache=kv.value_cache[layer_idx], max_seq=kv.layout.max_seq_len,
+                                      q_out=torch.empty((m, hq, d), device=x.device, dtype=x.dtype))
+            return q, None, None
+        k_out = torch.empty((m, hkv, d), device=x.device, dtype=x.dtype)
+        v_out = torch.empty((m, hkv, d), device=x.device, dtype=x.dtype)
+        q = K.qk_norm_rope_splits(part, s, batch, q_len, hq, hkv, d, qn, kn, cos_t, sin_t, eps=eps, k_out=k_out,
+                                  v_out=v_out, q_out=torch.empty((m, hq, d), device=x.device, dtype=x.dtype))
+        return q, k_out, v_out
     if m > SMALL_M:
         qkv = _linear_routed(x, qkv_w, norm_w=input_norm, eps=eps)
         if kv is not None:

@@ -191,11 +191,11 @@ def test_gemm_big_silu(m):
 
 
 @pytest.mark.parametrize("m", [1, 16, 32, 80, 128])
-def test_gemm_tc_split_partials_sum_to_reduced_output(m):
+def test_gemm_tc_split_partials_and_residual_norm(m):
     """Split-partial epilogue (QKV / o_proj / down of the one-GPU tensor-core
-    step): the splits added in order give the in-kernel reduction's bits, and
-    the residual + RMSNorm consumer equals the residual epilogue followed by
-    ls_rmsnorm bit for bit."""
+    step): the splits added in order are the product within the bound, and the
+    residual + RMSNorm consumer gives bf16(res + bf16(sum)) and ls_rmsnorm of
+    it bit for bit."""
     eps = 1e-6
     for i, (n, k) in enumerate([(6144, 2560), (2560, 4096), (2560, 9728)]):
         x = _rand((m, k), 1.0, f"spx{i}")
@@ -209,7 +209,6 @@ def test_gemm_tc_split_partials_sum_to_reduced_output(m):
             acc += p[j]
         assert torch.isnan(part[s * m * n:]).all()  # nothing written past the splits
         _check(acc.bfloat16(), x.float() @ w.float().t())
-        assert torch.equal(acc.bfloat16(), K.gemm_tc(x, w)), (n, k)
         if n != 2560:
             continue
         res = _rand((m, n), 1.0, f"spr{i}")
@@ -217,8 +216,9 @@ def test_gemm_tc_split_partials_sum_to_reduced_output(m):
         h = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
         xn = torch.empty_like(h)
         K.residual_rmsnorm_splits(part, s, res, out_residual=h, norm_w=nw, eps=eps, out_norm=xn)
-        want_h = K.gemm_tc(x, w, epilogue=K.EPI_RESIDUAL, residual=res)
+        want_h = (res.float() + acc.bfloat16().float()).bfloat16()
         assert torch.equal(h, want_h)
+        _check(h, res.float() + (x.float() @ w.float().t()).bfloat16().float())
         assert torch.equal(xn, K.rmsnorm(want_h, nw, eps))
         h2 = torch.empty_like(h)
         K.residual_rmsnorm_splits(part, s, res, out_residual=h2)
@@ -228,7 +228,8 @@ def test_gemm_tc_split_partials_sum_to_reduced_output(m):
 @pytest.mark.parametrize("batch,q_len", [(1, 1), (16, 5), (32, 1)])
 def test_qk_norm_rope_on_split_partials(batch, q_len):
     """q/k norm + RoPE + K/V append fed by the QKV GEMM's split partials equals
-    the same kernel fed by the reduced bf16 projection, bit for bit."""
+    the same kernel fed by the projection those partials sum to (in split
+    order, rounded once), bit for bit."""
     hq, hkv, d, hidden, S = 32, 8, 128, 2560, 64
     m = batch * q_len
     x = _rand((m, hidden), 1.0, "qx")
@@ -238,6 +239,15 @@ def test_qk_norm_rope_on_split_partials(batch, q_len):
     ang = torch.arange(S, device=DEV, dtype=torch.float32)[:, None] * 0.01 * torch.arange(1, d // 2 + 1, device=DEV)
     cos, sin = ang.cos().bfloat16(), ang.sin().bfloat16()
     pos = torch.arange(batch, device=DEV, dtype=torch.int32) % 7
+    s = K.gemm_splits(m, hidden, w.shape[0])
+    part = torch.empty(s * m * w.shape[0], device=DEV)
+    K.gemm_tc_splits(x, w, part)
+    p = part.view(s, m, w.shape[0])
+    qkv = p[0].clone()
+    for j in range(1, s):
+        qkv += p[j]
+    qkv = qkv.bfloat16()
+    _check(qkv, x.float() @ w.float().t())
     outs = []
     for use_split in (False, True):
         kc = torch.zeros(batch, hkv, S, d, device=DEV, dtype=torch.bfloat16)
@@ -245,12 +255,9 @@ def test_qk_norm_rope_on_split_partials(batch, q_len):
         q = torch.empty(m, hq, d, device=DEV, dtype=torch.bfloat16)
         common = dict(eps=1e-6, cache_pos=pos.clone(), k_cache=kc, v_cache=vc, max_seq=S, q_out=q)
         if use_split:
-            s = K.gemm_splits(m, hidden, w.shape[0])
-            part = torch.empty(s * m * w.shape[0], device=DEV)
-            K.gemm_tc_splits(x, w, part)
             K.qk_norm_rope_splits(part, s, batch, q_len, hq, hkv, d, qn, kn, cos, sin, **common)
         else:
-            K.qk_norm_rope(K.gemm_tc(x, w), batch, q_len, hq, hkv, d, qn, kn, cos, sin, **common)
+            K.qk_norm_rope(qkv, batch, q_len, hq, hkv, d, qn, kn, cos, sin, **common)
         outs.append((q, kc, vc))
     for a, b in zip(*outs):
         assert torch.equal(a, b)
