@@ -33,21 +33,22 @@ TC_MAX_M = 128   # largest token count of one tcgen05 GEMM launch
 BACKENDS = ("auto", "tc", "cuda_core")
 
 
-def resolve_backend(backend: str, batch_size: int) -> str:
-    """``auto``: tensor cores from 6 sequences on, CUDA-core streaming below.
+def resolve_backend(backend: str, batch_size: int, tensor_parallel: bool = False) -> str:
+    """``auto``: on one GPU, tensor cores from 2 sequences on and CUDA-core
+    streaming for one; under tensor parallelism (row-split linears through the
+    fused peer all-reduce of the CUDA-core kernel), tensor cores from 6.
 
     Measured on Qwen3-4B decode steps with 2048 cached positions (tok/s,
-    CUDA-core / tcgen05): B 1 387 / 271, 2 608 / 485, 3 923 / 760, 4 1109 / 995,
-    5 1229 / 1186, 6 1328 / 1413, 7 1429 / 1665, 8 1520 / 1873.  Per launch
-    the tcgen05 GEMM already wins from M = 2 (gate_up 25.8 vs 28.3 us); the
-    step keeps the CUDA-core kernels longer for their fused RMSNorm prologues
-    and shorter fixed costs.
-
+    CUDA-core / tcgen05), one GPU, split-partial GEMMs summed by the next
+    kernel and whole-K gate_up: B 1 388 / 383, 2 610 / 680, 3 926 / 1082,
+    4 1111 / 1418, 5 1228 / 1722, 6 1330 / 2025, 8 1524 / 2644.  Before those
+    GEMM forms (the tensor-parallel ones still reduce inside the GEMM): B 5
+    1229 / 1186, 6 1328 / 1413.
     """
     if backend not in BACKENDS:
         raise ValueError(f"unknown linear backend {backend!r}; choose from {BACKENDS}")
     if backend == "auto":
-        return "tc" if batch_size >= 6 else "cuda_core"
+        return "tc" if batch_size >= (6 if tensor_parallel else 2) else "cuda_core"
     return backend
 
 
@@ -63,7 +64,7 @@ class DecodeEngine:
             raise ValueError("a tensor-parallel engine needs its TPShard")
         self.vocab_offset = shard.vocab_offset if self.tp is not None else 0
         self.vocab_rows = runtime.lm_head_weight.shape[0]
-        self.backend = resolve_backend(linear_backend, batch_size)
+        self.backend = resolve_backend(linear_backend, batch_size, self.tp is not None)
         limit = TC_MAX_M if self.backend == "tc" else SMALL_M
         if batch_size < 1 or batch_size > limit:
             raise ValueError(f"batch_size {batch_size}: the {self.backend} step handles 1..{limit} sequences")
