@@ -310,6 +310,15 @@ int ls_linear_allreduce_residual(const void* x, int64_t m, int64_t k, const void
  * with max_ctas >= 128. */
 int ls_allreduce_residual_f32(const float* part, int64_t m, int64_t n, const void* residual, void* out,
                               const ls_p2p_exchange* ex, ls_stream_t stream);
+/* The same over the split partials of a row-split linear run in the
+ * LS_EPI_SPLIT_F32 form (part = [splits][m][n]): each rank adds its splits in
+ * order, then the ranks' sums are exchanged and added in rank order. */
+int ls_allreduce_residual_splits(const float* part, int64_t splits, int64_t m, int64_t n, const void* residual,
+                                 void* out, const ls_p2p_exchange* ex, ls_stream_t stream);
+/* out[i] = sum over the splits of part[s][i] (n elements per split), in split
+ * order: the local sum before an NCCL all-reduce of a row-split linear's
+ * split partials (no counterpart in the reference, which runs on one GPU). */
+int ls_sum_splits_f32(const float* part, int64_t splits, int64_t n, float* out, ls_stream_t stream);
 
 /* Tensor-parallel greedy head.  Each rank holds a vocab shard (rows
  * [vocab_offset, vocab_offset + vocab_rows) of lm_head) and writes, per row, an

@@ -102,6 +102,8 @@ SIGNATURES: dict[str, list] = {
                                         _i64, _p, _p, _i64, _p, _p, _p, _p],
     "ls_residual_rmsnorm_splits": [_p, _i64, _i64, _i64, _p, _p, _f32, _p, _p, _p],
     "ls_silu_mul_splits": [_p, _i64, _i64, _i64, _p, _p],
+    "ls_allreduce_residual_splits": [_p, _i64, _i64, _i64, _p, _p, _p, _p],
+    "ls_sum_splits_f32": [_p, _i64, _i64, _p, _p],
     "ls_advance_cursors": [_p, _p, _i64, _i64, _p],
 }
 _RESTYPES = {"ls_last_error": ctypes.c_char_p}

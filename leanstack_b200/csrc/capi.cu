@@ -201,6 +201,19 @@ __global__ void silu_mul_splits_kernel(const float* part, int splits, int m, int
   }
 }
 
+// out[i] = sum_j part[j][i] over the splits in order: the local sum of a
+// tensor-parallel row-split linear's split partials before an NCCL all-reduce
+// (the order the fused peer all-reduce uses, so both give the same bits).
+__global__ void sum_splits_kernel(const float* part, int splits, int64_t n, float* out) {
+  grid_dep_launch();
+  grid_dep_wait();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = part[i];
+    for (int j = 1; j < splits; ++j) v += part[(size_t)j * n + i];
+    out[i] = v;
+  }
+}
+
 // Row argmax over bf16 logits: grid (chunks, m); each CTA reduces one chunk of
 // one row, the last CTA of the row reduces the chunk winners.
 constexpr int kArgmaxThreads = 256;
@@ -842,6 +855,25 @@ int ls_silu_mul_splits(const float* part, int64_t splits, int64_t m, int64_t int
   cudaError_t e = cudaLaunchKernelEx(&cfg, lsb::silu_mul_splits_kernel, part, (int)splits, (int)m, (int)intermediate,
                                      static_cast<__nv_bfloat16*>(act));
   return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "silu_mul_splits launch: %s", cudaGetErrorString(e));
+}
+
+int ls_sum_splits_f32(const float* part, int64_t splits, int64_t n, float* out, ls_stream_t stream) {
+  LS_REQUIRE(part && out && splits >= 1 && n > 0 && n < (1ll << 40), LS_ERR_INVALID_ARGUMENT,
+             "ls_sum_splits_f32: bad arguments");
+  const int threads = 256;
+  int64_t blocks = (n + threads - 1) / threads;
+  if (blocks > 4 * (int64_t)sm_count()) blocks = 4 * (int64_t)sm_count();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(threads);
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, lsb::sum_splits_kernel, part, (int)splits, n, out);
+  return e == cudaSuccess ? LS_OK : set_error(LS_ERR_CUDA, "sum_splits launch: %s", cudaGetErrorString(e));
 }
 
 int ls_advance_cursors(int32_t* cache_pos, const int32_t* delta, int64_t batch, int64_t q_len, ls_stream_t stream) {

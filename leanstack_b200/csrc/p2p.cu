@@ -48,7 +48,10 @@ namespace lsb {
 constexpr int kArThreads = 256;
 constexpr int kArGrid = 128;
 
-__global__ void __launch_bounds__(kArThreads) allreduce_residual_kernel(const float* part,
+// part holds `splits` slabs of M x N (the split partials of the tcgen05
+// GEMM's LS_EPI_SPLIT_F32 form, added in slab order before the exchange), or
+// one slab.
+__global__ void __launch_bounds__(kArThreads) allreduce_residual_kernel(const float* part, int splits,
                                                                        const __nv_bfloat16* residual,
                                                                        __nv_bfloat16* out, int M, int N,
                                                                        P2PExchange ex, int* err) {
@@ -71,7 +74,8 @@ __global__ void __launch_bounds__(kArThreads) allreduce_residual_kernel(const fl
   const int stride = gridDim.x * kArThreads;
   for (int i = blockIdx.x * kArThreads + tid; i < total; i += stride) {
     const int m = i / N, n = i - m * N;
-    const float v = part[i];
+    float v = part[i];
+    for (int j = 1; j < splits; ++j) v += part[(size_t)j * total + i];
     const size_t off = slot_base + ((size_t)ex.rank * ex.max_rows + m) * ex.width + n;
     for (int q = 0; q < ex.world; ++q)
       st_pair_sys(reinterpret_cast<uint2*>(ex.peer[q] + recv_off) + off, __float_as_uint(v), epoch);
@@ -203,9 +207,10 @@ int ls_linear_allreduce_residual(const void* x, int64_t m, int64_t k, const void
   return launch_linear_allreduce(x, m, k, w, n, residual, out, &e, (cudaStream_t)stream);
 }
 
-int ls_allreduce_residual_f32(const float* part, int64_t m, int64_t n, const void* residual, void* out,
-                              const ls_p2p_exchange* ex, ls_stream_t stream) {
-  if (!part || !residual || !out) return set_error(LS_ERR_INVALID_ARGUMENT, "ls_allreduce_residual_f32: null pointer");
+int ls_allreduce_residual_splits(const float* part, int64_t splits, int64_t m, int64_t n, const void* residual,
+                                 void* out, const ls_p2p_exchange* ex, ls_stream_t stream) {
+  if (!part || !residual || !out || splits < 1 || splits > 64)
+    return set_error(LS_ERR_INVALID_ARGUMENT, "ls_allreduce_residual_f32: null pointer or bad split count");
   lsb::P2PExchange e;
   int rc = to_exchange(ex, n, "ls_allreduce_residual_f32", &e);
   if (rc) return rc;
@@ -224,11 +229,16 @@ int ls_allreduce_residual_f32(const float* part, int64_t m, int64_t n, const voi
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, lsb::allreduce_residual_kernel, part,
+  cudaError_t err = cudaLaunchKernelEx(&cfg, lsb::allreduce_residual_kernel, part, (int)splits,
                                        static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out),
                                        (int)m, (int)n, e, device_error_ptr());
   return err == cudaSuccess ? LS_OK
                             : set_error(LS_ERR_CUDA, "allreduce_residual launch: %s", cudaGetErrorString(err));
+}
+
+int ls_allreduce_residual_f32(const float* part, int64_t m, int64_t n, const void* residual, void* out,
+                              const ls_p2p_exchange* ex, ls_stream_t stream) {
+  return ls_allreduce_residual_splits(part, 1, m, n, residual, out, ex, stream);
 }
 
 }  // extern "C"

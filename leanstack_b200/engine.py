@@ -101,20 +101,23 @@ class DecodeEngine:
             # Split fp32 partials of QKV / o_proj / down (one GPU): the GEMMs
             # leave the cross-split sum to the next kernel (q/k norm, residual +
             # RMSNorm) instead of reducing behind a grid-wide wait.
-            self.tc_part = None
-            # gate_up as a plain [2I, H] linear with whole-K tiles (one split:
-            # no reduction across CTAs) when its 128-row tiles cover the SMs,
-            # followed by the SiLU*up combine; else the paired SiLU epilogue.
-            self.gu_plain = self.tp is None and all(
-                K.gate_up_whole_k(mm, g.hidden_size, 2 * g.intermediate_size)
-                for mm in range(batch_size, T + 1, batch_size))
-            if self.tp is None:
-                shapes_ = [(g.hidden_size, g.qkv_dim), (g.q_dim, g.hidden_size), (g.intermediate_size, g.hidden_size)]
-                if self.gu_plain:
-                    shapes_.append((g.hidden_size, 2 * g.intermediate_size))
-                part = max(K.gemm_splits(mm, k_, n_) * mm * n_
-                           for mm in range(batch_size, T + 1, batch_size) for k_, n_ in shapes_)
-                self.tc_part = torch.zeros(part, device=dev, dtype=torch.float32)
+            # gate_up as a plain [2I, H] linear (whole-K tiles when its 128-row
+            # tiles cover the SMs, else k-splits) followed by the SiLU*up
+            # combine; else the paired SiLU epilogue.
+            self.gu_plain = K.gate_up_plain(T, g.hidden_size, 2 * g.intermediate_size)
+            # Split fp32 partials of QKV / o_proj / down / gate_up: the GEMMs
+            # leave the cross-split sum to the next kernel (q/k norm, residual +
+            # RMSNorm, SiLU*up, or the tensor-parallel all-reduce) instead of
+            # reducing behind a grid-wide wait.  Shapes are this rank's shard.
+            rt0 = runtime.layers[0]
+            shapes_ = [(g.hidden_size, rt0.attention.qkv_proj_weight.shape[0]),
+                       (rt0.attention.o_proj_weight.shape[1], g.hidden_size),
+                       (rt0.mlp.down_proj_weight.shape[1], g.hidden_size)]
+            if self.gu_plain:
+                shapes_.append((g.hidden_size, rt0.mlp.gate_up_proj_weight.shape[0]))
+            part = max(K.gemm_splits(mm, k_, n_) * mm * n_
+                       for mm in range(batch_size, T + 1, batch_size) for k_, n_ in shapes_)
+            self.tc_part = torch.zeros(part, device=dev, dtype=torch.float32)
         else:
             self.lm_ws = torch.zeros(K.lmhead_workspace_bytes(self.T, self.vocab_rows), device=dev,
                                      dtype=torch.uint8)
@@ -149,18 +152,18 @@ class DecodeEngine:
         eps = g.rms_norm_eps
         kv = self.kv
         tc = self.backend == "tc"
-        split = tc and self.tp is None  # split-partial GEMMs, summed by the consumer kernels
-        part = self.tc_part if split else None
+        split = tc and self.tp is None  # one GPU: the residual linears' partials go to the residual consumer
+        part = self.tc_part if tc else None
         s_down = 0
         K.embed_gather(a.ids[:m], rt.embed_tokens_weight, out=a.x[:m])
         for li, layer in enumerate(rt.layers):
             att, mlp = layer.attention, layer.mlp
             tt = self.tc_tiles[li] if (tc and self.tc_tiles is not None) else {}
             # QKV projection (with the input RMSNorm) into a.qkv
-            if split:
-                if li == 0:
+            if tc:
+                if li == 0 or self.tp is not None:
                     K.rmsnorm(a.x[:m], layer.input_layernorm_weight, eps, out=self.xn[:m])
-                else:  # the previous layer's down residual, then this layer's input norm
+                else:  # the previous layer's down residual (one GPU), then this layer's input norm
                     K.residual_rmsnorm_splits(part, s_down, a.h[:m], out_residual=a.x[:m],
                                               norm_w=layer.input_layernorm_weight, eps=eps, out_norm=self.xn[:m])
                 s_qkv = K.gemm_tc_splits(self.xn[:m], att.qkv_proj_weight, part, tiled=tt.get("qkv"))
@@ -169,13 +172,8 @@ class DecodeEngine:
                                       cache_pos=kv.cache_pos, k_cache=kv.key_cache[li], v_cache=kv.value_cache[li],
                                       max_seq=self.S, q_out=a.q[:m])
             else:
-                if tc:
-                    K.rmsnorm(a.x[:m], layer.input_layernorm_weight, eps, out=self.xn[:m])
-                    K.gemm_tc(self.xn[:m], att.qkv_proj_weight, out=a.qkv[:m], workspace=self.tc_ws,
-                              tiled=tt.get("qkv"))
-                else:
-                    K.linear(a.x[:m], att.qkv_proj_weight, norm_w=layer.input_layernorm_weight, eps=eps,
-                             out=a.qkv[:m])
+                K.linear(a.x[:m], att.qkv_proj_weight, norm_w=layer.input_layernorm_weight, eps=eps,
+                         out=a.qkv[:m])
                 K.qk_norm_rope(a.qkv[:m], B, q_len, g.num_attention_heads, g.num_key_value_heads, g.head_dim,
                                att.q_norm_weight, att.k_norm_weight, self.cos, self.sin, eps=eps,
                                cache_pos=kv.cache_pos, k_cache=kv.key_cache[li], v_cache=kv.value_cache[li],
@@ -187,8 +185,7 @@ class DecodeEngine:
                 self._row_split(a.attn[:m], att.o_proj_weight, a.x[:m], a.h[:m], tc, tt.get("o"))
                 if tc:
                     K.rmsnorm(a.h[:m], layer.post_attention_layernorm_weight, eps, out=self.xn[:m])
-                    K.gemm_tc(self.xn[:m], mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=a.act[:m],
-                              workspace=self.tc_ws, tiled=tt.get("gu"))
+                    self._gate_up(self.xn[:m], mlp.gate_up_proj_weight, a.act[:m], tt.get("gu"))
                 else:
                     K.gateup_silu(a.h[:m], layer.post_attention_layernorm_weight, mlp.gate_up_proj_weight, eps,
                                   out=a.act[:m])
@@ -197,12 +194,7 @@ class DecodeEngine:
                 s_o = K.gemm_tc_splits(a.attn[:m], att.o_proj_weight, part, tiled=tt.get("o"))
                 K.residual_rmsnorm_splits(part, s_o, a.x[:m], out_residual=a.h[:m],
                                           norm_w=layer.post_attention_layernorm_weight, eps=eps, out_norm=self.xn[:m])
-                if self.gu_plain:  # (the paired tile image is the plain one when I is a multiple of 128)
-                    s_gu = K.gemm_tc_splits(self.xn[:m], mlp.gate_up_proj_weight, part, tiled=tt.get("gu"))
-                    K.silu_mul_splits(part, s_gu, m, g.intermediate_size, out=a.act[:m])
-                else:
-                    K.gemm_tc(self.xn[:m], mlp.gate_up_proj_weight, epilogue=K.EPI_SILU_MUL, out=a.act[:m],
-                              workspace=self.tc_ws, tiled=tt.get("gu"))
+                self._gate_up(self.xn[:m], mlp.gate_up_proj_weight, a.act[:m], tt.get("gu"))
                 s_down = K.gemm_tc_splits(a.act[:m], mlp.down_proj_weight, part, tiled=tt.get("down"))
             else:
                 K.oproj_residual(a.attn[:m], att.o_proj_weight, a.x[:m], out=a.h[:m])
@@ -307,15 +299,33 @@ class DecodeEngine:
         kv.note_advanced(P)
         return a.ids[:B].clone()
 
+    def _gate_up(self, xn: torch.Tensor, w: torch.Tensor, act: torch.Tensor, tiled: torch.Tensor | None) -> None:
+        """act = SiLU(gate) * up on the tensor cores: plain split-partial linear +
+        combine (the paired tile image is the plain one when I % 128 == 0), or
+        the paired SiLU epilogue."""
+        m = xn.shape[0]
+        if self.gu_plain:
+            s_gu = K.gemm_tc_splits(xn, w, self.tc_part, tiled=tiled)
+            K.silu_mul_splits(self.tc_part, s_gu, m, w.shape[0] // 2, out=act)
+        else:
+            K.gemm_tc(xn, w, epilogue=K.EPI_SILU_MUL, out=act, workspace=self.tc_ws, tiled=tiled)
+
     def _row_split(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor, out: torch.Tensor,
                    tc: bool, tiled: torch.Tensor | None = None) -> None:
-        """Row-split linear of tensor parallelism: fp32 partial, all-reduce, residual add."""
+        """Row-split linear of tensor parallelism: fp32 partial, all-reduce, residual add.
+        On the tensor cores the GEMM leaves its k-split partials; they are added
+        in split order on each rank (inside the fused all-reduce, or by a sum
+        kernel before NCCL), then across ranks."""
         if not tc and self.tp.p2p is not None:  # fused one-shot all-reduce in the linear's epilogue
             K.linear_allreduce_residual(x, w, residual, self.tp.p2p, out=out)
             return
         part = self.part[:x.shape[0]]
         if tc:
-            K.gemm_tc(x, w, epilogue=K.EPI_STORE_F32, out=part, workspace=self.tc_ws, tiled=tiled)
+            s = K.gemm_tc_splits(x, w, self.tc_part, tiled=tiled)
+            if self.tp.p2p_tc is not None:  # one-shot all-reduce of the partials + residual, over peer memory
+                K.allreduce_residual_splits(self.tc_part, s, residual, self.tp.p2p_tc, out=out)
+                return
+            K.sum_splits_f32(self.tc_part, s, part.numel(), out=part)
         else:
             K.linear(x, w, epilogue=K.EPI_STORE_F32, out=part)
         if self.tp.p2p_tc is not None:  # one-shot all-reduce of the partials + residual, over peer memory
@@ -468,6 +478,8 @@ class DecodeEngine:
         head = 3 if self.backend == "tc" else 1
         if self.tp is not None:  # + all-reduce / residual-add kernels after each row-split linear, + keys-to-ids
             if self.tp.p2p is None or self.backend == "tc":
+                per_layer += 2
+            if self.tp.p2p is None and self.backend == "tc":  # + the local split sums before NCCL
                 per_layer += 2
             head += 1
         return 1 + per_layer * len(self.rt.layers) + head + 1

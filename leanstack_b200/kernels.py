@@ -423,15 +423,14 @@ def residual_rmsnorm_splits(part: torch.Tensor, splits: int, residual: torch.Ten
              float(eps), out_residual.data_ptr(), _ptr(out_norm), _stream())
 
 
-def gate_up_whole_k(m: int, k: int, n_rows: int) -> bool:
-    """Whether the fused gate_up linear ``[n_rows = 2I, k]`` at ``m`` rows runs as a
-    plain linear with whole-K tiles (split-partial form with one split, then
-    :func:`silu_mul_splits`): its 128-row tiles cover at least 90% of the SMs,
-    I is a multiple of 128 (the paired tile image is then the plain one) and the
-    plan gives one split.  Otherwise the paired SiLU epilogue runs."""
-    tiles = -(-n_rows // 128)
-    return ((n_rows // 2) % 128 == 0 and tiles * 10 >= 9 * sm_count()
-            and gemm_splits(m, k, n_rows) == 1)
+def gate_up_plain(m: int, k: int, n_rows: int) -> bool:
+    """Whether the fused gate_up linear ``[n_rows = 2I, k]`` runs as a plain
+    linear in the split-partial form followed by :func:`silu_mul_splits`
+    (whole-K tiles when its 128-row tiles cover the SMs, else k-splits on two
+    CTAs per SM) instead of the paired SiLU epilogue: when I is a multiple of
+    128, so that the paired pre-tiled image is also the plain one."""
+    del m, k
+    return (n_rows // 2) % 128 == 0
 
 
 def silu_mul_splits(part: torch.Tensor, splits: int, m: int, intermediate: int, *, out: torch.Tensor) -> None:
@@ -505,6 +504,31 @@ def allreduce_residual_f32(part: torch.Tensor, residual: torch.Tensor, exchange,
         out = torch.empty_like(residual)
     nat.call("ls_allreduce_residual_f32", part.data_ptr(), m, n, residual.data_ptr(), out.data_ptr(),
              ctypes.byref(exchange.desc), _stream())
+    return out
+
+
+def allreduce_residual_splits(part: torch.Tensor, splits: int, residual: torch.Tensor, exchange, *,
+                              out: torch.Tensor) -> torch.Tensor:
+    """:func:`allreduce_residual_f32` over split partials ``part [splits, m, n]``
+    (each rank adds its splits in order first)."""
+    _check(part, "part", torch.float32)
+    _check(residual, "residual")
+    n = residual.shape[-1]
+    m = residual.numel() // n
+    if part.numel() < splits * m * n:
+        raise ValueError("split partials smaller than splits x m x n")
+    nat.call("ls_allreduce_residual_splits", part.data_ptr(), splits, m, n, residual.data_ptr(), out.data_ptr(),
+             ctypes.byref(exchange.desc), _stream())
+    return out
+
+
+def sum_splits_f32(part: torch.Tensor, splits: int, n: int, *, out: torch.Tensor) -> torch.Tensor:
+    """``out[:n] = sum_s part[s * n : (s + 1) * n]`` in split order (fp32)."""
+    _check(part, "part", torch.float32)
+    _check(out, "out", torch.float32)
+    if part.numel() < splits * n or out.numel() < n:
+        raise ValueError("sum_splits_f32: buffers smaller than the shapes")
+    nat.call("ls_sum_splits_f32", part.data_ptr(), splits, n, out.data_ptr(), _stream())
     return out
 
 

@@ -186,9 +186,10 @@ def _linear_routed(x: torch.Tensor, w: torch.Tensor, *, norm_w: torch.Tensor | N
     """``epilogue(w @ rmsnorm?(x))`` for x ``[m, k]``, on the kernel family for m.
 
     m <= 8: CUDA-core streaming linear with the RMSNorm in its prologue;
-    m <= 128: RMSNorm kernel, then the tcgen05 weight-streaming GEMM (gate_up
-    as a plain whole-K linear + the SiLU*up combine where the engine's step
-    runs it so, giving the engine's bits);
+    m <= 128: RMSNorm kernel, then the tcgen05 weight-streaming GEMM in the
+    split-partial form with the engine's consumers (residual add, SiLU*up
+    combine; the q/k norm takes the QKV partials in ``_qkv``), giving the
+    engine's bits;
     larger: RMSNorm kernel, then the persistent large-M tcgen05 GEMM.
     """
     m = x.shape[0]
@@ -203,8 +204,9 @@ def _linear_routed(x: torch.Tensor, w: torch.Tensor, *, norm_w: torch.Tensor | N
             out = torch.empty(m, w.shape[0], device=x.device, dtype=x.dtype)
             K.residual_rmsnorm_splits(part, s, residual, out_residual=out)
             return out
-        if epilogue == K.EPI_SILU_MUL and K.gate_up_whole_k(m, w.shape[1], w.shape[0]):
-            part = torch.empty(m * w.shape[0], device=x.device, dtype=torch.float32)
+        if epilogue == K.EPI_SILU_MUL and K.gate_up_plain(m, w.shape[1], w.shape[0]):
+            part = torch.empty(K.gemm_splits(m, w.shape[1], w.shape[0]) * m * w.shape[0], device=x.device,
+                               dtype=torch.float32)
             s = K.gemm_tc_splits(xn, w, part)
             act = torch.empty(m, w.shape[0] // 2, device=x.device, dtype=x.dtype)
             K.silu_mul_splits(part, s, m, w.shape[0] // 2, out=act)
