@@ -154,6 +154,7 @@ def _attn_ref(q, kc, vc, cache_pos, q_len, hq, hkv, scale):
                                               (2, 5, [64, 1024]), (1, 8, [504]), (4, 2, [1, 2, 3, 17]),
                                               # 20 / 32 rows per kv head on enough pairs: two 16-row tiles per CTA
                                               (16, 5, [1024 - 61 * i for i in range(16)]),
+                                              (3, 6, [0, 5, 300]),  # 24 rows: 8-row tiles, split keys
                                               (10, 8, [0, 1, 15, 16, 17, 300, 511, 512, 1000, 4088])])
 def test_decode_attention(batch, q_len, lens):
     hq, hkv, d, S = 32, 8, 128, 4096
