@@ -149,6 +149,16 @@ def main(argv=None) -> int:
         t = _time(lambda i: K.decode_attention(q, kcs[i % 2], vcs[i % 2], m, 1, 32, 8, 128, S, 128 ** -0.5,
                                                cache_pos=pos, out=o, workspace=ws), args.reps)
         out[f"attention(seq={args.seq})"] = (t, m * args.seq * g.kv_dim * 2 * 2)
+    if "verify_attn" in wanted:  # verify pass: --batch sequences x --m new tokens over --seq cached positions
+        B, Q, S = args.batch, m, 2048
+        kcs = [synth.normal((B, g.num_key_value_heads, S, g.head_dim), 1.0, c, "mb/vk", device=dev) for c in range(2)]
+        vcs = [synth.normal((B, g.num_key_value_heads, S, g.head_dim), 1.0, c, "mb/vv", device=dev) for c in range(2)]
+        q = synth.normal((B * Q, g.num_attention_heads, g.head_dim), 1.0, 0, "mb/vq", device=dev)
+        pos = torch.full((B,), args.seq, device=dev, dtype=torch.int32)
+        o = torch.empty(B * Q, g.q_dim, device=dev, dtype=torch.bfloat16)
+        t = _time(lambda i: K.decode_attention(q, kcs[i % 2], vcs[i % 2], B, Q, 32, 8, 128, S, 128 ** -0.5,
+                                               cache_pos=pos, out=o), args.reps)
+        out[f"verify_attn(B={B},q={Q},seq={args.seq})"] = (t, B * (args.seq + Q) * g.kv_dim * 2 * 2)
     if "prefill_attn" in wanted:  # causal attention of --m prompt tokens per sequence, batch --batch
         B, P = args.batch, m
         kc = synth.normal((B, g.num_key_value_heads, P, g.head_dim), 1.0, 0, "mb/pk", device=dev)
