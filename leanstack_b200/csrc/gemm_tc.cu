@@ -11,7 +11,11 @@
 // whole matrix are divided evenly over one CTA per SM, so every SM streams the
 // same number of weight bytes whatever the shape.  A tile whose k-blocks are
 // split between CTAs is finished by its last contributor, which sums the fp32
-// partials of all contributors in CTA order (deterministic).
+// partials of all contributors in CTA order (deterministic).  The split-partial
+// epilogue (SPLIT_F32, below) skips that reduction: with fewer tiles than SMs
+// its grid is tile-aligned on two CTAs per SM (each with a ring cut to fit
+// beside the other), with more it is one whole-K CTA per tile, and the next
+// kernel adds the partials.
 //
 // Warp roles (6 warps): warp 4 issues TMA loads of weight and activation
 // k-blocks into a shared-memory ring (128-byte swizzle, the canonical K-major
@@ -50,8 +54,8 @@ constexpr size_t kTcCounterBytes = (size_t)2 * kTcMaxTiles * sizeof(unsigned int
 // TEPI_SPLIT_F32: no reduction in the kernel.  The grid is tile-aligned (every
 // CTA holds the k-range of exactly one tile) and CTA j of a tile's splits
 // writes its unrounded fp32 sum to out[j][b][n]; the consumer kernel adds the
-// splits in order j = 0, 1, ... (the order the in-kernel reduction uses, so
-// the result is bit-identical) and applies the epilogue itself.
+// splits in order j = 0, 1, ... and applies the epilogue itself (bit-identical
+// to the in-kernel reduction of the same split count).
 enum { TEPI_STORE = 0, TEPI_RESIDUAL = 1, TEPI_SILU_MUL = 2, TEPI_STORE_F32 = 4, TEPI_SPLIT_F32 = 8 };
 
 struct TcParams {
