@@ -677,7 +677,11 @@ struct BgParams {
   void* out;                      // [M, N] bf16 (fp32 for STORE_F32)
   int* err;
   int M, N, tiles_n, tiles_m, kblocks, BN, stages, stage_bytes;
+  uint32_t tmem_cols;  // 2 accumulators x BN x (1 or 2) columns
+  int vec_epi;         // N % 16 == 0 and 16-byte aligned out / residual: row-vector epilogue through smem
 };
+constexpr int kBgStageCols = 16;                          // activation columns per epilogue chunk
+constexpr int kBgEpiBytes = kBgStageCols * kTcTileN * 4;  // fp32 staging of one chunk: 8 KB
 
 __device__ __forceinline__ void bg_tile(int i, const BgParams& p, int& tn, int& tm) {
   const int band_tiles = kBgGroup * p.tiles_n;
@@ -702,6 +706,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* acc_full = empty + NS;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  float* epi_stage = reinterpret_cast<float*>(smem + (size_t)NS * p.stage_bytes + 1024);  // [16][128]
   __shared__ int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -726,7 +731,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(512)
+                 "r"(p.tmem_cols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -809,6 +814,62 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         float v[16], w2[16];
         tmem_ld16(acc_addr + (uint32_t)cb, v);
         if (SILU) tmem_ld16(acc_addr + (uint32_t)(p.BN + cb), w2);
+        if (p.vec_epi) {
+          // Stage the chunk as [16 activation rows][128 weight rows] (SiLU*up
+          // already formed), then each thread writes 16 consecutive outputs of
+          // one activation row with 16-byte vectors (and loads the residual
+          // the same way): 8 threads per row, whole 256-byte row segments.
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float y = v[j];
+            if (SILU) {
+              const float g = round_bf16(v[j]);
+              y = round_bf16(g / (1.0f + expf(-g))) * round_bf16(w2[j]);
+            }
+            epi_stage[j * kTcTileN + row] = y;
+          }
+          named_bar_sync(1, kTcEpiThreads);
+          {
+            const int jj = threadIdx.x >> 3, part = threadIdx.x & 7;
+            const int b = tm * p.BN + cb + jj;
+            const int n0 = tn * kTcTileN + part * 16;
+            if (b < p.M && n0 < p.N) {
+              const float4* src = reinterpret_cast<const float4*>(epi_stage + jj * kTcTileN + part * 16);
+              float y[16];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float4 f = src[q];
+                y[4 * q] = f.x, y[4 * q + 1] = f.y, y[4 * q + 2] = f.z, y[4 * q + 3] = f.w;
+              }
+              const size_t o = (size_t)b * p.N + n0;
+              if (EPI == TEPI_RESIDUAL) {
+                float r[16];
+                unpack8(ldg16(p.residual + o), r);
+                unpack8(ldg16(p.residual + o + 8), r + 8);
+#pragma unroll
+                for (int q = 0; q < 16; ++q) y[q] = r[q] + round_bf16(y[q]);
+              }
+              if (EPI == TEPI_STORE_F32) {
+                float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + o);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) dst[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+              } else {
+                uint4 pk[2];
+                uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                  __nv_bfloat162 h2 = __floats2bfloat162_rn(y[2 * q], y[2 * q + 1]);
+                  pw[q] = *reinterpret_cast<uint32_t*>(&h2);
+                }
+                uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + o);
+                dst[0] = pk[0];
+                dst[1] = pk[1];
+              }
+            }
+          }
+          named_bar_sync(1, kTcEpiThreads);  // the staging buffer is free again
+          continue;
+        }
         if (n < p.N) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -835,7 +896,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols) : "memory");
   }
 }
 
@@ -1133,21 +1194,29 @@ int launch_gemm_big(const void* x, int64_t m, int64_t k, const void* w, int64_t 
   const bool silu = epi == TEPI_SILU_MUL;
   if (silu && ((n_out * k * 2) % 16)) return set_error(LS_ERR_MISALIGNED, "gemm_big: up-projection view misaligned");
   BgParams p = {};
-  p.BN = silu ? 128 : 256;
+  // Non-SiLU epilogues with long K (o_proj, down): two CTAs per SM on
+  // 128 x 128 tiles, 3 x 32 KB rings and 256 TMEM columns each, so that two
+  // producer / MMA pipelines share the SM and cover the latency of operands
+  // that miss L2 (a 128 x 256 tile of down needs 7.5 MB over its K).
+  const bool two_per_sm = !silu && k >= 4096;
+  p.BN = (silu || two_per_sm) ? 128 : 256;
   p.M = (int)m;
   p.N = (int)n_out;
   p.tiles_n = (int)((n_out + kTcTileN - 1) / kTcTileN);
   p.tiles_m = (int)((m + p.BN - 1) / p.BN);
   p.kblocks = (int)((k + kTcBlockK - 1) / kTcBlockK);
-  p.stage_bytes = (silu ? 2 : 1) * kTcTileN * kTcBlockK * 2 + p.BN * kTcBlockK * 2;  // 48 KB either way
-  p.stages = 4;
+  p.stage_bytes = (silu ? 2 : 1) * kTcTileN * kTcBlockK * 2 + p.BN * kTcBlockK * 2;
+  p.stages = two_per_sm ? 3 : 4;
+  p.tmem_cols = two_per_sm ? 256u : 512u;
   p.residual = static_cast<const __nv_bfloat16*>(residual);
   p.out = out;
   p.err = device_error_ptr();
   const long long total = (long long)p.tiles_n * p.tiles_m;
   if (total > (1ll << 31) - 1) return set_error(LS_ERR_UNSUPPORTED_SHAPE, "gemm_big: too many tiles");
-  const int grid = (int)(total < sm_count() ? total : sm_count());
-  const size_t smem = 1024 + (size_t)p.stages * p.stage_bytes + (size_t)(2 * p.stages + 4) * 8 + 16;
+  const int cap = (two_per_sm ? 2 : 1) * sm_count();
+  const int grid = (int)(total < cap ? total : cap);
+  p.vec_epi = (n_out % 16 == 0) && aligned16(out) && (!residual || aligned16(residual)) ? 1 : 0;
+  const size_t smem = 1024 + (size_t)p.stages * p.stage_bytes + 1024 + (size_t)kBgEpiBytes;
   CUtensorMap mw, mw2, mx;
   int rc = make_map(&mw, w, n_out, k, kTcTileN);
   if (rc) return rc;

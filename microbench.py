@@ -214,6 +214,8 @@ def main(argv=None) -> int:
             big_case("qkv", g.qkv_dim, H, K.EPI_STORE)
         if "big_gateup" in big:
             big_case("gateup", 2 * I, H, K.EPI_SILU_MUL)
+        if "big_oproj" in big:
+            big_case("oproj", H, g.q_dim, K.EPI_RESIDUAL)
         if "big_down" in big:
             big_case("down", H, I, K.EPI_RESIDUAL)
     tc = {k for k in wanted if k.startswith("tc_")}
