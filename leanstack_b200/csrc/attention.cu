@@ -57,12 +57,20 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(QkRopeParams p
     const size_t slab = (size_t)gridDim.x * qkv_dim;
     const float* q = p.part + (size_t)t * qkv_dim + col;
     float4 a = __ldcg(reinterpret_cast<const float4*>(q));
-    for (int j = 1; j < p.splits; ++j) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(q + j * slab));
-      a.x += v.x;
-      a.y += v.y;
-      a.z += v.z;
-      a.w += v.w;
+    // Eight splits' loads in flight at a time, added in split order.
+    for (int j0 = 1; j0 < p.splits; j0 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (j0 + u < p.splits) v[u] = __ldcg(reinterpret_cast<const float4*>(q + (j0 + u) * slab));
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (j0 + u < p.splits) {
+          a.x += v[u].x;
+          a.y += v[u].y;
+          a.z += v[u].z;
+          a.w += v[u].w;
+        }
     }
     __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y), hi = __floats2bfloat162_rn(a.z, a.w);
     return make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
@@ -75,6 +83,8 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(QkRopeParams p
   }
 
   const uint2 raw_u = load4(h * kHeadDim + e0);
+  // A key head's V columns, fetched before the norm so both loads overlap.
+  const uint2 v_u = is_q ? make_uint2(0u, 0u) : load4((h + p.Hkv) * kHeadDim + e0);
   float raw[4] = {bf16_lo(raw_u.x), bf16_hi(raw_u.x), bf16_lo(raw_u.y), bf16_hi(raw_u.y)};
   float ss = raw[0] * raw[0] + raw[1] * raw[1] + raw[2] * raw[2] + raw[3] * raw[3];
   ss = warp_sum(ss);
@@ -105,7 +115,6 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(QkRopeParams p
     *reinterpret_cast<uint2*>(p.q_out + ((size_t)t * p.Hq + h) * kHeadDim + e0) = packed;
     return;
   }
-  const uint2 v_u = load4((h + p.Hkv) * kHeadDim + e0);
   if (p.k_cache) {
     const size_t off = (((size_t)b * p.Hkv + hk) * p.max_seq + pos) * kHeadDim + e0;
     *reinterpret_cast<uint2*>(p.k_cache + off) = packed;

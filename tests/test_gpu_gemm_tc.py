@@ -225,29 +225,63 @@ def test_gemm_tc_split_partials_and_residual_norm(m):
         assert torch.equal(h2, want_h)
 
 
-@pytest.mark.parametrize("batch,q_len", [(1, 1), (16, 5), (32, 1)])
-def test_qk_norm_rope_on_split_partials(batch, q_len):
-    """q/k norm + RoPE + K/V append fed by the QKV GEMM's split partials equals
-    the same kernel fed by the projection those partials sum to (in split
-    order, rounded once), bit for bit."""
+@pytest.mark.parametrize("n,splits", [(8, 3), (256, 1), (512, 2), (1024, 5), (2304, 14), (2560, 14), (3584, 6),
+                                      (4096, 16), (12296, 4), (16384, 9)])
+def test_residual_norm_splits_rows(n, splits):
+    """The residual + RMSNorm consumer of split partials, for rows of one to 32
+    warps and rows with more 8-column groups than threads: h is bf16(res +
+    bf16(partials summed in split order)) and the norm equals ls_rmsnorm of h,
+    bit for bit; without a norm only h is written."""
+    eps = 1e-6
+    for m in (1, 7, 80):
+        p = _rand((splits, m, n), 0.5, f"rnp{n}_{m}").float()
+        res = _rand((m, n), 1.0, f"rnr{n}_{m}")
+        nw = 1.0 + _rand((n,), 0.01, f"rnw{n}")
+        acc = p[0].clone()
+        for j in range(1, splits):
+            acc += p[j]
+        want_h = (res.float() + acc.bfloat16().float()).bfloat16()
+        h = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
+        xn = torch.empty_like(h)
+        K.residual_rmsnorm_splits(p.reshape(-1), splits, res, out_residual=h, norm_w=nw, eps=eps, out_norm=xn)
+        assert torch.equal(h, want_h)
+        assert torch.equal(xn, K.rmsnorm(want_h, nw, eps))
+        h2 = torch.full_like(h, float("nan"))
+        K.residual_rmsnorm_splits(p.reshape(-1), splits, res, out_residual=h2)
+        assert torch.equal(h2, want_h)
+
+
+@pytest.mark.parametrize("batch,q_len,splits", [(1, 1, None), (16, 5, None), (32, 1, None), (3, 2, 1), (2, 1, 8),
+                                                (4, 3, 9), (1, 1, 16)])
+def test_qk_norm_rope_on_split_partials(batch, q_len, splits):
+    """q/k norm + RoPE + K/V append fed by split partials equals the same
+    kernel fed by the projection those partials sum to (in split order,
+    rounded once), bit for bit: the QKV GEMM's own partials (splits None), or
+    synthetic ones at split counts around the kernel's 8-load batches."""
     hq, hkv, d, hidden, S = 32, 8, 128, 2560, 64
     m = batch * q_len
-    x = _rand((m, hidden), 1.0, "qx")
-    w = _rand(((hq + 2 * hkv) * d, hidden), 0.02, "qw")
     qn = 1.0 + _rand((d,), 0.01, "qn")
     kn = 1.0 + _rand((d,), 0.01, "kn")
     ang = torch.arange(S, device=DEV, dtype=torch.float32)[:, None] * 0.01 * torch.arange(1, d // 2 + 1, device=DEV)
     cos, sin = ang.cos().bfloat16(), ang.sin().bfloat16()
     pos = torch.arange(batch, device=DEV, dtype=torch.int32) % 7
-    s = K.gemm_splits(m, hidden, w.shape[0])
-    part = torch.empty(s * m * w.shape[0], device=DEV)
-    K.gemm_tc_splits(x, w, part)
-    p = part.view(s, m, w.shape[0])
+    n = (hq + 2 * hkv) * d
+    if splits is None:
+        x = _rand((m, hidden), 1.0, "qx")
+        w = _rand((n, hidden), 0.02, "qw")
+        s = K.gemm_splits(m, hidden, n)
+        part = torch.empty(s * m * n, device=DEV)
+        K.gemm_tc_splits(x, w, part)
+    else:
+        s = splits
+        part = _rand((s * m * n,), 0.4, f"qp{s}").float()
+    p = part.view(s, m, n)
     qkv = p[0].clone()
     for j in range(1, s):
         qkv += p[j]
     qkv = qkv.bfloat16()
-    _check(qkv, x.float() @ w.float().t())
+    if splits is None:
+        _check(qkv, x.float() @ w.float().t())
     outs = []
     for use_split in (False, True):
         kc = torch.zeros(batch, hkv, S, d, device=DEV, dtype=torch.bfloat16)
