@@ -215,6 +215,21 @@ int ls_decode_attention(const void* q, const void* k_cache, const void* v_cache,
                         ls_stream_t stream);
 int ls_decode_attention_workspace_bytes(int64_t batch, int64_t q_len, int64_t num_heads, int64_t num_kv_heads,
                                         int64_t head_dim, int64_t max_seq, int64_t* bytes);
+/* One decode token per sequence from the raw fused projection qkv [batch,
+ * (Hq + 2 Hkv) D] (bf16, as ls_linear_bf16 writes it): the per-head q/k
+ * RMSNorm and NeoX RoPE of ls_qk_norm_rope_kvappend (bit for bit), the K/V
+ * append at cache_pos[b], and the attention of ls_decode_attention over keys
+ * 0..cache_pos[b], in one launch.  Replaces, for the bs1 / small-batch decode
+ * step, src/leanstack/runtime/qwen_explicit.py:733-806 (q/k norm, RoPE),
+ * src/leanstack/runtime/kv_cache.py:247-254 (append_and_get) and the SDPA at
+ * qwen_explicit.py:886-903.  num_heads / num_kv_heads <= 16; q is not written
+ * out.  A position outside the cache or the rope table sets
+ * LS_ERR_KV_OVERFLOW on the device and appends nothing. */
+int ls_decode_attention_qkv(const void* qkv, int64_t batch, int64_t num_heads, int64_t num_kv_heads,
+                            int64_t head_dim, const void* q_norm_w, const void* k_norm_w, float eps,
+                            const void* rope_cos, const void* rope_sin, int64_t rope_len, int64_t rope_offset,
+                            const int32_t* cache_pos, int64_t uniform_past, void* k_cache, void* v_cache,
+                            int64_t max_seq, float scale, void* out, ls_stream_t stream);
 
 /* h = residual + bf16(o_w attn): o_proj with the residual epilogue
  * (src/leanstack/runtime/qwen_explicit.py:913 and :1262, :819-820). */

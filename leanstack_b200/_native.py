@@ -67,6 +67,8 @@ SIGNATURES: dict[str, list] = {
                                      _i64, _p, _i64, _p, _p, _i64, _p, _p, _p, _p, _p],
     "ls_decode_attention": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _p, _i64, _p],
     "ls_decode_attention_workspace_bytes": [_i64, _i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_i64)],
+    "ls_decode_attention_qkv": [_p, _i64, _i64, _i64, _i64, _p, _p, _f32, _p, _p, _i64, _i64, _p, _i64, _p, _p,
+                                _i64, _f32, _p, _p],
     "ls_oproj_residual": [_p, _i64, _i64, _p, _i64, _p, _p, _p],
     "ls_rmsnorm_gateup_silu": [_p, _i64, _i64, _p, _f32, _p, _i64, _p, _p],
     "ls_down_residual": [_p, _i64, _i64, _p, _i64, _p, _p, _p],

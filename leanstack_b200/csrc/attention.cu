@@ -85,32 +85,12 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(QkRopeParams p
   const uint2 raw_u = load4(h * kHeadDim + e0);
   // A key head's V columns, fetched before the norm so both loads overlap.
   const uint2 v_u = is_q ? make_uint2(0u, 0u) : load4((h + p.Hkv) * kHeadDim + e0);
-  float raw[4] = {bf16_lo(raw_u.x), bf16_hi(raw_u.x), bf16_lo(raw_u.y), bf16_hi(raw_u.y)};
-  float ss = raw[0] * raw[0] + raw[1] * raw[1] + raw[2] * raw[2] + raw[3] * raw[3];
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / (float)kHeadDim + p.eps);
   const __nv_bfloat16* nw = is_q ? p.q_norm_w : p.k_norm_w;
   const uint2 w_u = *reinterpret_cast<const uint2*>(nw + e0);
-  const float wv[4] = {bf16_lo(w_u.x), bf16_hi(w_u.x), bf16_lo(w_u.y), bf16_hi(w_u.y)};
-  float n[4], other[4], o[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) n[j] = round_bf16((raw[j] * r) * wv[j]);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) other[j] = __shfl_xor_sync(0xffffffffu, n[j], 16);
-  const bool first_half = lane < 16;
-  const int idx = first_half ? e0 : e0 - kHeadDim / 2;
+  const int idx = lane < 16 ? e0 : e0 - kHeadDim / 2;
   const uint2 c_u = *reinterpret_cast<const uint2*>(p.cos + (size_t)row * (kHeadDim / 2) + idx);
   const uint2 s_u = *reinterpret_cast<const uint2*>(p.sin + (size_t)row * (kHeadDim / 2) + idx);
-  const float c[4] = {bf16_lo(c_u.x), bf16_hi(c_u.x), bf16_lo(c_u.y), bf16_hi(c_u.y)};
-  const float s[4] = {bf16_lo(s_u.x), bf16_hi(s_u.x), bf16_lo(s_u.y), bf16_hi(s_u.y)};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    if (first_half) o[j] = round_bf16(round_bf16(n[j] * c[j]) - round_bf16(other[j] * s[j]));
-    else o[j] = round_bf16(round_bf16(n[j] * c[j]) + round_bf16(other[j] * s[j]));
-  }
-  __nv_bfloat162 lo2 = __floats2bfloat162_rn(o[0], o[1]);
-  __nv_bfloat162 hi2 = __floats2bfloat162_rn(o[2], o[3]);
-  uint2 packed = make_uint2(*reinterpret_cast<uint32_t*>(&lo2), *reinterpret_cast<uint32_t*>(&hi2));
+  const uint2 packed = head_norm_rope(raw_u, w_u, c_u, s_u, p.eps, lane);
   if (is_q) {
     *reinterpret_cast<uint2*>(p.q_out + ((size_t)t * p.Hq + h) * kHeadDim + e0) = packed;
     return;

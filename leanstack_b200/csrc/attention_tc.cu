@@ -40,6 +40,7 @@ constexpr int kTaMaxSplits = 16;
 constexpr int kTaMergeBytes = kTaWarps * kTaRows * (kTaHeadDim + 2) * 4;  // reuses the ring
 constexpr int kTaRecvBytes = kTaRows * kTaHeadDim * 4 + 2 * kTaMaxSplits * kTaRows * 4;
 constexpr int kTaSmemBytes = kTaRingBytes + kTaRecvBytes;
+constexpr int kTaQStageBytes = kTaRows * kTaHeadDim * 2;  // fused mode: the CTA's normalised query rows
 static_assert(kTaMergeBytes <= kTaRingBytes, "merge buffers must fit in the ring");
 
 struct TaParams {
@@ -52,6 +53,18 @@ struct TaParams {
   int* err;
   int q_len, Hq, Hkv, G, R, RG, splits, max_seq;
   float scale_log2;
+  // Fused q/k norm + RoPE + K/V append (q_len 1): when qkv is set, q is formed
+  // here from the raw projection and the new token's K/V row goes into the
+  // cache and, from registers, into the shared-memory tile that holds it.
+  const __nv_bfloat16* qkv;      // [B, (Hq + 2 Hkv) D] or null
+  const __nv_bfloat16* q_norm_w;
+  const __nv_bfloat16* k_norm_w;
+  const __nv_bfloat16* cos;      // [rope_len, D/2]
+  const __nv_bfloat16* sin;
+  __nv_bfloat16* k_store;        // the caches, writable
+  __nv_bfloat16* v_store;
+  int rope_len, rope_offset;
+  float eps;
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
@@ -106,6 +119,7 @@ __device__ __forceinline__ uint32_t ta_swz(int key, int chunk) {
   return (uint32_t)(key * (kTaHeadDim * 2) + ((chunk ^ (key & 7)) << 4));
 }
 
+template <bool FUSED>
 __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParams p) {
   extern __shared__ __align__(128) unsigned char ta_smem[];
   float* recv_o = reinterpret_cast<float*>(ta_smem + kTaRingBytes);  // [splits][16][128/splits]
@@ -133,6 +147,16 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
   const int blk0 = min(s * blk_per, nblk_all), blk1 = min(blk0 + blk_per, nblk_all);
   const int r0 = rg * kTaRows;
   const int nrows = min(kTaRows, p.R - r0);
+  // Fused mode (q_len 1): the new token's key (position cp) is not in the
+  // cache yet, so the copies stop before it; its tile row is written from
+  // registers by the warp that owns its block.
+  constexpr bool fused = FUSED;
+  const int Lcopy = fused ? min(L, max(cp, 0)) : L;
+  const int e0 = lane * 4;  // fused mode: the 4 head dims this lane normalises
+  const size_t qkv_dim = (size_t)(p.Hq + 2 * p.Hkv) * kTaHeadDim;
+  const int rrow = cp - p.rope_offset;
+  const bool rope_ok = fused && cp >= 0 && rrow >= 0 && rrow < p.rope_len;
+  if (fused && !rope_ok && threadIdx.x == 0 && s == 0) raise_device_error(p.err, LS_ERR_KV_OVERFLOW);
 
   const size_t head_base = ((size_t)b * p.Hkv + hkv) * p.max_seq * kTaHeadDim;
   const __nv_bfloat16* kbase = p.k_cache + head_base;
@@ -149,7 +173,7 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
       const int c = lane + 32 * it;
       const int r = c >> 4, cc = c & 15;
       const int j = kb + r;
-      const bool ok = j < L;
+      const bool ok = j < Lcopy;
       const size_t off = (size_t)(ok ? j : 0) * kTaHeadDim + cc * 8;
       const uint32_t so = ta_swz(r, cc);
       cp_async16(st + so, kbase + off, ok ? 16u : 0u);
@@ -168,6 +192,42 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
     cp_async_commit();
   }
 
+  // Fused mode: the normalised, rotated query rows into shared memory (warp w
+  // forms rows w, w + 4, ...), and the new token's K (normalised, rotated) and
+  // V rows in the registers of the warp whose block holds position cp; that
+  // warp also appends them to the cache.
+  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(ta_smem + kTaSmemBytes);
+  int n_new = -1;
+  uint2 knew = make_uint2(0u, 0u), vnew = make_uint2(0u, 0u);
+  if (fused) {
+    const __nv_bfloat16* xt = p.qkv + (size_t)b * qkv_dim;
+    const int idx = lane < 16 ? e0 : e0 - kTaHeadDim / 2;
+    uint2 c_u = make_uint2(0u, 0u), s_u = make_uint2(0u, 0u);
+    if (rope_ok) {
+      c_u = *reinterpret_cast<const uint2*>(p.cos + (size_t)rrow * (kTaHeadDim / 2) + idx);
+      s_u = *reinterpret_cast<const uint2*>(p.sin + (size_t)rrow * (kTaHeadDim / 2) + idx);
+    }
+    const int blk_new = cp / kTaKeys;
+    if (rope_ok && cp < p.max_seq && blk_new >= blk0 && blk_new < blk1 && (blk_new - blk0) % kTaWarps == warp) {
+      n_new = (blk_new - blk0) / kTaWarps;
+      const uint2 rk = *reinterpret_cast<const uint2*>(xt + (size_t)(p.Hq + hkv) * kTaHeadDim + e0);
+      vnew = *reinterpret_cast<const uint2*>(xt + (size_t)(p.Hq + p.Hkv + hkv) * kTaHeadDim + e0);
+      knew = head_norm_rope(rk, *reinterpret_cast<const uint2*>(p.k_norm_w + e0), c_u, s_u, p.eps, lane);
+      if (rg == 0) {
+        const size_t off = (((size_t)b * p.Hkv + hkv) * p.max_seq + cp) * kTaHeadDim + e0;
+        *reinterpret_cast<uint2*>(p.k_store + off) = knew;
+        *reinterpret_cast<uint2*>(p.v_store + off) = vnew;
+      }
+    }
+    const uint2 wq = *reinterpret_cast<const uint2*>(p.q_norm_w + e0);
+    for (int r = warp; r < nrows; r += kTaWarps) {  // q_len 1: row r0 + r is query head hkv * G + r0 + r
+      const uint2 rq = *reinterpret_cast<const uint2*>(xt + (size_t)(hkv * p.G + r0 + r) * kTaHeadDim + e0);
+      const uint2 o = rope_ok ? head_norm_rope(rq, wq, c_u, s_u, p.eps, lane) : make_uint2(0u, 0u);
+      *reinterpret_cast<uint2*>(qs + r * kTaHeadDim + e0) = o;
+    }
+    __syncthreads();
+  }
+
   // Q fragments (A operand, rows g8 and g8 + 8, 8 k-steps of 16 dims) and the
   // last key each of the two rows may see.
   uint32_t qa[8][4];
@@ -179,7 +239,8 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
     const int i = valid ? row / p.G : 0;
     const int gq = valid ? row - i * p.G : 0;
     lim[hr] = valid ? cp + i : -1;
-    const __nv_bfloat16* qp = p.q + ((size_t)(b * p.q_len + i) * p.Hq + hkv * p.G + gq) * kTaHeadDim;
+    const __nv_bfloat16* qp = fused ? qs + (size_t)(row - r0) * kTaHeadDim
+                                    : p.q + ((size_t)(b * p.q_len + i) * p.Hq + hkv * p.G + gq) * kTaHeadDim;
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       qa[ks][hr] = valid ? *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 2 * t4) : 0u;
@@ -194,6 +255,12 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
     const uint32_t stK = ring + stage * kTaStageBytes;
     const uint32_t stV = stK + kTaTileBytes;
     const int jb = (blk0 + warp + n * kTaWarps) * kTaKeys;
+    if (fused && n == n_new) {  // fused mode: the new token's K / V row over the tile's zero-filled row
+      const uint32_t o = ta_swz(cp - jb, lane >> 1) + (lane & 1) * 8;
+      asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(stK + o), "r"(knew.x), "r"(knew.y) : "memory");
+      asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(stV + o), "r"(vnew.x), "r"(vnew.y) : "memory");
+      __syncwarp();
+    }
 
     // S = Q K^T for 16 keys (two n-tiles of 8 keys).
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -381,15 +448,41 @@ static TaPlan ta_plan(int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int
   return pl;
 }
 
-int launch_decode_attention_tc(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
-                               int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv,
-                               int64_t max_seq, float scale, void* out, cudaStream_t stream) {
-  const TaPlan pl = ta_plan(batch, q_len, hq, hkv, max_seq);
-  if ((int64_t)hkv * pl.RG > 65535)
-    return set_error(LS_ERR_UNSUPPORTED_SHAPE, "decode_attention: %lld kv heads x %d row groups exceed the grid",
-                     (long long)hkv, pl.RG);
+template <bool FUSED>
+static int launch_ta(const TaParams& p, const TaPlan& pl, int64_t batch, int64_t hkv, cudaStream_t stream) {
+  constexpr size_t smem = kTaSmemBytes + (FUSED ? kTaQStageBytes : 0);
+  static bool attrs_set = false;
+  if (!attrs_set) {
+    cudaError_t e =
+        cudaFuncSetAttribute(decode_attention_tc_kernel<FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(decode_attention_tc_kernel<FUSED>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "attention_tc attributes: %s", cudaGetErrorString(e));
+    attrs_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.splits, (unsigned)(hkv * pl.RG), (unsigned)batch);
+  cfg.blockDim = dim3(kTaThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = pl.splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_attention_tc_kernel<FUSED>, p);
+  if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "decode_attention_tc launch: %s", cudaGetErrorString(e));
+  return LS_OK;
+}
+
+static TaParams ta_params(const TaPlan& pl, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
+                          int64_t uniform_past, int64_t q_len, int64_t hq, int64_t hkv, int64_t max_seq, float scale,
+                          void* out) {
   TaParams p = {};
-  p.q = static_cast<const __nv_bfloat16*>(q);
   p.k_cache = static_cast<const __nv_bfloat16*>(k_cache);
   p.v_cache = static_cast<const __nv_bfloat16*>(v_cache);
   p.cache_pos = cache_pos;
@@ -405,37 +498,44 @@ int launch_decode_attention_tc(const void* q, const void* k_cache, const void* v
   p.max_seq = (int)max_seq;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = device_error_ptr();
-  static bool attrs_set = false;
-  if (!attrs_set) {
-    cudaError_t e = cudaFuncSetAttribute(decode_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kTaSmemBytes);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(decode_attention_tc_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "attention_tc attributes: %s", cudaGetErrorString(e));
-    attrs_set = true;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.splits, (unsigned)(hkv * pl.RG), (unsigned)batch);
-  cfg.blockDim = dim3(kTaThreads);
-  cfg.dynamicSmemBytes = kTaSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  int na = 0;
-  attr[na].id = cudaLaunchAttributeClusterDimension;
-  attr[na].val.clusterDim.x = pl.splits;
-  attr[na].val.clusterDim.y = 1;
-  attr[na].val.clusterDim.z = 1;
-  ++na;
-  {
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na].val.programmaticStreamSerializationAllowed = 1;
-    ++na;
-  }
-  cfg.attrs = attr;
-  cfg.numAttrs = na;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_attention_tc_kernel, p);
-  if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "decode_attention_tc launch: %s", cudaGetErrorString(e));
-  return LS_OK;
+  return p;
+}
+
+int launch_decode_attention_tc(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
+                               int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv,
+                               int64_t max_seq, float scale, void* out, cudaStream_t stream) {
+  const TaPlan pl = ta_plan(batch, q_len, hq, hkv, max_seq);
+  if ((int64_t)hkv * pl.RG > 65535)
+    return set_error(LS_ERR_UNSUPPORTED_SHAPE, "decode_attention: %lld kv heads x %d row groups exceed the grid",
+                     (long long)hkv, pl.RG);
+  TaParams p = ta_params(pl, k_cache, v_cache, cache_pos, uniform_past, q_len, hq, hkv, max_seq, scale, out);
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  return launch_ta<false>(p, pl, batch, hkv, stream);
+}
+
+// One decode token per sequence (q_len 1) straight from the raw fused QKV
+// projection: q/k RMSNorm + RoPE, the K/V append at cache_pos[b], and the
+// attention, in one launch (the kernel's fused mode).
+int launch_decode_attention_qkv(const void* qkv, int64_t batch, int64_t hq, int64_t hkv, const void* qn,
+                                const void* kn, float eps, const void* cos, const void* sin, int64_t rope_len,
+                                int64_t rope_offset, const int32_t* cache_pos, int64_t uniform_past, void* k_cache,
+                                void* v_cache, int64_t max_seq, float scale, void* out, cudaStream_t stream) {
+  const TaPlan pl = ta_plan(batch, 1, hq, hkv, max_seq);
+  if (pl.RG != 1)
+    return set_error(LS_ERR_UNSUPPORTED_SHAPE, "decode_attention_qkv: %d query heads per kv head (at most %d)",
+                     pl.G, kTaRows);
+  TaParams p = ta_params(pl, k_cache, v_cache, cache_pos, uniform_past, 1, hq, hkv, max_seq, scale, out);
+  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  p.q_norm_w = static_cast<const __nv_bfloat16*>(qn);
+  p.k_norm_w = static_cast<const __nv_bfloat16*>(kn);
+  p.cos = static_cast<const __nv_bfloat16*>(cos);
+  p.sin = static_cast<const __nv_bfloat16*>(sin);
+  p.k_store = static_cast<__nv_bfloat16*>(k_cache);
+  p.v_store = static_cast<__nv_bfloat16*>(v_cache);
+  p.rope_len = (int)rope_len;
+  p.rope_offset = (int)rope_offset;
+  p.eps = eps;
+  return launch_ta<true>(p, pl, batch, hkv, stream);
 }
 
 }  // namespace lsb_host

@@ -387,6 +387,10 @@ int attention_workspace_bytes(int64_t batch, int64_t q_len, int64_t hq, int64_t 
 int launch_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cache_pos,
                             int64_t uniform_past, int64_t batch, int64_t q_len, int64_t hq, int64_t hkv, int64_t max_seq, float scale,
                             void* out, void* workspace, int64_t workspace_bytes, cudaStream_t stream);
+int launch_decode_attention_qkv(const void* qkv, int64_t batch, int64_t hq, int64_t hkv, const void* qn,
+                                const void* kn, float eps, const void* cos, const void* sin, int64_t rope_len,
+                                int64_t rope_offset, const int32_t* cache_pos, int64_t uniform_past, void* k_cache,
+                                void* v_cache, int64_t max_seq, float scale, void* out, cudaStream_t stream);
 
 int tc_workspace_bytes(int64_t m, int64_t k, int64_t n_out, int epi, int64_t* bytes);
 int tc_split_count(int64_t m, int64_t k, int64_t n_out, int64_t* splits);
@@ -544,6 +548,30 @@ int ls_decode_attention(const void* q, const void* k_cache, const void* v_cache,
              "ls_decode_attention: pointers must be 16-byte aligned");
   return launch_decode_attention(q, k_cache, v_cache, cache_pos, uniform_past, batch, q_len, num_heads, num_kv_heads, max_seq,
                                  scale, out, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int ls_decode_attention_qkv(const void* qkv, int64_t batch, int64_t num_heads, int64_t num_kv_heads,
+                            int64_t head_dim, const void* q_norm_w, const void* k_norm_w, float eps,
+                            const void* rope_cos, const void* rope_sin, int64_t rope_len, int64_t rope_offset,
+                            const int32_t* cache_pos, int64_t uniform_past, void* k_cache, void* v_cache,
+                            int64_t max_seq, float scale, void* out, ls_stream_t stream) {
+  LS_REQUIRE(qkv && q_norm_w && k_norm_w && rope_cos && rope_sin && k_cache && v_cache && out,
+             LS_ERR_INVALID_ARGUMENT, "ls_decode_attention_qkv: null pointer");
+  LS_REQUIRE(head_dim == 128, LS_ERR_UNSUPPORTED_SHAPE, "head_dim=%lld (only 128 is implemented)",
+             (long long)head_dim);
+  LS_REQUIRE(batch > 0 && batch <= 65535 && num_kv_heads > 0 && num_heads % num_kv_heads == 0 &&
+                 num_heads / num_kv_heads <= 16 && max_seq > 0 && max_seq < (1ll << 31),
+             LS_ERR_INVALID_ARGUMENT, "ls_decode_attention_qkv: bad sizes");
+  LS_REQUIRE(rope_len > 0 && rope_offset >= 0, LS_ERR_INVALID_ARGUMENT, "bad rope table");
+  LS_REQUIRE(cache_pos || (uniform_past >= rope_offset && uniform_past < rope_offset + rope_len &&
+                           uniform_past < max_seq),
+             LS_ERR_KV_OVERFLOW, "uniform_past=%lld outside the cache or the rope table", (long long)uniform_past);
+  LS_REQUIRE(aligned16(qkv) && aligned16(q_norm_w) && aligned16(k_norm_w) && aligned16(rope_cos) &&
+                 aligned16(rope_sin) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out),
+             LS_ERR_MISALIGNED, "ls_decode_attention_qkv: pointers must be 16-byte aligned");
+  return launch_decode_attention_qkv(qkv, batch, num_heads, num_kv_heads, q_norm_w, k_norm_w, eps, rope_cos, rope_sin,
+                                     rope_len, rope_offset, cache_pos, uniform_past, k_cache, v_cache, max_seq, scale,
+                                     out, (cudaStream_t)stream);
 }
 
 int ls_oproj_residual(const void* attn, int64_t m, int64_t k, const void* o_w, int64_t n, const void* residual,

@@ -169,6 +169,37 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// q/k RMSNorm of one 128-dim head held by a warp (lane l holds dims 4l..4l+3
+// as packed bf16), then the NeoX-half rotary embedding, with the reference's
+// bf16 rounding points (src/leanstack/runtime/qwen_explicit.py:733-806):
+// n = bf16((x * r) * w), r = rsqrt(mean(x^2) + eps); each RoPE product and the
+// sum / difference round to bf16.  w_u: norm weight of the lane's dims; c_u /
+// s_u: the cos / sin row at the lane's rotary index (dims mod 64).  Every
+// kernel that forms q or k goes through this function, so they agree bit for bit.
+__device__ __forceinline__ uint2 head_norm_rope(uint2 raw_u, uint2 w_u, uint2 c_u, uint2 s_u, float eps, int lane) {
+  const float raw[4] = {bf16_lo(raw_u.x), bf16_hi(raw_u.x), bf16_lo(raw_u.y), bf16_hi(raw_u.y)};
+  float ss = raw[0] * raw[0] + raw[1] * raw[1] + raw[2] * raw[2] + raw[3] * raw[3];
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / 128.f + eps);
+  const float wv[4] = {bf16_lo(w_u.x), bf16_hi(w_u.x), bf16_lo(w_u.y), bf16_hi(w_u.y)};
+  float n[4], other[4], o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) n[j] = round_bf16((raw[j] * r) * wv[j]);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) other[j] = __shfl_xor_sync(0xffffffffu, n[j], 16);
+  const bool first_half = lane < 16;
+  const float c[4] = {bf16_lo(c_u.x), bf16_hi(c_u.x), bf16_lo(c_u.y), bf16_hi(c_u.y)};
+  const float s[4] = {bf16_lo(s_u.x), bf16_hi(s_u.x), bf16_lo(s_u.y), bf16_hi(s_u.y)};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (first_half) o[j] = round_bf16(round_bf16(n[j] * c[j]) - round_bf16(other[j] * s[j]));
+    else o[j] = round_bf16(round_bf16(n[j] * c[j]) + round_bf16(other[j] * s[j]));
+  }
+  __nv_bfloat162 lo2 = __floats2bfloat162_rn(o[0], o[1]);
+  __nv_bfloat162 hi2 = __floats2bfloat162_rn(o[2], o[3]);
+  return make_uint2(*reinterpret_cast<uint32_t*>(&lo2), *reinterpret_cast<uint32_t*>(&hi2));
+}
+
 
 
 // Orderable 64-bit key of a (logit, vocab id) candidate: a signed max over

@@ -174,13 +174,20 @@ class DecodeEngine:
             else:
                 K.linear(a.x[:m], att.qkv_proj_weight, norm_w=layer.input_layernorm_weight, eps=eps,
                          out=a.qkv[:m])
-                K.qk_norm_rope(a.qkv[:m], B, q_len, g.num_attention_heads, g.num_key_value_heads, g.head_dim,
-                               att.q_norm_weight, att.k_norm_weight, self.cos, self.sin, eps=eps,
-                               cache_pos=kv.cache_pos, k_cache=kv.key_cache[li], v_cache=kv.value_cache[li],
-                               max_seq=self.S, q_out=a.q[:m])
-            K.decode_attention(a.q[:m], kv.key_cache[li], kv.value_cache[li], B, q_len, g.num_attention_heads,
-                               g.num_key_value_heads, g.head_dim, self.S, att.attention_scale,
-                               cache_pos=kv.cache_pos, out=a.attn[:m], workspace=self.attn_ws)
+                if q_len == 1:  # q/k norm, RoPE, K/V append and attention in one launch
+                    K.decode_attention_qkv(a.qkv[:m], B, g.num_attention_heads, g.num_key_value_heads, g.head_dim,
+                                           att.q_norm_weight, att.k_norm_weight, self.cos, self.sin,
+                                           kv.key_cache[li], kv.value_cache[li], self.S, att.attention_scale,
+                                           eps=eps, cache_pos=kv.cache_pos, out=a.attn[:m])
+                else:
+                    K.qk_norm_rope(a.qkv[:m], B, q_len, g.num_attention_heads, g.num_key_value_heads, g.head_dim,
+                                   att.q_norm_weight, att.k_norm_weight, self.cos, self.sin, eps=eps,
+                                   cache_pos=kv.cache_pos, k_cache=kv.key_cache[li], v_cache=kv.value_cache[li],
+                                   max_seq=self.S, q_out=a.q[:m])
+            if tc or q_len != 1:
+                K.decode_attention(a.q[:m], kv.key_cache[li], kv.value_cache[li], B, q_len, g.num_attention_heads,
+                                   g.num_key_value_heads, g.head_dim, self.S, att.attention_scale,
+                                   cache_pos=kv.cache_pos, out=a.attn[:m], workspace=self.attn_ws)
             if self.tp is not None:
                 self._row_split(a.attn[:m], att.o_proj_weight, a.x[:m], a.h[:m], tc, tt.get("o"))
                 if tc:
@@ -474,7 +481,7 @@ class DecodeEngine:
 
     def kernel_launches_per_step(self) -> int:
         """Kernels one decode step launches (embedding, layers, head, cursor advance)."""
-        per_layer = (9 if self.gu_plain else 8) if self.backend == "tc" else 6
+        per_layer = (9 if self.gu_plain else 8) if self.backend == "tc" else 5  # CUDA cores: attention takes the q/k norm
         head = 3 if self.backend == "tc" else 1
         if self.tp is not None:  # + all-reduce / residual-add kernels after each row-split linear, + keys-to-ids
             if self.tp.p2p is None or self.backend == "tc":

@@ -233,6 +233,29 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     return out
 
 
+def decode_attention_qkv(qkv: torch.Tensor, batch: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                         q_norm_w: torch.Tensor, k_norm_w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                         k_cache: torch.Tensor, v_cache: torch.Tensor, max_seq: int, scale: float, *,
+                         eps: float = 1e-6, cache_pos: torch.Tensor | None = None, uniform_past: int = 0,
+                         rope_offset: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode token per sequence from the raw fused projection ``qkv [batch, (Hq+2Hkv) D]``:
+    :func:`qk_norm_rope` (q/k norm, RoPE, K/V append at ``cache_pos``) and :func:`decode_attention`
+    in one launch, with the same bits as the two."""
+    _check(qkv, "qkv")
+    for name, t in (("k_cache", k_cache), ("v_cache", v_cache)):
+        if t.dtype != BF16 or t.device.type != "cuda":
+            raise TypeError(f"{name} must be a bf16 CUDA tensor")
+    if cache_pos is not None:
+        _check(cache_pos, "cache_pos", torch.int32)
+    if out is None:
+        out = torch.empty((batch, num_heads * head_dim), device=qkv.device, dtype=BF16)
+    nat.call("ls_decode_attention_qkv", qkv.data_ptr(), batch, num_heads, num_kv_heads, head_dim,
+             q_norm_w.data_ptr(), k_norm_w.data_ptr(), float(eps), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
+             int(rope_offset), _ptr(cache_pos), int(uniform_past), k_cache.data_ptr(), v_cache.data_ptr(),
+             int(max_seq), float(scale), out.data_ptr(), _stream())
+    return out
+
+
 def oproj_residual(attn: torch.Tensor, o_w: torch.Tensor, residual: torch.Tensor,
                    out: torch.Tensor | None = None) -> torch.Tensor:
     _check(attn, "attn")

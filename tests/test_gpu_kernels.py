@@ -172,6 +172,59 @@ def test_decode_attention(batch, q_len, lens):
         assert torch.equal(out, out2)
 
 
+@pytest.mark.parametrize("hq,hkv,lens,S", [(32, 8, [512], 4096),  # config 2
+                                           (32, 8, [0], 64),  # first token, empty cache
+                                           (32, 8, [15, 16, 4000], 4096),  # 16-key block edges, long context
+                                           (16, 8, [1, 31, 32, 700], 1024),  # the 0.6B draft's heads (G 2)
+                                           (32, 8, [63, 4094], 4095)])  # the last cache slot
+def test_decode_attention_qkv_fused_equals_two_launches(hq, hkv, lens, S):
+    """The one-launch decode attention from the raw QKV projection writes the
+    same K/V rows into the cache and returns the same output, bit for bit, as
+    ls_qk_norm_rope_kvappend followed by ls_decode_attention."""
+    d, batch = 128, len(lens)
+    qkv = _rand((batch, (hq + 2 * hkv) * d), 1.0, f"fq{hq}_{batch}")
+    qn = synth.norm_weight((d,), 2, "fqn", device=DEV)
+    kn = synth.norm_weight((d,), 3, "fkn", device=DEV)
+    cos, sin = qo.rope_cache(qo.rope_inv_freq(d, 1e6), S, torch.bfloat16)
+    cos, sin = cos.to(DEV), sin.to(DEV)
+    kc0 = _rand((batch, hkv, S, d), 1.0, f"fkc{batch}")
+    vc0 = _rand((batch, hkv, S, d), 1.0, f"fvc{batch}")
+    cache_pos = torch.tensor(lens, device=DEV, dtype=torch.int32)
+    scale = d ** -0.5
+    K.device_error(clear=True)
+    kc1, vc1 = kc0.clone(), vc0.clone()
+    q = K.qk_norm_rope(qkv, batch, 1, hq, hkv, d, qn, kn, cos, sin, cache_pos=cache_pos, k_cache=kc1, v_cache=vc1,
+                       max_seq=S)
+    want = K.decode_attention(q, kc1, vc1, batch, 1, hq, hkv, d, S, scale, cache_pos=cache_pos)
+    kc2, vc2 = kc0.clone(), vc0.clone()
+    got = K.decode_attention_qkv(qkv, batch, hq, hkv, d, qn, kn, cos, sin, kc2, vc2, S, scale, cache_pos=cache_pos)
+    assert K.device_error(clear=True) == 0
+    assert torch.equal(kc2, kc1) and torch.equal(vc2, vc1)
+    assert torch.equal(got, want)
+    if len(set(lens)) == 1:  # uniform cursor via the host argument
+        kc3, vc3 = kc0.clone(), vc0.clone()
+        got3 = K.decode_attention_qkv(qkv, batch, hq, hkv, d, qn, kn, cos, sin, kc3, vc3, S, scale,
+                                      uniform_past=lens[0])
+        assert torch.equal(got3, want) and torch.equal(kc3, kc1)
+
+
+def test_decode_attention_qkv_overflow_sets_flag_and_appends_nothing():
+    hq, hkv, d, S = 32, 8, 128, 64
+    qkv = _rand((1, (hq + 2 * hkv) * d), 1.0, "fo")
+    qn = synth.norm_weight((d,), 2, "foqn", device=DEV)
+    cos, sin = qo.rope_cache(qo.rope_inv_freq(d, 1e6), 2 * S, torch.bfloat16)
+    kc = _rand((1, hkv, S, d), 1.0, "fokc")
+    vc = _rand((1, hkv, S, d), 1.0, "fovc")
+    k0, v0 = kc.clone(), vc.clone()
+    K.device_error(clear=True)
+    cache_pos = torch.tensor([S], device=DEV, dtype=torch.int32)  # one past the arena
+    K.decode_attention_qkv(qkv, 1, hq, hkv, d, qn, qn, cos.to(DEV), sin.to(DEV), kc, vc, S, d ** -0.5,
+                           cache_pos=cache_pos)
+    assert K.device_error(clear=True) == 6  # LS_ERR_KV_OVERFLOW
+    assert torch.equal(kc, k0) and torch.equal(vc, v0)
+    assert K.device_error(clear=True) == 0
+
+
 def test_lmhead_argmax_matches_bf16_logits_and_ties():
     vocab, hidden = 151936, 2560
     w = _rand((vocab, hidden), 0.02, "lm")
