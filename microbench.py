@@ -60,10 +60,13 @@ def profile_step(kind: str) -> int:
     g = QWEN3_4B
     dev = torch.device("cuda")
     rt = materialize_from_tensors(g, synth.synth_checkpoint(g, 1, device=dev), device=dev, free_source=True)
-    B, cached, k = (32, 2048, 0) if kind == "bs32" else (16, 1024, 4)
-    eng = DecodeEngine(rt, batch_size=B, max_seq_len=cached + 64, linear_backend="tc")
+    B, cached, k = {"bs1": (1, 512, 0), "bs32": (32, 2048, 0), "verify": (16, 1024, 4)}[kind]
+    if kind == "bs1":  # config 2: static KV of 4096 positions, the default (CUDA-core) backend
+        eng = DecodeEngine(rt, batch_size=B, max_seq_len=4096)
+    else:
+        eng = DecodeEngine(rt, batch_size=B, max_seq_len=cached + 64, linear_backend="tc")
     eng.prefill_full(synth.token_ids((B, cached), g.vocab_size, 1, f"mb/step/{kind}"))
-    if kind == "bs32":
+    if kind in ("bs1", "bs32"):
         eng.capture()
         step = eng.decode_step
     else:
@@ -84,7 +87,7 @@ def profile_step(kind: str) -> int:
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     print(json.dumps({"step": kind, "batch": B, "cached": cached, "ms_per_step": a.elapsed_time(b) / 2,
-                      "launches_per_step": eng.kernel_launches_per_step() if kind == "bs32" else None}))
+                      "launches_per_step": eng.kernel_launches_per_step() if kind != "verify" else None}))
     return 0
 
 
@@ -96,7 +99,7 @@ def main(argv=None) -> int:
     ap.add_argument("--seq", type=int, default=600, help="cached positions for attention")
     ap.add_argument("--copies", type=int, default=4)
     ap.add_argument("--batch", type=int, default=1, help="sequences of the prefill_attn case")
-    ap.add_argument("--step", choices=("bs32", "verify"), default=None,
+    ap.add_argument("--step", choices=("bs1", "bs32", "verify"), default=None,
                     help="instead of kernels: one whole captured step of Qwen3-4B (config 3 bs32 decode over 2048 "
                          "cached, or the config-4 verify pass), two replays inside the NVTX range 'step' "
                          "(for `ncu --nvtx --nvtx-include step/`)")
