@@ -37,6 +37,10 @@ struct QkRopeParams {
   float eps;
 };
 
+// PART: the projection comes as split fp32 partials (p.part), else as bf16
+// (p.qkv); two instances, so the bf16 one (prefill, one row per token and
+// head over 65k tokens) keeps its registers low and its occupancy high.
+template <bool PART>
 __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(QkRopeParams p) {
   grid_dep_wait();
   grid_dep_launch();
@@ -53,7 +57,7 @@ __global__ void __launch_bounds__(128) qk_norm_rope_append_kernel(QkRopeParams p
   // Four bf16 elements of the projection at column col of token t: loaded, or
   // the split partials summed in split order and rounded once.
   auto load4 = [&](int col) -> uint2 {
-    if (p.qkv) return *reinterpret_cast<const uint2*>(p.qkv + (size_t)t * qkv_dim + col);
+    if (!PART) return *reinterpret_cast<const uint2*>(p.qkv + (size_t)t * qkv_dim + col);
     const size_t slab = (size_t)gridDim.x * qkv_dim;
     const float* q = p.part + (size_t)t * qkv_dim + col;
     float4 a = __ldcg(reinterpret_cast<const float4*>(q));
@@ -156,7 +160,8 @@ int launch_qk_norm_rope(const void* qkv, const float* part, int64_t splits, int6
   const int m = (int)(batch * q_len);
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_config(dim3(m, (unsigned)((hq + hkv + 3) / 4)), dim3(128), 0, stream, attr);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, qk_norm_rope_append_kernel, p);
+  cudaError_t e = qkv ? cudaLaunchKernelEx(&cfg, qk_norm_rope_append_kernel<false>, p)
+                      : cudaLaunchKernelEx(&cfg, qk_norm_rope_append_kernel<true>, p);
   if (e != cudaSuccess) return set_error(LS_ERR_CUDA, "qk_norm_rope launch: %s", cudaGetErrorString(e));
   return LS_OK;
 }
