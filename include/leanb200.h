@@ -224,7 +224,12 @@ int ls_decode_attention_workspace_bytes(int64_t batch, int64_t q_len, int64_t nu
  * src/leanstack/runtime/kv_cache.py:247-254 (append_and_get) and the SDPA at
  * qwen_explicit.py:886-903.  num_heads / num_kv_heads <= 16; q is not written
  * out.  A position outside the cache or the rope table sets
- * LS_ERR_KV_OVERFLOW on the device and appends nothing. */
+ * LS_ERR_KV_OVERFLOW on the device and appends nothing.  The kernel starts
+ * under programmatic dependent launch and reads cache_pos, the cache rows
+ * before it, the rope table and the norm weights before it waits for the
+ * previous kernel in the stream; only qkv is read after the wait.  So those
+ * must not be written by a kernel that may still run when this one starts
+ * (a kernel that lets its dependents launch before it ends). */
 int ls_decode_attention_qkv(const void* qkv, int64_t batch, int64_t num_heads, int64_t num_kv_heads,
                             int64_t head_dim, const void* q_norm_w, const void* k_norm_w, float eps,
                             const void* rope_cos, const void* rope_sin, int64_t rope_len, int64_t rope_offset,

@@ -127,7 +127,12 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
   float* recv_l = recv_m + kTaMaxSplits * kTaRows;
 
   if (p.splits > 1) ta_cluster_arrive_relaxed();  // this CTA is running
-  grid_dep_wait();
+  // Fused mode waits for the previous kernel (the QKV projection) only before
+  // reading the raw projection: cache_pos, the cache rows before it, the rope
+  // table and the norm weights are written by no kernel that can still be
+  // running (the cursor and accept kernels let their dependents start only at
+  // their own end), so the first K/V copies go out under the projection's tail.
+  if (!FUSED) grid_dep_wait();
   grid_dep_launch();
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -135,7 +140,7 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
   const int b = blockIdx.z;
   const int hkv = blockIdx.y / p.RG, rg = blockIdx.y - hkv * p.RG;
   const int s = p.splits > 1 ? (int)ta_cluster_rank() : 0;
-  const int cp = p.cache_pos ? p.cache_pos[b] : p.uniform_past;
+  const int cp = p.cache_pos ? (FUSED ? __ldcg(p.cache_pos + b) : p.cache_pos[b]) : p.uniform_past;
   int L = cp + p.q_len;
   if (L > p.max_seq || cp < 0) {
     if (threadIdx.x == 0 && s == 0) raise_device_error(p.err, LS_ERR_KV_OVERFLOW);
@@ -207,19 +212,21 @@ __global__ void __launch_bounds__(kTaThreads) decode_attention_tc_kernel(TaParam
       c_u = *reinterpret_cast<const uint2*>(p.cos + (size_t)rrow * (kTaHeadDim / 2) + idx);
       s_u = *reinterpret_cast<const uint2*>(p.sin + (size_t)rrow * (kTaHeadDim / 2) + idx);
     }
+    const uint2 wk = *reinterpret_cast<const uint2*>(p.k_norm_w + e0);
+    const uint2 wq = *reinterpret_cast<const uint2*>(p.q_norm_w + e0);
+    grid_dep_wait();  // the raw projection is the previous kernel's output
     const int blk_new = cp / kTaKeys;
     if (rope_ok && cp < p.max_seq && blk_new >= blk0 && blk_new < blk1 && (blk_new - blk0) % kTaWarps == warp) {
       n_new = (blk_new - blk0) / kTaWarps;
       const uint2 rk = *reinterpret_cast<const uint2*>(xt + (size_t)(p.Hq + hkv) * kTaHeadDim + e0);
       vnew = *reinterpret_cast<const uint2*>(xt + (size_t)(p.Hq + p.Hkv + hkv) * kTaHeadDim + e0);
-      knew = head_norm_rope(rk, *reinterpret_cast<const uint2*>(p.k_norm_w + e0), c_u, s_u, p.eps, lane);
+      knew = head_norm_rope(rk, wk, c_u, s_u, p.eps, lane);
       if (rg == 0) {
         const size_t off = (((size_t)b * p.Hkv + hkv) * p.max_seq + cp) * kTaHeadDim + e0;
         *reinterpret_cast<uint2*>(p.k_store + off) = knew;
         *reinterpret_cast<uint2*>(p.v_store + off) = vnew;
       }
     }
-    const uint2 wq = *reinterpret_cast<const uint2*>(p.q_norm_w + e0);
     for (int r = warp; r < nrows; r += kTaWarps) {  // q_len 1: row r0 + r is query head hkv * G + r0 + r
       const uint2 rq = *reinterpret_cast<const uint2*>(xt + (size_t)(hkv * p.G + r0 + r) * kTaHeadDim + e0);
       const uint2 o = rope_ok ? head_norm_rope(rq, wq, c_u, s_u, p.eps, lane) : make_uint2(0u, 0u);
