@@ -79,6 +79,31 @@ def test_version_and_argument_errors_without_gpu(lib):
         nat.call("ls_embed_gather", None, 1, None, 10, 8, None, None)
 
 
+def test_split_and_fused_entry_points_validate_before_any_cuda_call(lib):
+    """The split-partial consumers and the one-launch bs1 attention reject bad
+    arguments with a status code before touching the device (the addresses
+    below are never dereferenced)."""
+    f = ctypes.c_float(1e-6)
+    p = 256  # a 16-byte aligned stand-in address
+    # one-launch attention: null qkv; head_dim 64; 32 query heads per kv head (at most 16)
+    args = [p, 1, 32, 8, 128, p, p, f, p, p, 4096, 0, p, 0, p, p, 4096, ctypes.c_float(0.088), p, None]
+    for i, v, code in ((0, None, 1), (4, 64, 2), (3, 1, 1)):
+        a = list(args)
+        a[i] = v
+        assert lib.ls_decode_attention_qkv(*a) == code
+    # a host cursor outside the cache
+    a = list(args)
+    a[12], a[13] = None, 4096
+    assert lib.ls_decode_attention_qkv(*a) == 6
+    assert "outside" in nat.last_error()
+    # residual + norm over split partials: the norm needs both weight and output
+    assert lib.ls_residual_rmsnorm_splits(p, 4, 2, 2560, p, p, f, p, None, None) == 1
+    # rows that are not a multiple of 8
+    assert lib.ls_residual_rmsnorm_splits(p, 4, 2, 2564, p, None, f, p, None, None) == 3
+    # zero splits
+    assert lib.ls_sum_splits_f32(p, 0, 16, p, None) == 1
+
+
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(nat, "LIB_PATH", tmp_path / "nope.so")
     monkeypatch.setattr(nat, "_LIB", None)
